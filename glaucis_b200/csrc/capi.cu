@@ -1,0 +1,273 @@
+// extern "C" surface of libglaucis_b200.so: argument validation, per-device
+// state (SM count, library-owned error word), TMA descriptor encoding and the
+// thread-local last-error message.  See include/glaucis_b200.h.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+#include <set>
+#include <string>
+#include <utility>
+
+#include "../../include/glaucis_b200.h"
+#include "tmap.h"
+
+// Launchers defined next to their kernels.
+int gl_launch_quant_act(const void* x, int64_t M, int64_t K, void* q, float* s, cudaStream_t st,
+                        int num_sms);
+int gl_launch_quant_w(const void* w, int64_t G, int64_t K, int64_t N, void* q, float* s,
+                      cudaStream_t st, int num_sms);
+int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
+                      const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                      void* out, int out_f32, int* err, cudaStream_t st, int num_sms,
+                      const char** why);
+int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float* g,
+                        const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
+                        int64_t H, int64_t K, int64_t V, void* o, float* ht, int* err,
+                        cudaStream_t st, int num_sms, const char** why);
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
+struct DeviceState {
+  int num_sms = 0;
+  int* err = nullptr;
+};
+
+std::mutex g_mu;
+DeviceState g_dev[64];
+std::set<std::pair<int, const void*>> g_smem_attr_done;
+
+// Returns 0 and fills the current device's state, allocating the library
+// error word on first use.
+int device_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(GL_ELAUNCH, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& d = g_dev[dev];
+  if (d.num_sms == 0) {
+    e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e));
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0) {
+      d.num_sms = 0;
+      return fail(GL_ELAUNCH, "libglaucis_b200 is built for sm_100a (B200) only; device is sm_" +
+                                  std::to_string(major) + std::to_string(minor));
+    }
+  }
+  if (d.err == nullptr) {
+    e = cudaMalloc(&d.err, sizeof(int));
+    if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("cudaMalloc(error word): ") + cudaGetErrorString(e));
+    e = cudaMemset(d.err, 0, sizeof(int));
+    if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("cudaMemset(error word): ") + cudaGetErrorString(e));
+  }
+  *out = &d;
+  return GL_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn(const char** why) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) *why = "cuTensorMapEncodeTiled is not available from the driver";
+  return fn;
+}
+
+uint32_t elem_bytes(CUtensorMapDataType dt) {
+  switch (dt) {
+    case CU_TENSOR_MAP_DATA_TYPE_UINT8: return 1;
+    case CU_TENSOR_MAP_DATA_TYPE_BFLOAT16:
+    case CU_TENSOR_MAP_DATA_TYPE_FLOAT16: return 2;
+    case CU_TENSOR_MAP_DATA_TYPE_FLOAT32: return 4;
+    default: return 0;
+  }
+}
+
+}  // namespace
+
+bool gl_make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, int64_t inner,
+                     int64_t outer, int64_t row_stride_elems, uint32_t box_inner,
+                     uint32_t box_outer, CUtensorMapSwizzle sw, const char** why) {
+  auto fn = encode_fn(why);
+  if (!fn) return false;
+  const uint32_t eb = elem_bytes(dt);
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_elems) * eb};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *why = "cuTensorMapEncodeTiled (2-D) rejected the operand (alignment / stride / box)";
+    return false;
+  }
+  return true;
+}
+
+bool gl_make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, int64_t d0,
+                     int64_t d1, int64_t d2, int64_t s1_elems, int64_t s2_elems, uint32_t b0,
+                     uint32_t b1, uint32_t b2, CUtensorMapSwizzle sw, const char** why) {
+  auto fn = encode_fn(why);
+  if (!fn) return false;
+  const uint32_t eb = elem_bytes(dt);
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1),
+                        static_cast<cuuint64_t>(d2)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(s1_elems) * eb,
+                           static_cast<cuuint64_t>(s2_elems) * eb};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *why = "cuTensorMapEncodeTiled (3-D) rejected the operand (alignment / stride / box)";
+    return false;
+  }
+  return true;
+}
+
+bool gl_set_smem_attr(const void* func, int, int bytes, const char** why) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_smem_attr_done.count({dev, func})) return true;
+  }
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+    *why = "cudaFuncSetAttribute(MaxDynamicSharedMemorySize) failed";
+    return false;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_smem_attr_done.insert({dev, func});
+  return true;
+}
+
+extern "C" {
+
+const char* gl_last_error(void) { return t_last_error.c_str(); }
+
+const char* gl_version(void) { return "glaucis_b200 0.1 (sm_100a)"; }
+
+int gl_quant_act_1x128(const void* x, int64_t M, int64_t K, void* q, float* s, int* err_word,
+                       void* stream) {
+  (void)err_word;
+  if (!x || !q || !s) return fail(GL_EINVAL, "gl_quant_act_1x128: null pointer");
+  if (M < 0 || K <= 0 || K % 128 != 0)
+    return fail(GL_EINVAL, "gl_quant_act_1x128: need M >= 0 and K a positive multiple of 128");
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u))
+    return fail(GL_EINVAL, "gl_quant_act_1x128: x must be 16-byte and q 8-byte aligned");
+  if (M == 0) return GL_OK;
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  if (gl_launch_quant_act(x, M, K, q, s, static_cast<cudaStream_t>(stream), d->num_sms) != 0)
+    return fail(GL_ELAUNCH, std::string("quant_act launch: ") + cudaGetErrorString(cudaGetLastError()));
+  return GL_OK;
+}
+
+int gl_quant_w_128x128(const void* w, int64_t G, int64_t K, int64_t N, void* q, float* s,
+                       int* err_word, void* stream) {
+  (void)err_word;
+  if (!w || !q || !s) return fail(GL_EINVAL, "gl_quant_w_128x128: null pointer");
+  if (G <= 0 || K <= 0 || N <= 0 || K % 128 != 0 || N % 128 != 0)
+    return fail(GL_EINVAL, "gl_quant_w_128x128: need G > 0 and K, N positive multiples of 128");
+  if (!aligned16(w) || (reinterpret_cast<uintptr_t>(q) & 7u))
+    return fail(GL_EINVAL, "gl_quant_w_128x128: w must be 16-byte and q 8-byte aligned");
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  if (gl_launch_quant_w(w, G, K, N, q, s, static_cast<cudaStream_t>(stream), d->num_sms) != 0)
+    return fail(GL_ELAUNCH, std::string("quant_w launch: ") + cudaGetErrorString(cudaGetLastError()));
+  return GL_OK;
+}
+
+int gl_gmm_fp8_fwd(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
+                   const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                   void* out, int out_dtype, int* err_word, void* stream) {
+  if (!a_q || !a_s || !b_q || !b_s || !group_sizes || !out)
+    return fail(GL_EINVAL, "gl_gmm_fp8_fwd: null pointer");
+  if (G < 1 || G > 1024) return fail(GL_EINVAL, "gl_gmm_fp8_fwd: need 1 <= G <= 1024");
+  if (M < 0 || K <= 0 || N <= 0 || K % 128 != 0 || N % 128 != 0)
+    return fail(GL_EINVAL, "gl_gmm_fp8_fwd: need K, N positive multiples of 128");
+  if (M > (int64_t(1) << 31) - 256 || G * K > (int64_t(1) << 31) - 256)
+    return fail(GL_EINVAL, "gl_gmm_fp8_fwd: M and G*K must fit in 31 bits");
+  if (out_dtype != GL_OUT_BF16 && out_dtype != GL_OUT_F32)
+    return fail(GL_EINVAL, "gl_gmm_fp8_fwd: out_dtype must be GL_OUT_BF16 or GL_OUT_F32");
+  if (!aligned16(a_q) || !aligned16(b_q) || !aligned16(out))
+    return fail(GL_EINVAL, "gl_gmm_fp8_fwd: a_q, b_q and out must be 16-byte aligned");
+  if (M == 0) return GL_OK;
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  const char* why = "";
+  const int rc = gl_launch_gmm_fp8(a_q, a_s, b_q, b_s, group_sizes, G, M, K, N, out,
+                                   out_dtype == GL_OUT_F32, err_word ? err_word : d->err,
+                                   static_cast<cudaStream_t>(stream), d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string("gl_gmm_fp8_fwd: ") + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string("gl_gmm_fp8_fwd: ") + why);
+  return GL_OK;
+}
+
+int gl_chunk_gla_fwd(const void* q, const void* k, const void* v, const float* g,
+                     const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
+                     int64_t H, int64_t K, int64_t V, int64_t chunk_size, void* o, float* ht,
+                     int* err_word, void* stream) {
+  if (!q || !k || !v || !o) return fail(GL_EINVAL, "gl_chunk_gla_fwd: null pointer");
+  if ((g == nullptr) == (g_gamma == nullptr))
+    return fail(GL_EINVAL, "gl_chunk_gla_fwd: exactly one of g / g_gamma must be given");
+  if (K != 128 || V != 128) return fail(GL_EINVAL, "gl_chunk_gla_fwd: K and V must be 128");
+  if (chunk_size != 64) return fail(GL_EINVAL, "gl_chunk_gla_fwd: chunk_size must be 64");
+  if (B <= 0 || H <= 0 || T <= 0 || T % 64 != 0)
+    return fail(GL_EINVAL, "gl_chunk_gla_fwd: need B, H > 0 and T a positive multiple of 64");
+  if (B * T * H > (int64_t(1) << 31) - 1)
+    return fail(GL_EINVAL, "gl_chunk_gla_fwd: B*T*H must fit in 31 bits");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || (g && !aligned16(g)) ||
+      (h0 && !aligned16(h0)) || (ht && !aligned16(ht)))
+    return fail(GL_EINVAL, "gl_chunk_gla_fwd: tensors must be 16-byte aligned");
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  const char* why = "";
+  const int rc = gl_launch_chunk_gla(q, k, v, g, g_gamma, h0, scale, B, T, H, K, V, o, ht,
+                                     err_word ? err_word : d->err,
+                                     static_cast<cudaStream_t>(stream), d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string("gl_chunk_gla_fwd: ") + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string("gl_chunk_gla_fwd: ") + why);
+  return GL_OK;
+}
+
+int gl_device_status(int* err_word, void* stream, int* code) {
+  if (!code) return fail(GL_EINVAL, "gl_device_status: null code pointer");
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  int* w = err_word ? err_word : d->err;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("stream sync: ") + cudaGetErrorString(e));
+  int h = 0;
+  e = cudaMemcpyAsync(&h, w, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(w, 0, sizeof(int), st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("reading error word: ") + cudaGetErrorString(e));
+  *code = h;
+  return GL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,353 @@
+// Grouped (ragged) FP8 matmul forward with block-wise fp32 scales, sm_100a.
+//
+//   out[m, n] = sum_kb a_s[m, kb] * b_s[g, kb, n/128] * (a_q[m, kb-block] . b_q[g, kb-block, n])
+//
+// Replaces the tokamax Pallas TPU `gmm` call made by the Glaucis template
+// (KE/examples/kernels/gmm_fp8_blockwise.py:109-119).
+//
+// Design (one persistent CTA per SM, 320 threads, warp specialised):
+//   warp 0      TMA producer: per 128-deep K block loads the 128x128 e4m3
+//               activation tile (K-major) and the 128x256 e4m3 weight tile
+//               (N-major, two 128-byte-wide boxes) into a 4-stage ring.
+//   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (128x256x32) per K
+//               block into one of two TMEM accumulators (2 x 256 columns).
+//   warps 2-9   promotion + epilogue: after every K block each thread reads
+//               its row's 128 columns of the partial sum out of TMEM and
+//               accumulates partial * (a_s * b_s) in fp32 registers, releasing
+//               the TMEM buffer so the next K block's MMAs overlap the
+//               promotion.  The finished row is written as bf16 (or fp32).
+// Ragged groups: tiles never straddle a group; M tiles start at each group's
+// row offset, the last tile of a group is partial and its foreign rows are
+// computed but never stored.  The tile list (group-major, N outer, M inner so
+// CTAs running together share weight tiles in L2) is derived on the device
+// from group_sizes; no host synchronisation.
+#include "common.cuh"
+
+namespace gl {
+namespace gmm {
+
+constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
+constexpr int A_BYTES = BM * BK;  // 16 KB
+constexpr int B_BYTES = BK * BN;  // 32 KB
+constexpr int NUM_THREADS = 320;
+constexpr int MAX_G = 1024;
+constexpr int TMEM_COLS = 512;
+
+constexpr uint32_t OFF_A = 0;
+constexpr uint32_t OFF_B = OFF_A + STAGES * A_BYTES;
+constexpr uint32_t OFF_BAR = OFF_B + STAGES * B_BYTES;  // 196608
+constexpr uint32_t OFF_MISC = OFF_BAR + 128;
+constexpr uint32_t OFF_ROWOFF = OFF_MISC + 128;
+constexpr uint32_t OFF_TILEOFF = OFF_ROWOFF + (MAX_G + 1) * 4;
+constexpr uint32_t SMEM_USED = OFF_TILEOFF + (MAX_G + 1) * 4;
+constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;  // slack for 1 KB alignment
+
+// e4m3 x e4m3 -> f32, A K-major, B MN-major, M=128, N=256.
+constexpr uint32_t IDESC = idesc(1, 0, 0, 0, 1, BM, BN);
+
+struct Params {
+  const float* a_s;
+  const float* b_s;
+  const int32_t* group_sizes;
+  void* out;
+  int* err;
+  int G, M, K, N;
+  int out_f32;
+};
+
+struct Tile {
+  int g, m0, rows, n0;
+};
+
+__device__ __forceinline__ Tile decode_tile(int t, const int* tile_off, const int* row_off, int G) {
+  int lo = 0, hi = G - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tile_off[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  Tile r;
+  r.g = lo;
+  const int local = t - tile_off[lo];
+  const int size = row_off[lo + 1] - row_off[lo];
+  const int mt = (size + BM - 1) / BM;
+  const int i = local % mt, j = local / mt;
+  r.m0 = row_off[lo] + i * BM;
+  r.rows = min(BM, size - i * BM);
+  r.n0 = j * BN;
+  return r;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gmm_fp8_fwd_kernel(const __grid_constant__ CUtensorMap tm_a,
+                       const __grid_constant__ CUtensorMap tm_b, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  int* abort_flag = reinterpret_cast<int*>(smem + OFF_MISC + 4);
+  int* total_tiles_s = reinterpret_cast<int*>(smem + OFF_MISC + 8);
+  int* row_off = reinterpret_cast<int*>(smem + OFF_ROWOFF);
+  int* tile_off = reinterpret_cast<int*>(smem + OFF_TILEOFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G, K = p.K, N = p.N;
+  const int KB = K / BK, NB = N / 128;
+  const int ntn = (N + BN - 1) / BN;
+  const Abort ab{abort_flag, p.err};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_a);
+      prefetch_tmap(&tm_b);
+    }
+    tmem_alloc(tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int i = 0; i < STAGES; ++i) {
+        mbar_init(&full[i], 1);
+        mbar_init(&empty[i], 1);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&tfull[i], 1);
+        mbar_init(&tempty[i], 8);  // one arrival per epilogue warp
+      }
+      mbar_init(drain, 1);
+      *abort_flag = 0;
+      fence_mbar_init();
+    }
+  } else if (warp == 2) {
+    // Group table: exclusive prefix sums of rows and tiles (warp scan).
+    const int per = (G + 31) / 32;
+    const int g0 = min(G, lane * per), g1 = min(G, g0 + per);
+    int rsum = 0, tsum = 0, bad = 0;
+    for (int g = g0; g < g1; ++g) {
+      const int sz = p.group_sizes[g];
+      bad |= sz < 0;
+      const int s = max(sz, 0);
+      rsum += s;
+      tsum += (s + BM - 1) / BM * ntn;
+    }
+    int rinc = rsum, tinc = tsum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int rv = __shfl_up_sync(0xffffffffu, rinc, o);
+      const int tv = __shfl_up_sync(0xffffffffu, tinc, o);
+      if (lane >= o) {
+        rinc += rv;
+        tinc += tv;
+      }
+    }
+    int r = rinc - rsum, tt = tinc - tsum;
+    for (int g = g0; g < g1; ++g) {
+      const int s = max(p.group_sizes[g], 0);
+      row_off[g] = r;
+      tile_off[g] = tt;
+      r += s;
+      tt += (s + BM - 1) / BM * ntn;
+    }
+    bad = __any_sync(0xffffffffu, bad);
+    if (lane == 31) {
+      row_off[G] = rinc;
+      tile_off[G] = tinc;
+      const bool ok = !bad && rinc <= p.M;
+      *total_tiles_s = ok ? tinc : 0;
+      if (!ok) atomicExch(p.err, GL_DEV_BAD_GROUPS);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int total = *total_tiles_s;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const Tile tl = decode_tile(t, tile_off, row_off, G);
+        const int brow = tl.g * K;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, ab)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+          uint8_t* sa = smem + OFF_A + s * A_BYTES;
+          uint8_t* sb = smem + OFF_B + s * B_BYTES;
+          tma_load_2d(sa, &tm_a, &full[s], kb * BK, tl.m0);
+          tma_load_2d(sb, &tm_b, &full[s], tl.n0, brow + kb * BK);
+          tma_load_2d(sb + 16384, &tm_b, &full[s], tl.n0 + 128, brow + kb * BK);
+        }
+      }
+      if (!ok) {
+        // Let copies already in flight land before the CTA exits.
+        const int first = it > STAGES ? it - STAGES : 0;
+        for (int j = first; j < it; ++j) {
+          const int s = j % STAGES;
+          const uint64_t t0 = global_ns();
+          while (!mbar_try_wait(&full[s], (j / STAGES) & 1) && global_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA
+      int it = 0, acc_it = 0;
+      bool ok = true;
+      const uint32_t a_base = smem_u32(smem + OFF_A), b_base = smem_u32(smem + OFF_B);
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        for (int kb = 0; kb < KB; ++kb, ++it, ++acc_it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          const int buf = acc_it & 1;
+          const uint32_t aph = (acc_it >> 1) & 1;
+          if (!mbar_wait(&tempty[buf], aph ^ 1, ab)) { ok = false; break; }
+          if (!mbar_wait(&full[s], ph, ab)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d = tmem + buf * BN;
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            const uint64_t ad = sdesc(a_base + s * A_BYTES + kk * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bd = sdesc(b_base + s * B_BYTES + kk * 4096, 16384, 1024, kSwizzle128B);
+            mma_f8f6f4(d, ad, bd, IDESC, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+          tc_commit(&tfull[buf]);
+        }
+      }
+      // Wait for every MMA issued above before TMEM can be released.
+      tc_commit(drain);
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 100000000ull) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------- epilogue
+    const int ew = warp - 2;
+    const int quad = warp & 3;
+    const int chalf = ew >> 2;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + chalf * 128;
+    int acc_it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      const Tile tl = decode_tile(t, tile_off, row_off, G);
+      const bool row_ok = r < tl.rows;
+      const int64_t grow = static_cast<int64_t>(tl.m0) + r;
+      const int ncol0 = tl.n0 + chalf * 128;
+      const bool col_ok = ncol0 < N;
+      const int nb = ncol0 >> 7;
+      const float* sa_row = p.a_s + grow * KB;
+      const float* sb_col = p.b_s + static_cast<int64_t>(tl.g) * KB * NB + nb;
+      float acc[128];
+#pragma unroll
+      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      float sa_next = row_ok ? __ldg(sa_row) : 0.f;
+      float sb_next = col_ok ? __ldg(sb_col) : 0.f;
+      for (int kb = 0; kb < KB; ++kb, ++acc_it) {
+        const float sc = sa_next * sb_next;
+        if (kb + 1 < KB) {
+          sa_next = row_ok ? __ldg(sa_row + kb + 1) : 0.f;
+          sb_next = col_ok ? __ldg(sb_col + static_cast<int64_t>(kb + 1) * NB) : 0.f;
+        }
+        const int buf = acc_it & 1;
+        if (!mbar_wait(&tfull[buf], (acc_it >> 1) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ta = lane_base + buf * BN;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          uint32_t v[32];
+          tmem_ld32(ta + h * 32, v);
+          tmem_ld_wait(v);
+          if (h == 3) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[h * 32 + j] = fmaf(__uint_as_float(v[j]), sc, acc[h * 32 + j]);
+        }
+      }
+      if (!ok) break;
+      if (row_ok && col_ok) {
+        if (p.out_f32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + grow * N + ncol0);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + grow * N + ncol0);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            dst[i] = make_uint4(pack_bf16x2(acc[8 * i], acc[8 * i + 1]),
+                                pack_bf16x2(acc[8 * i + 2], acc[8 * i + 3]),
+                                pack_bf16x2(acc[8 * i + 4], acc[8 * i + 5]),
+                                pack_bf16x2(acc[8 * i + 6], acc[8 * i + 7]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace gmm
+}  // namespace gl
+
+// ---------------------------------------------------------------------------
+// Host launcher (called from capi.cu after argument validation).
+// ---------------------------------------------------------------------------
+#include "tmap.h"
+
+int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
+                      const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                      void* out, int out_f32, int* err, cudaStream_t st, int num_sms,
+                      const char** why) {
+  using namespace gl::gmm;
+  CUtensorMap tm_a, tm_b;
+  if (!gl_make_tmap_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, a_q, K, M, K, 128, 128,
+                       CU_TENSOR_MAP_SWIZZLE_128B, why))
+    return -1;
+  if (!gl_make_tmap_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, b_q, N, G * K, N, 128, 128,
+                       CU_TENSOR_MAP_SWIZZLE_128B, why))
+    return -1;
+  if (!gl_set_smem_attr(reinterpret_cast<const void*>(gl::gmm::gmm_fp8_fwd_kernel), 0,
+                        static_cast<int>(SMEM_BYTES), why))
+    return -2;
+  const int64_t ntn = (N + BN - 1) / BN;
+  const int64_t max_tiles = ((M + BM - 1) / BM + G) * ntn;
+  const int grid = static_cast<int>(max_tiles < num_sms ? (max_tiles > 0 ? max_tiles : 1) : num_sms);
+  Params p;
+  p.a_s = a_s;
+  p.b_s = b_s;
+  p.group_sizes = group_sizes;
+  p.out = out;
+  p.err = err;
+  p.G = static_cast<int>(G);
+  p.M = static_cast<int>(M);
+  p.K = static_cast<int>(K);
+  p.N = static_cast<int>(N);
+  p.out_f32 = out_f32;
+  gl::gmm::gmm_fp8_fwd_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tm_a, tm_b, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return -2;
+  }
+  return 0;
+}

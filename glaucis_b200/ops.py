@@ -1,0 +1,200 @@
+"""Torch-facing ops over the C ABI.  Tensors must live on a CUDA device; every
+op launches on the current stream and never falls back to another backend.
+
+Op names and argument meaning mirror the Glaucis kernel templates
+(KE/examples/kernels/gmm_fp8_blockwise.py, KE/examples/kernels/chunk_gla.py).
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+FP8 = torch.float8_e4m3fn
+TILE = 128
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need_cuda(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("glaucis_b200 ops take CUDA tensors (no CPU path)")
+        if not t.is_contiguous():
+            raise ValueError("glaucis_b200 ops take contiguous tensors")
+
+
+# ---------------------------------------------------------------------------
+# Block-wise FP8 quantisers
+# ---------------------------------------------------------------------------
+def quant_act_1x128(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [M, K] -> (e4m3 [M, K], fp32 scales [M, K/128]).
+
+    Replaces qwix.pallas.quantize(lhs, channelwise_axes=[0], tiled_axes={1: 128},
+    absmax, fp32 scale) at KE/examples/kernels/gmm_fp8_blockwise.py:84-91.
+    """
+    _need_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise ValueError("quant_act_1x128 expects a 2-D bf16 tensor")
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=FP8, device=x.device)
+    s = torch.empty((M, K // TILE), dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    _lib.check(lib.gl_quant_act_1x128(x.data_ptr(), M, K, q.data_ptr(), s.data_ptr(), None,
+                                      _stream()), "gl_quant_act_1x128")
+    return q, s
+
+
+def quant_w_128x128(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [G, K, N] -> (e4m3 [G, K, N], fp32 scales [G, K/128, N/128]).
+
+    Replaces qwix.pallas.quantize(rhs, channelwise_axes=[0],
+    tiled_axes={1: 128, 2: 128}) at KE/examples/kernels/gmm_fp8_blockwise.py:100-107.
+    """
+    _need_cuda(w)
+    if w.dtype != torch.bfloat16 or w.dim() != 3:
+        raise ValueError("quant_w_128x128 expects a 3-D bf16 tensor")
+    G, K, N = w.shape
+    q = torch.empty((G, K, N), dtype=FP8, device=w.device)
+    s = torch.empty((G, K // TILE, N // TILE), dtype=torch.float32, device=w.device)
+    lib = _lib.load()
+    _lib.check(lib.gl_quant_w_128x128(w.data_ptr(), G, K, N, q.data_ptr(), s.data_ptr(), None,
+                                      _stream()), "gl_quant_w_128x128")
+    return q, s
+
+
+# ---------------------------------------------------------------------------
+# Grouped matmul
+# ---------------------------------------------------------------------------
+def gmm_fp8_fwd(a_q: torch.Tensor, a_s: torch.Tensor, b_q: torch.Tensor, b_s: torch.Tensor,
+                group_sizes: torch.Tensor, out_dtype: torch.dtype = torch.float32,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Grouped matmul on pre-quantised operands (QArray-equivalent inputs).
+
+    Replaces tokamax pallas_mosaic_tpu_kernel.gmm(lhs=QArray, rhs=QArray,
+    group_sizes, out_dtype, transpose_rhs=False) at
+    KE/examples/kernels/gmm_fp8_blockwise.py:109-119.  Rows at or beyond
+    sum(group_sizes) are zero.
+    """
+    _need_cuda(a_q, a_s, b_q, b_s, group_sizes)
+    M, K = a_q.shape
+    G, K2, N = b_q.shape
+    if K2 != K:
+        raise ValueError(f"K mismatch: lhs {K} vs rhs {K2}")
+    if group_sizes.dtype != torch.int32 or group_sizes.numel() != G:
+        raise ValueError("group_sizes must be int32 [G]")
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("out_dtype must be bf16 or fp32")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a_q.device)
+    code = _lib.GL_OUT_F32 if out.dtype == torch.float32 else _lib.GL_OUT_BF16
+    lib = _lib.load()
+    _lib.check(lib.gl_gmm_fp8_fwd(a_q.data_ptr(), a_s.data_ptr(), b_q.data_ptr(), b_s.data_ptr(),
+                                  group_sizes.data_ptr(), G, M, K, N, out.data_ptr(), code, None,
+                                  _stream()), "gl_gmm_fp8_fwd")
+    return out
+
+
+def _zero_tail_rows(out: torch.Tensor, group_sizes: torch.Tensor) -> None:
+    # Rows past sum(group_sizes) belong to no group: zero them on the device
+    # without a host round trip.
+    M = out.shape[0]
+    total = group_sizes.sum()
+    rows = torch.arange(M, device=out.device)
+    out.masked_fill_((rows >= total).unsqueeze(1), 0)
+
+
+def gmm_fp8_blockwise(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.Tensor,
+                      tiling: tuple = (256, 512, 256, 256, 512, 128, 1024, 512, 128),
+                      out_dtype: torch.dtype = torch.float32,
+                      zero_unassigned_rows: bool = True) -> torch.Tensor:
+    """Forward of the Glaucis `gmm_fp8_blockwise(lhs, rhs, group_sizes, tiling)`
+    (KE/examples/kernels/gmm_fp8_blockwise.py:53-120): quantise lhs 1x128 and
+    rhs 128x128 to e4m3 with fp32 absmax scales, then the grouped matmul with
+    per-K-block fp32 promotion.  `tiling` is accepted for signature
+    compatibility; the B200 kernel's tiles are fixed (128x256x128).
+    """
+    del tiling
+    a_q, a_s = quant_act_1x128(lhs)
+    b_q, b_s = quant_w_128x128(rhs)
+    out = gmm_fp8_fwd(a_q, a_s, b_q, b_s, group_sizes, out_dtype=out_dtype)
+    if zero_unassigned_rows:
+        _zero_tail_rows(out, group_sizes)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Chunked GLA forward
+# ---------------------------------------------------------------------------
+class GLAForward(tuple):
+    """Result of chunk_gla_fwd, unpackable as the reference's
+    (g_cumsum, A, h, o).  The fused kernel keeps g_cumsum, A and the per-chunk
+    states on chip, so those entries are None; the final state is `.ht`."""
+
+    def __new__(cls, o: torch.Tensor, ht: Optional[torch.Tensor]):
+        self = tuple.__new__(cls, (None, None, None, o))
+        self.ht = ht
+        return self
+
+    @property
+    def o(self) -> torch.Tensor:
+        return self[3]
+
+
+def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                  g_gamma: Optional[torch.Tensor], scale: float, chunk_size: int = 64, *,
+                  g: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
+                  output_final_state: bool = False,
+                  o: Optional[torch.Tensor] = None,
+                  ht: Optional[torch.Tensor] = None) -> GLAForward:
+    """Chunked GLA forward (KE/examples/kernels/chunk_gla.py:258-273), fused
+    into one kernel.  Either the per-head constant gate `g_gamma` [H] (the
+    reference template's mode) or the per-key log-gate `g` [B, T, H, K] (raw,
+    chunk-local cumsum taken in-kernel; semantics of
+    KE/upstream/fused_chunk_simple_gla/common_chunk_h.py:330-334) is used.
+    """
+    _need_cuda(q, k, v, g_gamma, g, h0)
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bf16")
+    if g is not None and (g.dtype != torch.float32 or tuple(g.shape) != (B, T, H, K)):
+        raise ValueError("g must be fp32 [B, T, H, K]")
+    if g_gamma is not None and (g_gamma.dtype != torch.float32 or g_gamma.numel() != H):
+        raise ValueError("g_gamma must be fp32 [H]")
+    if h0 is not None and (h0.dtype != torch.float32 or tuple(h0.shape) != (B, H, K, V)):
+        raise ValueError("h0 must be fp32 [B, H, K, V]")
+    if o is None:
+        o = torch.empty((B, T, H, V), dtype=torch.bfloat16, device=q.device)
+    if output_final_state and ht is None:
+        ht = torch.empty((B, H, K, V), dtype=torch.float32, device=q.device)
+    lib = _lib.load()
+    _lib.check(lib.gl_chunk_gla_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
+                                    _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
+                                    chunk_size, o.data_ptr(), _ptr(ht), None, _stream()),
+               "gl_chunk_gla_fwd")
+    return GLAForward(o, ht if output_final_state else None)
+
+
+def chunk_gla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g_gamma: torch.Tensor,
+              scale: float, chunk_size: int = 64) -> torch.Tensor:
+    """Forward of `chunk_gla(q, k, v, g_gamma, scale, chunk_size)`
+    (KE/examples/kernels/chunk_gla.py:434-456).  Returns o (bf16)."""
+    return chunk_gla_fwd(q, k, v, g_gamma, scale, chunk_size).o
+
+
+def device_status() -> int:
+    """Synchronises the current stream and returns (and clears) the library's
+    device error word: 0 when no kernel reported a problem."""
+    return _lib.device_status(_stream())

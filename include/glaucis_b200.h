@@ -1,0 +1,140 @@
+/*
+ * glaucis_b200 — C ABI of the B200 (sm_100a) kernels behind the two scored
+ * kernel templates of the Glaucis kernel evaluator:
+ *
+ *   gmm_fp8_blockwise  grouped (ragged, MoE-style) matmul with block-wise FP8
+ *                      quantisation: activations 1x128 fp32 scales, weights
+ *                      128x128 fp32 scales, fp32 accumulation.
+ *   chunk_gla          chunked Gated Linear Attention, forward.
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers owned by the caller.  The library
+ *     borrows them for the duration of the (asynchronous) call and never
+ *     frees or retains them.
+ *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy
+ *     default stream.  Every call is stream-ordered and returns before the
+ *     GPU work finishes.
+ *   - `err_word` is an optional device int.  Kernels write a non-zero
+ *     GL_DEV_* code there when a bounded device-side wait gives up; pass NULL
+ *     to use a per-device word owned by the library.  Read it back with
+ *     gl_device_status().
+ *   - Return value: GL_OK (0) on a successful launch, a negative GL_E* code
+ *     otherwise; gl_last_error() then holds a message (per host thread).
+ *
+ * Each entry point names the reference interface it replaces (paths are
+ * relative to the Glaucis repository, kernel-evolve = KE).
+ */
+#ifndef GLAUCIS_B200_H
+#define GLAUCIS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. */
+#define GL_OK 0
+#define GL_EINVAL (-1)   /* bad shape, alignment or argument */
+#define GL_ELAUNCH (-2)  /* CUDA launch / driver failure */
+#define GL_EDEVICE (-3)  /* device error word was set */
+
+/* Device error word codes (written by kernels). */
+#define GL_DEV_OK 0
+#define GL_DEV_WAIT_TIMEOUT 1   /* an mbarrier wait exceeded its poll budget */
+#define GL_DEV_BAD_GROUPS 2     /* group_sizes sum exceeds M or a size < 0 */
+
+/* Output dtypes of the grouped matmul. */
+#define GL_OUT_BF16 0
+#define GL_OUT_F32 1
+
+/*
+ * Block-wise activation quantiser, 1x128 tiles along K.
+ *   x  bf16 [M, K] row-major, K % 128 == 0
+ *   q  e4m3fn [M, K] row-major (one byte per element)
+ *   s  fp32 [M, K/128] row-major, s = absmax(block)/448 (1.0 for an all-zero
+ *      block), q = round-to-nearest-even(x / s) saturated to +-448.
+ * Replaces: qwix.pallas.quantize(lhs, float8_e4m3fn, channelwise_axes=[0],
+ *   tiled_axes={1: 128}, calibration_method="absmax", scale_dtype=f32)
+ *   called at KE/examples/kernels/gmm_fp8_blockwise.py:84-91.
+ */
+int gl_quant_act_1x128(const void* x, int64_t M, int64_t K, void* q, float* s,
+                       int* err_word, void* stream);
+
+/*
+ * Block-wise weight quantiser, 128x128 tiles over (K, N) per group.
+ *   w  bf16 [G, K, N] row-major, K % 128 == 0, N % 128 == 0
+ *   q  e4m3fn [G, K, N] row-major
+ *   s  fp32 [G, K/128, N/128]
+ * Replaces: qwix.pallas.quantize(rhs, float8_e4m3fn, channelwise_axes=[0],
+ *   tiled_axes={1: 128, 2: 128}, ...) at
+ *   KE/examples/kernels/gmm_fp8_blockwise.py:100-107.
+ */
+int gl_quant_w_128x128(const void* w, int64_t G, int64_t K, int64_t N, void* q,
+                       float* s, int* err_word, void* stream);
+
+/*
+ * Grouped matmul forward on pre-quantised operands:
+ *   out[m, n] = sum_kb a_s[m, kb] * b_s[g, kb, n/128]
+ *                      * sum_{k in block kb} a_q[m, k] * b_q[g, k, n]
+ * where rows [off_g, off_g + group_sizes[g]) belong to group g and off_g is
+ * the exclusive prefix sum of group_sizes.  Rows at or beyond
+ * sum(group_sizes) are not written.
+ *   a_q e4m3fn [M, K], a_s fp32 [M, K/128]      (layout of gl_quant_act_1x128)
+ *   b_q e4m3fn [G, K, N], b_s fp32 [G, K/128, N/128] (gl_quant_w_128x128)
+ *   group_sizes int32 [G] (device), out [M, N] bf16 or fp32 (out_dtype).
+ *   K % 128 == 0, N % 128 == 0, 1 <= G <= 1024.
+ * Replaces: tokamax pallas_mosaic_tpu_kernel.gmm(lhs=QArray, rhs=QArray,
+ *   group_sizes, out_dtype=f32, transpose_rhs=False) at
+ *   KE/examples/kernels/gmm_fp8_blockwise.py:109-119 (reference oracle:
+ *   KE/examples/kernels/gmm_fp8_blockwise_ref.py:67-77).
+ */
+int gl_gmm_fp8_fwd(const void* a_q, const float* a_s, const void* b_q,
+                   const float* b_s, const int32_t* group_sizes, int64_t G,
+                   int64_t M, int64_t K, int64_t N, void* out, int out_dtype,
+                   int* err_word, void* stream);
+
+/*
+ * Chunked Gated Linear Attention forward (fixed-length sequences).
+ *   q, k  bf16 [B, T, H, K];  v bf16 [B, T, H, V];  K == 128, V == 128
+ *   g       fp32 [B, T, H, K] per-key log-gate (raw, not cumsummed) or NULL
+ *   g_gamma fp32 [H] per-head constant log-gate or NULL (exactly one of
+ *           g / g_gamma must be non-NULL)
+ *   h0      fp32 [B, H, K, V] initial state or NULL (zeros)
+ *   o       bf16 [B, T, H, V] output
+ *   ht      fp32 [B, H, K, V] final state or NULL (not written)
+ *   chunk_size == 64, T % 64 == 0.
+ * Semantics: within each chunk G = cumsum(g) (chunk-local);
+ *   o = scale*(q*e^G) h_n + tril(scale*(q*e^G)(k*e^-G)^T) v
+ *   h_{n+1} = e^{G_last} * h_n + (k*e^{G_last-G})^T v.
+ * Replaces: chunk_gla_fwd(q, k, v, g_gamma, scale, chunk_size) at
+ *   KE/examples/kernels/chunk_gla.py:258-273 (three pallas_calls
+ *   chunk_fwd_h :94-138, chunk_gla_fwd_intra_gk :163-188,
+ *   chunk_gla_fwd_o_gk :218-250), with the per-key gate / h0 / final-state
+ *   semantics of chunk_fwd_h_ref at
+ *   KE/upstream/fused_chunk_simple_gla/common_chunk_h.py:363-489.
+ */
+int gl_chunk_gla_fwd(const void* q, const void* k, const void* v, const float* g,
+                     const float* g_gamma, const float* h0, float scale,
+                     int64_t B, int64_t T, int64_t H, int64_t K, int64_t V,
+                     int64_t chunk_size, void* o, float* ht, int* err_word,
+                     void* stream);
+
+/*
+ * Synchronises `stream`, reads the device error word (the library word when
+ * err_word is NULL) into *code and clears it.  Returns GL_OK or GL_ELAUNCH.
+ */
+int gl_device_status(int* err_word, void* stream, int* code);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* gl_last_error(void);
+
+/* Library version string. */
+const char* gl_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GLAUCIS_B200_H */

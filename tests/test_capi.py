@@ -1,0 +1,74 @@
+"""The C-ABI library loads and exports every symbol the header declares; the
+argument checks that run before any device work reject bad calls (no GPU)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from glaucis_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "glaucis_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\s*\*)\s*(gl_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_abi():
+    syms = declared_symbols()
+    assert set(_lib.SIGNATURES) == set(syms), syms
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_lib.lib_path()))
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+    assert _lib.load().gl_version().startswith(b"glaucis_b200")
+
+
+def _err():
+    return _lib.load().gl_last_error().decode()
+
+
+def test_gmm_rejects_bad_arguments_without_device():
+    lib = _lib.load()
+    rc = lib.gl_gmm_fp8_fwd(None, None, None, None, None, 4, 128, 256, 256, None, 0, None, None)
+    assert rc == _lib.GL_EINVAL and "null pointer" in _err()
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    rc = lib.gl_gmm_fp8_fwd(p, p, p, p, p, 4, 128, 200, 256, p, 0, None, None)
+    assert rc == _lib.GL_EINVAL and "multiples of 128" in _err()
+    rc = lib.gl_gmm_fp8_fwd(p, p, p, p, p, 0, 128, 256, 256, p, 0, None, None)
+    assert rc == _lib.GL_EINVAL and "G" in _err()
+    rc = lib.gl_gmm_fp8_fwd(p, p, p, p, p, 4, 128, 256, 256, p, 7, None, None)
+    assert rc == _lib.GL_EINVAL and "out_dtype" in _err()
+
+
+def test_gla_rejects_bad_arguments_without_device():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    f = ctypes.c_void_p(32)
+    rc = lib.gl_chunk_gla_fwd(p, p, p, f, f, None, 0.1, 1, 64, 1, 128, 128, 64, p, None, None, None)
+    assert rc == _lib.GL_EINVAL and "exactly one" in _err()
+    rc = lib.gl_chunk_gla_fwd(p, p, p, f, None, None, 0.1, 1, 64, 1, 64, 128, 64, p, None, None, None)
+    assert rc == _lib.GL_EINVAL and "128" in _err()
+    rc = lib.gl_chunk_gla_fwd(p, p, p, f, None, None, 0.1, 1, 100, 1, 128, 128, 64, p, None, None, None)
+    assert rc == _lib.GL_EINVAL and "multiple of 64" in _err()
+    rc = lib.gl_chunk_gla_fwd(p, p, p, f, None, None, 0.1, 1, 64, 1, 128, 128, 32, p, None, None, None)
+    assert rc == _lib.GL_EINVAL and "chunk_size" in _err()
+
+
+def test_quantisers_reject_bad_arguments_without_device():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    assert lib.gl_quant_act_1x128(p, 4, 100, p, p, None, None) == _lib.GL_EINVAL
+    assert lib.gl_quant_w_128x128(p, 1, 128, 96, p, p, None, None) == _lib.GL_EINVAL
+    assert lib.gl_quant_act_1x128(None, 4, 128, p, p, None, None) == _lib.GL_EINVAL
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from glaucis_b200 import ops
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.quant_act_1x128(torch.zeros(4, 128, dtype=torch.bfloat16))

@@ -1,0 +1,107 @@
+"""Parity of the fused sm_100a chunked-GLA forward against the CPU oracle,
+through the C ABI.
+
+Tolerance (o and the final state): |gpu - ref| <= 2e-2 * |ref| + 2e-2 * rms(ref)
+element-wise, plus a relative Frobenius error below 1e-2.  The kernel feeds
+the tensor cores bf16 operands (q e^G, k e^-G, tril(A), the state copy h_n)
+with fp32 accumulation and an fp32 recurrent state; the oracle is fp32
+throughout, as the reference's Precision.HIGHEST path.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from glaucis_b200 import configs, ops
+from oracle import gla_oracle as O
+from oracle.gmm_oracle import bf16_bits_to_f32
+from tests.helpers import assert_close, rel_fro
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+RTOL, ATOL_FRAC, FRO = 2e-2, 2e-2, 1e-2
+
+
+def _run(cuda, cfg: configs.GLAConfig, seed=0):
+    inp = configs.make_gla_inputs(cfg, device="cpu", seed=seed)
+    dev = {k: (v.to(cuda) if v is not None else None) for k, v in inp.items()}
+    res = ops.chunk_gla_fwd(dev["q"], dev["k"], dev["v"], dev["g_gamma"], cfg.K ** -0.5, cfg.C,
+                            g=dev["g"], h0=dev["h0"], output_final_state=True)
+    assert ops.device_status() == 0
+    f = lambda t: None if t is None else t.float().numpy()
+    ref_o, ref_ht = O.chunk_gla_fwd(f(inp["q"]), f(inp["k"]), f(inp["v"]), g=f(inp["g"]),
+                                    g_gamma=f(inp["g_gamma"]), h0=f(inp["h0"]),
+                                    scale=cfg.K ** -0.5, chunk_size=cfg.C)
+    got_o = res.o.float().cpu().numpy()
+    got_ht = res.ht.cpu().numpy()
+    return got_o, got_ht, ref_o, ref_ht
+
+
+def _check(got_o, got_ht, ref_o, ref_ht, what):
+    assert_close(got_o, ref_o, RTOL, ATOL_FRAC, what=f"{what} o")
+    assert_close(got_ht, ref_ht, RTOL, ATOL_FRAC, what=f"{what} ht")
+    assert rel_fro(got_o, ref_o) < FRO, rel_fro(got_o, ref_o)
+    assert rel_fro(got_ht, ref_ht) < FRO, rel_fro(got_ht, ref_ht)
+
+
+@pytest.mark.parametrize("h0", [0.0, 0.1])
+def test_gla_per_key_gate_split_v(cuda, h0):
+    # B*H small -> the V dimension is split across two CTAs per sequence
+    cfg = configs.GLAConfig("t", B=2, T=256, H=3, h0_std=h0)
+    _check(*_run(cuda, cfg), what=f"per-key h0={h0}")
+
+
+def test_gla_per_key_gate_full_v(cuda):
+    # B*H > SMs/2 -> one CTA per sequence with the full V = 128 width
+    cfg = configs.GLAConfig("t", B=2, T=128, H=40, h0_std=0.1)
+    _check(*_run(cuda, cfg), what="per-key full-V")
+
+
+def test_gla_gamma_gate_reference_mode(cuda):
+    # the template's own mode: per-head constant gate g_gamma [H], no h0
+    cfg = configs.GLAConfig("t", B=2, T=320, H=4, gate="gamma")
+    _check(*_run(cuda, cfg, seed=5), what="g_gamma")
+
+
+def test_gla_single_chunk(cuda):
+    cfg = configs.GLAConfig("t", B=1, T=64, H=1, h0_std=0.1)
+    _check(*_run(cuda, cfg, seed=2), what="T=C")
+
+
+def test_gla_golden_fixture(cuda):
+    d = np.load(os.path.join(GOLDEN, "gla_per_key_h0.npz"))
+    to_bf = lambda a: torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).to(cuda)
+    res = ops.chunk_gla_fwd(to_bf(d["q_bf16"]), to_bf(d["k_bf16"]), to_bf(d["v_bf16"]), None,
+                            128 ** -0.5, 64, g=torch.from_numpy(d["g"]).to(cuda),
+                            h0=torch.from_numpy(d["h0"]).to(cuda), output_final_state=True)
+    _check(res.o.float().cpu().numpy(), res.ht.cpu().numpy(), d["o"], d["ht"], what="golden")
+
+
+def test_gla_public_chunk_gla_op(cuda):
+    cfg = configs.GLAConfig("t", B=1, T=128, H=2, gate="gamma")
+    inp = configs.make_gla_inputs(cfg, device="cpu", seed=9)
+    o = ops.chunk_gla(inp["q"].to(cuda), inp["k"].to(cuda), inp["v"].to(cuda),
+                      inp["g_gamma"].to(cuda), 128 ** -0.5, 64)
+    assert o.shape == (1, 128, 2, 128) and o.dtype == torch.bfloat16
+    ref, _ = O.chunk_gla_fwd(inp["q"].float().numpy(), inp["k"].float().numpy(),
+                             inp["v"].float().numpy(), g_gamma=inp["g_gamma"].numpy())
+    assert_close(o.float().cpu().numpy(), ref, RTOL, ATOL_FRAC, what="chunk_gla")
+
+
+@pytest.mark.parametrize("name", ["gla_b8_t4096", "gla_b1_t32768"])
+def test_gla_full_size_sampled_heads(cuda, name):
+    # Full benchmark shapes on the GPU; the oracle recomputes three (b, h)
+    # sequences end to end (state carried through every chunk).
+    cfg = configs.GLA_CONFIGS[name]
+    inp = configs.make_gla_inputs(cfg, device=cuda, seed=0)
+    res = ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], cfg.K ** -0.5, cfg.C,
+                            g=inp["g"], h0=inp["h0"], output_final_state=True)
+    assert ops.device_status() == 0
+    for (b, h) in [(0, 0), (cfg.B - 1, cfg.H - 1), (cfg.B // 2, cfg.H // 3)]:
+        sl = lambda t: t[b:b + 1, :, h:h + 1].float().cpu().numpy()
+        h0 = None if inp["h0"] is None else inp["h0"][b:b + 1, h:h + 1].cpu().numpy()
+        ref_o, ref_ht = O.chunk_gla_fwd(sl(inp["q"]), sl(inp["k"]), sl(inp["v"]), g=sl(inp["g"]),
+                                        h0=h0, scale=cfg.K ** -0.5)
+        _check(sl(res.o), res.ht[b:b + 1, h:h + 1].cpu().numpy(), ref_o, ref_ht,
+               what=f"{name} (b={b}, h={h})")

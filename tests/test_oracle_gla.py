@@ -1,0 +1,72 @@
+"""CPU checks of the chunked-GLA oracle (no GPU)."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import gla_oracle as O
+from oracle.gmm_oracle import bf16_bits_to_f32
+from tests.helpers import assert_close
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _inputs(B, T, H, seed, gate="per_key", h0=True):
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((B, T, H, 128)).astype(np.float32)
+    k = rng.standard_normal((B, T, H, 128)).astype(np.float32)
+    v = rng.standard_normal((B, T, H, 128)).astype(np.float32)
+    g = (-np.logaddexp(0.0, -rng.standard_normal((B, T, H, 128))) / 16).astype(np.float32)
+    gg = (-np.abs(rng.standard_normal(H)) * 0.1).astype(np.float32)
+    hh = (rng.standard_normal((B, H, 128, 128)) * 0.1).astype(np.float32) if h0 else None
+    return q, k, v, (g if gate == "per_key" else None), (gg if gate == "gamma" else None), hh
+
+
+@pytest.mark.parametrize("gate", ["per_key", "gamma"])
+@pytest.mark.parametrize("h0", [False, True])
+def test_chunked_matches_token_recurrence(gate, h0):
+    q, k, v, g, gg, hh = _inputs(2, 192, 2, seed=1, gate=gate, h0=h0)
+    o, ht = O.chunk_gla_fwd(q, k, v, g=g, g_gamma=gg, h0=hh)
+    o2, ht2 = O.naive_recurrence(q, k, v, g=g, g_gamma=gg, h0=hh)
+    assert_close(o, o2, rtol=1e-4, atol_frac=1e-5, what="o")
+    assert_close(ht, ht2, rtol=1e-4, atol_frac=1e-5, what="ht")
+
+
+def test_gamma_equals_broadcast_per_key_gate():
+    # chunk_gla_ref.py:109-111 builds g_cumsum = g_gamma * (1..C); a per-key
+    # gate equal to g_gamma at every token must give the same result.
+    q, k, v, _, gg, hh = _inputs(1, 128, 3, seed=2, gate="gamma")
+    g = np.broadcast_to(gg.reshape(1, 1, 3, 1), (1, 128, 3, 128)).astype(np.float32)
+    a = O.chunk_gla_fwd(q, k, v, g_gamma=gg, h0=hh)
+    b = O.chunk_gla_fwd(q, k, v, g=g, h0=hh)
+    assert_close(a[0], b[0], rtol=1e-3, atol_frac=1e-5, what="o")
+    assert_close(a[1], b[1], rtol=1e-3, atol_frac=1e-5, what="ht")
+
+
+def test_reference_cpu_smoke_shape():
+    # KE/tests/test_chunk_gla.py:81-95: B=1, T=64, H=2, K=V=128, chunk 16.
+    q, k, v, _, gg, _ = _inputs(1, 64, 2, seed=3, gate="gamma", h0=False)
+    o, ht = O.chunk_gla_fwd(q, k, v, g_gamma=gg, chunk_size=16)
+    assert o.shape == (1, 64, 2, 128) and np.isfinite(o).all()
+    o64, _ = O.chunk_gla_fwd(q, k, v, g_gamma=gg, chunk_size=64)
+    assert_close(o, o64, rtol=1e-4, atol_frac=1e-5, what="chunk-size invariance")
+
+
+def test_states_are_stored_before_update():
+    q, k, v, g, _, hh = _inputs(1, 128, 1, seed=4)
+    _, _, h_all = O.chunk_gla_fwd(q, k, v, g=g, h0=hh, return_states=True)
+    assert np.array_equal(h_all[:, 0], hh)
+
+
+def test_golden_fixture_reproduces():
+    d = np.load(os.path.join(GOLDEN, "gla_per_key_h0.npz"))
+    f = bf16_bits_to_f32
+    o, ht = O.chunk_gla_fwd(f(d["q_bf16"]), f(d["k_bf16"]), f(d["v_bf16"]), g=d["g"],
+                            h0=d["h0"], scale=128 ** -0.5)
+    assert_close(o, d["o"], rtol=1e-5, atol_frac=1e-6, what="golden o")
+    assert_close(ht, d["ht"], rtol=1e-5, atol_frac=1e-6, what="golden ht")
+
+
+def test_flop_and_byte_model():
+    assert O.gla_flops(8, 4096, 16) == pytest.approx(51.54e9, rel=1e-3)
+    assert O.gla_bytes(8, 4096, 16) == pytest.approx(0.814e9, rel=2e-2)
