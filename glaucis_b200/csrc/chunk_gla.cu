@@ -18,12 +18,15 @@
 // once and o (+ the final state) written once.
 //
 // One CTA per (batch, head, V slice of width VS), 512 threads:
-//   warp 0        TMA producer (q, k, v chunk; g chunk)
-//   warp 1        tcgen05.mma issuer
+//   warp 0        TMA producer (g chunk, then q, k, v chunk; 2-stage rings)
+//   warp 1        tcgen05.mma issuer, one chunk ahead: A_{n+1}, S_{n+1}, O_n
 //   warp 2        TMEM allocator
-//   warps 4-7     gating (thread = key), then A -> tril -> bf16 P
-//   warps 8-15    two warpgroups, each owning VS/2 state columns: state
-//                 update (thread = key row), then the O epilogue
+//   warps 4-7     gating (thread = key): Qs, Kg in place, e^{G_last}
+//   warps 8-15    two warpgroups, each owning VS/2 state columns and 32 of
+//                 the 64 P columns: A -> tril -> bf16 P, state update
+//                 (thread = key row), the O epilogue
+// Buffers: g, q, k, v double-buffered; A double-buffered in TMEM; P and the
+// bf16 state copy H single-buffered (rewritten only after O_n completed).
 #include "common.cuh"
 
 namespace gl {
@@ -43,15 +46,15 @@ struct Cfg {
   static constexpr uint32_t OFF_K = OFF_Q + 2 * Q_BYTES;
   static constexpr uint32_t OFF_V = OFF_K + 2 * Q_BYTES;
   static constexpr uint32_t OFF_G = OFF_V + 2 * V_BYTES;
-  static constexpr uint32_t OFF_P = OFF_G + G_BYTES;
+  static constexpr uint32_t OFF_P = OFF_G + 2 * G_BYTES;
   static constexpr uint32_t OFF_H = OFF_P + P_BYTES;
-  static constexpr uint32_t OFF_DEC = OFF_H + 2 * H_BYTES;  // 2 x 128 floats
+  static constexpr uint32_t OFF_DEC = OFF_H + H_BYTES;      // 2 x 128 floats
   static constexpr uint32_t OFF_BAR = OFF_DEC + 2 * KD * 4;
   static constexpr uint32_t OFF_MISC = OFF_BAR + 256;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;
-  // TMEM columns: A [0,64), O [64,64+VS), S0, S1
-  static constexpr uint32_t COL_A = 0, COL_O = 64, COL_S = 64 + VS;
-  static constexpr uint32_t TMEM_COLS = (64 + 3 * VS) <= 256 ? 256 : 512;
+  // TMEM columns: A0, A1 [0,128), O [128,128+VS), S0, S1
+  static constexpr uint32_t COL_A = 0, COL_O = 128, COL_S = 128 + VS;
+  static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t IDESC_A = idesc(1, 1, 1, 0, 0, 64, 64);    // bf16, K-major x K-major
   static constexpr uint32_t IDESC_S = idesc(1, 1, 1, 1, 1, 128, VS);  // MN-major x MN-major
   static constexpr uint32_t IDESC_O = idesc(1, 1, 1, 0, 1, 64, VS);   // K-major x MN-major
@@ -68,25 +71,25 @@ struct Params {
   int has_g;
 };
 
-// Barrier indices.
+// Barrier indices ([2] = one per buffer).
 enum {
-  B_QKV_FULL = 0,   // [2]
-  B_QKV_EMPTY = 2,  // [2]
-  B_G_FULL = 4,
-  B_G_EMPTY = 5,
-  B_PREP = 6,       // [2]
-  B_DEC_FULL = 8,   // [2]
-  B_DEC_EMPTY = 10, // [2]
-  B_A_FULL = 12,
-  B_A_EMPTY = 13,
-  B_P_FULL = 14,
-  B_S_FULL = 15,    // [2]
-  B_S_EMPTY = 17,   // [2]
-  B_H_FULL = 19,    // [2]
-  B_O_FULL = 21,
-  B_O_EMPTY = 22,
-  B_DRAIN = 23,
-  NUM_BARS = 24
+  B_QKV_FULL = 0,    // [2] TMA -> gating
+  B_QKV_EMPTY = 2,   // [2] O_n committed -> TMA
+  B_G_FULL = 4,      // [2] TMA -> gating
+  B_G_EMPTY = 6,     // [2] gating -> TMA (4 warps)
+  B_PREP = 8,        // [2] gating -> MMA (4 warps)
+  B_DEC_FULL = 10,   // [2] gating -> state (4 warps)
+  B_DEC_EMPTY = 12,  // [2] state -> gating (8 warps)
+  B_A_FULL = 14,     // [2] MMA A_n committed -> P epilogue
+  B_A_EMPTY = 16,    // [2] P epilogue -> MMA (8 warps)
+  B_S_FULL = 18,     // [2] MMA S_n committed -> state
+  B_S_EMPTY = 20,    // [2] state -> MMA (8 warps)
+  B_P_FULL = 22,     // P written -> MMA (8 warps)
+  B_H_FULL = 23,     // H_n written -> MMA (8 warps)
+  B_O_FULL = 24,     // MMA O_n committed -> state
+  B_O_EMPTY = 25,    // O read -> MMA (8 warps)
+  B_DRAIN = 26,
+  NUM_BARS = 27
 };
 
 // Offset of bf16 element (row, col) in a K-major, 128B-swizzled tile made of
@@ -129,18 +132,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar[B_QKV_FULL + i], 1);
       mbar_init(&bar[B_QKV_EMPTY + i], 1);
+      mbar_init(&bar[B_G_FULL + i], 1);
+      mbar_init(&bar[B_G_EMPTY + i], 4);
       mbar_init(&bar[B_PREP + i], 4);
       mbar_init(&bar[B_DEC_FULL + i], 4);
       mbar_init(&bar[B_DEC_EMPTY + i], 8);
+      mbar_init(&bar[B_A_FULL + i], 1);
+      mbar_init(&bar[B_A_EMPTY + i], 8);
       mbar_init(&bar[B_S_FULL + i], 1);
       mbar_init(&bar[B_S_EMPTY + i], 8);
-      mbar_init(&bar[B_H_FULL + i], 8);
     }
-    mbar_init(&bar[B_G_FULL], 1);
-    mbar_init(&bar[B_G_EMPTY], 4);
-    mbar_init(&bar[B_A_FULL], 1);
-    mbar_init(&bar[B_A_EMPTY], 4);
-    mbar_init(&bar[B_P_FULL], 4);
+    mbar_init(&bar[B_P_FULL], 8);
+    mbar_init(&bar[B_H_FULL], 8);
     mbar_init(&bar[B_O_FULL], 1);
     mbar_init(&bar[B_O_EMPTY], 8);
     mbar_init(&bar[B_DRAIN], 1);
@@ -157,13 +160,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t s_base = smem_u32(smem);
 
   if (warp == 0) {
-    // ----------------------------------------------------------------- TMA
+    // ------------------------------------------------------- TMA q, k, v
     if (lane == 0) {
-      bool ok = true;
-      for (int n = 0; n < NT && ok; ++n) {
+      for (int n = 0; n < NT; ++n) {
         const int s = n & 1;
         const int tok = tok0 + n * C;
-        if (!mbar_wait(&bar[B_QKV_EMPTY + s], ((n >> 1) & 1) ^ 1, ab)) { ok = false; break; }
+        if (!mbar_wait(&bar[B_QKV_EMPTY + s], ((n >> 1) & 1) ^ 1, ab)) break;
         mbar_arrive_expect_tx(&bar[B_QKV_FULL + s], 2 * CF::Q_BYTES + CF::V_BYTES);
         uint8_t* qd = smem + CF::OFF_Q + s * CF::Q_BYTES;
         uint8_t* kd = smem + CF::OFF_K + s * CF::Q_BYTES;
@@ -175,51 +177,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int j = 0; j < CF::V_BOXES; ++j)
           tma_load_3d(vd + j * 8192, &tm_v, &bar[B_QKV_FULL + s], v0 + 64 * j, h, tok);
-        if (p.has_g) {
-          if (!mbar_wait(&bar[B_G_EMPTY], (n & 1) ^ 1, ab)) { ok = false; break; }
-          mbar_arrive_expect_tx(&bar[B_G_FULL], CF::G_BYTES);
-          tma_load_3d(smem + CF::OFF_G, &tm_g, &bar[B_G_FULL], 0, h, tok);
-        }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
     if (lane == 0) {
-      bool ok = true;
       const uint32_t p_addr = s_base + CF::OFF_P;
-      for (int n = 0; n < NT && ok; ++n) {
-        const int s = n & 1;
-        const uint32_t ph2 = (n >> 1) & 1;
+      const uint32_t h_addr = s_base + CF::OFF_H;
+      // A_m = Qs Kg^T (M=64 query rows, N=64 key rows, K=128 features) into
+      // TMEM buffer m%2; S_m = Kg^T V (M=128 features, N=VS, K=64 tokens).
+      // A_m = Qs Kg^T (M=64 query rows, N=64 key rows, K=128 features) into
+      // TMEM buffer m%2; S_m = Kg^T V (M=128 features, N=VS, K=64 tokens).
+      auto issue_a_s = [&](int m) {
+        const int s = m & 1;
         const uint32_t q_addr = s_base + CF::OFF_Q + s * CF::Q_BYTES;
         const uint32_t k_addr = s_base + CF::OFF_K + s * CF::Q_BYTES;
         const uint32_t v_addr = s_base + CF::OFF_V + s * CF::V_BYTES;
-        const uint32_t h_addr = s_base + CF::OFF_H + s * CF::H_BYTES;
-        if (!mbar_wait(&bar[B_PREP + s], ph2, ab)) { ok = false; break; }
-        if (!mbar_wait(&bar[B_A_EMPTY], (n & 1) ^ 1, ab)) { ok = false; break; }
-        tc_fence_after();
-        // A = Qs Kg^T: M=64 (query rows), N=64 (key rows), K=128 features.
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t koff = (kk >> 2) * 8192 + (kk & 3) * 32;
-          mma_f16(tmem + CF::COL_A, sdesc(q_addr + koff, 16, 1024, kSwizzle128B),
+          mma_f16(tmem + CF::COL_A + s * 64, sdesc(q_addr + koff, 16, 1024, kSwizzle128B),
                   sdesc(k_addr + koff, 16, 1024, kSwizzle128B), CF::IDESC_A, kk > 0);
         }
-        tc_commit(&bar[B_A_FULL]);
-        // S = Kg^T V: M=128 features (MN-major A), N=VS (MN-major B), K=64 tokens.
-        if (!mbar_wait(&bar[B_S_EMPTY + s], ph2 ^ 1, ab)) { ok = false; break; }
-        tc_fence_after();
+        tc_commit(&bar[B_A_FULL + s]);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           mma_f16(tmem + CF::COL_S + s * VS, sdesc(k_addr + kk * 2048, 8192, 1024, kSwizzle128B),
                   sdesc(v_addr + kk * 2048, 8192, 1024, kSwizzle128B), CF::IDESC_S, kk > 0);
         }
         tc_commit(&bar[B_S_FULL + s]);
-        // O = Qs H_n + P V: M=64, N=VS.
-        if (!mbar_wait(&bar[B_P_FULL], n & 1, ab)) { ok = false; break; }
-        if (!mbar_wait(&bar[B_H_FULL + s], ph2, ab)) { ok = false; break; }
-        if (!mbar_wait(&bar[B_O_EMPTY], (n & 1) ^ 1, ab)) { ok = false; break; }
-        tc_fence_after();
+      };
+      // O_n = Qs H_n + P V (M=64, N=VS, K=128+64); frees the q/k/v stage.
+      auto issue_o = [&](int n) {
+        const int s = n & 1;
+        const uint32_t q_addr = s_base + CF::OFF_Q + s * CF::Q_BYTES;
+        const uint32_t v_addr = s_base + CF::OFF_V + s * CF::V_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t koff = (kk >> 2) * 8192 + (kk & 3) * 32;
@@ -233,89 +226,138 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_commit(&bar[B_O_FULL]);
         tc_commit(&bar[B_QKV_EMPTY + s]);
+      };
+      // Dataflow issue: A/S of chunk na (needs its gating) may run one chunk
+      // ahead of O of chunk no (needs P_no and H_no); O has priority.
+      int na = 0, no = 0;
+      uint64_t t0 = global_ns();
+      uint32_t spins = 0;
+      while (no < NT) {
+        bool progressed = false;
+        if (no < na && mbar_try_wait(&bar[B_P_FULL], no & 1) &&
+            mbar_try_wait(&bar[B_H_FULL], no & 1) &&
+            mbar_try_wait(&bar[B_O_EMPTY], (no & 1) ^ 1)) {
+          tc_fence_after();
+          issue_o(no);
+          ++no;
+          progressed = true;
+        }
+        if (na < NT && na <= no + 1) {
+          const int s = na & 1;
+          const uint32_t ph2 = (na >> 1) & 1;
+          if (mbar_try_wait(&bar[B_PREP + s], ph2) && mbar_try_wait(&bar[B_A_EMPTY + s], ph2 ^ 1) &&
+              mbar_try_wait(&bar[B_S_EMPTY + s], ph2 ^ 1)) {
+            tc_fence_after();
+            issue_a_s(na);
+            ++na;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          t0 = global_ns();
+          spins = 0;
+        } else if ((++spins & 255u) == 0) {
+          if (*abort_flag) break;
+          if (global_ns() - t0 > kWaitNs) {
+            *abort_flag = 1;
+            atomicExch(p.err, GL_DEV_WAIT_TIMEOUT);
+            break;
+          }
+        }
       }
       tc_commit(&bar[B_DRAIN]);
-      const uint64_t t0 = global_ns();
-      while (!mbar_try_wait(&bar[B_DRAIN], 0) && global_ns() - t0 < 100000000ull) {
+      const uint64_t td = global_ns();
+      while (!mbar_try_wait(&bar[B_DRAIN], 0) && global_ns() - td < 100000000ull) {
+      }
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ----------------------------------------------------------- TMA g
+    if (lane == 0 && p.has_g) {
+      for (int n = 0; n < NT; ++n) {
+        const int s = n & 1;
+        if (!mbar_wait(&bar[B_G_EMPTY + s], ((n >> 1) & 1) ^ 1, ab)) break;
+        mbar_arrive_expect_tx(&bar[B_G_FULL + s], CF::G_BYTES);
+        tma_load_3d(smem + CF::OFF_G + s * CF::G_BYTES, &tm_g, &bar[B_G_FULL + s], 0, h,
+                    tok0 + n * C);
       }
     }
     __syncwarp();
   } else if (warp >= 4 && warp < 8) {
-    // ------------------------------------------------ gating + P epilogue
-    const int key = (warp - 4) * 32 + lane;             // gating: thread = feature
-    const int quad = warp & 3;                          // TMEM lane quadrant
-    const int prow = quad * 16 + lane;                  // P row (valid for lane < 16)
-    const float* gsm = reinterpret_cast<const float*>(smem + CF::OFF_G);
+    // ---------------------------------------------------------- gating
+    // thread = (key pair kp, token half hf): keys 2kp, 2kp+1, tokens
+    // 32hf .. 32hf+31.  Second-half threads first sum the gate over the
+    // first 32 tokens themselves (no cross-thread barrier), then continue the
+    // chunk-local cumsum.
+    const int tid = (warp - 4) * 32 + lane;
+    const int kp = tid & 63, hf = tid >> 6;
     const float gamma = p.has_g ? 0.f : __ldg(p.g_gamma + h);
     const float scale = p.scale;
-    bool ok = true;
-    for (int n = 0; n < NT && ok; ++n) {
+    const uint32_t atom = (kp >> 5) * 8192u, chunk = (kp & 31) >> 2, sub = (kp & 3) * 4u;
+    for (int n = 0; n < NT; ++n) {
       const int s = n & 1;
       const uint32_t ph2 = (n >> 1) & 1;
-      if (!mbar_wait(&bar[B_QKV_FULL + s], ph2, ab)) { ok = false; break; }
-      if (p.has_g && !mbar_wait(&bar[B_G_FULL], n & 1, ab)) { ok = false; break; }
-      if (!mbar_wait(&bar[B_DEC_EMPTY + s], ph2 ^ 1, ab)) { ok = false; break; }
-      uint8_t* qs = smem + CF::OFF_Q + s * CF::Q_BYTES;
-      uint8_t* ks = smem + CF::OFF_K + s * CF::Q_BYTES;
-      float G = 0.f;
+      if (p.has_g && !mbar_wait(&bar[B_G_FULL + s], ph2, ab)) break;
+      if (!mbar_wait(&bar[B_QKV_FULL + s], ph2, ab)) break;
+      if (!mbar_wait(&bar[B_DEC_EMPTY + s], ph2 ^ 1, ab)) break;
+      const float2* gsm = reinterpret_cast<const float2*>(smem + CF::OFF_G + s * CF::G_BYTES) + kp;
+      uint8_t* qs = smem + CF::OFF_Q + s * CF::Q_BYTES + atom + sub;
+      uint8_t* ks = smem + CF::OFF_K + s * CF::Q_BYTES + atom + sub;
+      float G0 = 0.f, G1 = 0.f;
+      if (hf == 1) {
+        if (p.has_g) {
 #pragma unroll 8
-      for (int t = 0; t < C; ++t) {
-        G = p.has_g ? G + gsm[t * KD + key] : gamma * static_cast<float>(t + 1);
-        const float eg = __expf(G), en = __expf(-G);
-        const uint32_t off = kmaj_off(t, key, 8192);
-        __nv_bfloat16* qp = reinterpret_cast<__nv_bfloat16*>(qs + off);
-        __nv_bfloat16* kp = reinterpret_cast<__nv_bfloat16*>(ks + off);
-        *qp = __float2bfloat16_rn(__bfloat162float(*qp) * eg * scale);
-        *kp = __float2bfloat16_rn(__bfloat162float(*kp) * en);
+          for (int t = 0; t < 32; ++t) {
+            const float2 gv = gsm[t * (KD / 2)];
+            G0 += gv.x;
+            G1 += gv.y;
+          }
+        } else {
+          G0 = G1 = gamma * 32.f;
+        }
       }
-      dec[s * KD + key] = __expf(G);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int t = hf * 32 + i;
+        if (p.has_g) {
+          const float2 gv = gsm[t * (KD / 2)];
+          G0 += gv.x;
+          G1 += gv.y;
+        } else {
+          G0 = G1 = gamma * static_cast<float>(t + 1);
+        }
+        const uint32_t off = static_cast<uint32_t>(t) * 128u + ((chunk ^ (t & 7)) << 4);
+        uint32_t* qp = reinterpret_cast<uint32_t*>(qs + off);
+        uint32_t* kq = reinterpret_cast<uint32_t*>(ks + off);
+        const uint32_t qv = *qp, kv = *kq;
+        const float e0 = __expf(G0), e1 = __expf(G1);
+        const float n0 = __expf(-G0), n1 = __expf(-G1);
+        *qp = pack_bf16x2(__uint_as_float(qv << 16) * (e0 * scale),
+                          __uint_as_float(qv & 0xFFFF0000u) * (e1 * scale));
+        *kq = pack_bf16x2(__uint_as_float(kv << 16) * n0, __uint_as_float(kv & 0xFFFF0000u) * n1);
+      }
+      if (hf == 1) {
+        dec[s * KD + 2 * kp] = __expf(G0);
+        dec[s * KD + 2 * kp + 1] = __expf(G1);
+      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        if (p.has_g) mbar_arrive(&bar[B_G_EMPTY]);
+        if (p.has_g) mbar_arrive(&bar[B_G_EMPTY + s]);
         mbar_arrive(&bar[B_PREP + s]);
         mbar_arrive(&bar[B_DEC_FULL + s]);
       }
-      // P = tril(A) in bf16, K-major (row i = query, 128 B per row).
-      if (!mbar_wait(&bar[B_A_FULL], n & 1, ab)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t a[32], a2[32];
-      const uint32_t ta = tmem + (static_cast<uint32_t>(quad * 32) << 16) + CF::COL_A;
-      tmem_ld32(ta, a);
-      tmem_ld32(ta + 32, a2);
-      tmem_ld_wait(a);
-      tmem_ld_wait(a2);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_A_EMPTY]);
-      if (lane < 16) {
-        uint8_t* pp = smem + CF::OFF_P;
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          float f[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int j = c8 * 8 + e;
-            const float x = __uint_as_float(j < 32 ? a[j] : a2[j - 32]);
-            f[e] = j <= prow ? x : 0.f;
-          }
-          const uint4 w = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                                     pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
-          *reinterpret_cast<uint4*>(pp + prow * 128 + ((c8 ^ (prow & 7)) << 4)) = w;
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_P_FULL]);
     }
   } else if (warp >= 8) {
-    // ----------------------------------------- state update + O epilogue
+    // ------------------------- P epilogue, state update, O epilogue
     constexpr int HC = VS / 2;                     // state columns per warpgroup
-    const int wg = (warp - 8) >> 2;                // 0 / 1 -> columns [wg*HC, (wg+1)*HC)
+    const int wg = (warp - 8) >> 2;                // 0 / 1
     const int quad = warp & 3;
     const int key = quad * 32 + lane;              // state row == TMEM lane
+    const int prow = quad * 16 + (lane & 15);      // row of an M=64 accumulator
     const int c0 = wg * HC;
     const int64_t bhi = static_cast<int64_t>(b) * H + h;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     float hreg[HC];
     if (p.h0) {
       const float4* src =
@@ -332,9 +374,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int j = 0; j < HC; ++j) hreg[j] = 0.f;
     }
-    // H tile: MN-major B operand [128 keys][VS], 64-column atoms 16 KB apart.
-    auto store_h = [&](int buf) {
-      uint8_t* hp = smem + CF::OFF_H + buf * CF::H_BYTES;
+    // H: MN-major B operand [128 keys][VS], 64-column atoms 16 KB apart.
+    auto store_h = [&]() {
+      uint8_t* hp = smem + CF::OFF_H;
 #pragma unroll
       for (int c8 = 0; c8 < HC / 8; ++c8) {
         const int col = c0 + c8 * 8;
@@ -346,14 +388,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_H_FULL + buf]);
+      if (lane == 0) mbar_arrive(&bar[B_H_FULL]);
     };
-    store_h(0);
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    bool ok = true;
+    // P = tril(A_m) in bf16, K-major (row = query, 128 B), this warpgroup's
+    // 32 columns.
+    auto p_epilogue = [&](int m) -> bool {
+      const int s = m & 1;
+      if (!mbar_wait(&bar[B_A_FULL + s], (m >> 1) & 1, ab)) return false;
+      tc_fence_after();
+      uint32_t a[32];
+      tmem_ld32(lane_addr + CF::COL_A + s * 64 + wg * 32, a);
+      tmem_ld_wait(a);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_A_EMPTY + s]);
+      if (lane < 16) {
+        uint8_t* pp = smem + CF::OFF_P + prow * 128;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int j = wg * 32 + c4 * 8 + e;
+            f[e] = j <= prow ? __uint_as_float(a[c4 * 8 + e]) : 0.f;
+          }
+          const uint32_t chunk = static_cast<uint32_t>(wg * 4 + c4) ^ (prow & 7);
+          *reinterpret_cast<uint4*>(pp + (chunk << 4)) =
+              make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                         pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_P_FULL]);
+      return true;
+    };
+    store_h();
+    bool ok = p_epilogue(0);
     for (int n = 0; n < NT && ok; ++n) {
       const int s = n & 1;
       const uint32_t ph2 = (n >> 1) & 1;
+      // state update: h <- e^{G_last} (h + S_n)
       if (!mbar_wait(&bar[B_DEC_FULL + s], ph2, ab)) { ok = false; break; }
       const float d = dec[s * KD + key];
       __syncwarp();
@@ -371,11 +446,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_S_EMPTY + s]);
-      if (n + 1 < NT) store_h((n + 1) & 1);
-      // O epilogue: rows 16*quad + lane (lane < 16) of the M=64 accumulator.
+      // O_n done -> H and P may be rewritten for chunk n+1
       if (!mbar_wait(&bar[B_O_FULL], n & 1, ab)) { ok = false; break; }
       tc_fence_after();
-      const int64_t row = static_cast<int64_t>(tok0) + n * C + quad * 16 + (lane & 15);
+      if (n + 1 < NT) store_h();
+      // O epilogue: rows 16*quad + lane (lane < 16) of the M=64 accumulator.
+      const int64_t row = static_cast<int64_t>(tok0) + n * C + prow;
       uint4* dst = reinterpret_cast<uint4*>(p.o + (row * H + h) * 128 + v0 + c0);
 #pragma unroll
       for (int j = 0; j < HC; j += 32) {
@@ -395,6 +471,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_O_EMPTY]);
+      if (n + 1 < NT && !p_epilogue(n + 1)) { ok = false; break; }
     }
     if (ok && p.ht) {
       float4* dst = reinterpret_cast<float4*>(p.ht + (bhi * KD + key) * 128 + v0 + c0);

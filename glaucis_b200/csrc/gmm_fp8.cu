@@ -5,17 +5,23 @@
 // Replaces the tokamax Pallas TPU `gmm` call made by the Glaucis template
 // (KE/examples/kernels/gmm_fp8_blockwise.py:109-119).
 //
-// Design (one persistent CTA per SM, 320 threads, warp specialised):
+// Design (one persistent CTA per SM, 384 threads, warp specialised):
 //   warp 0      TMA producer: per 128-deep K block loads the 128x128 e4m3
 //               activation tile (K-major) and the 128x256 e4m3 weight tile
 //               (N-major, two 128-byte-wide boxes) into a 4-stage ring.
 //   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (128x256x32) per K
 //               block into one of two TMEM accumulators (2 x 256 columns).
-//   warps 2-9   promotion + epilogue: after every K block each thread reads
-//               its row's 128 columns of the partial sum out of TMEM and
-//               accumulates partial * (a_s * b_s) in fp32 registers, releasing
-//               the TMEM buffer so the next K block's MMAs overlap the
-//               promotion.  The finished row is written as bf16 (or fp32).
+//   warp 3      derives the ragged tile table from group_sizes.
+//   warps 4-11  promotion + epilogue (two warpgroups, 128 columns each):
+//               after every K block each thread reads its row's columns of
+//               the partial sum out of TMEM (double-buffered 32-column loads)
+//               and accumulates partial * (a_s * b_s) in fp32 registers with
+//               packed f32x2 FMAs, releasing the TMEM buffer so the next K
+//               block's MMAs overlap the promotion.  The finished row is
+//               written as bf16 (or fp32).
+//   Registers: the control warpgroup drops to 56 per thread and the two
+//   promotion warpgroups rise to 224 (128 x 56 + 256 x 224 = 384 x 168, the
+//   launch allocation).
 // Ragged groups: tiles never straddle a group; M tiles start at each group's
 // row offset, the last tile of a group is partial and its foreign rows are
 // computed but never stored.  The tile list (group-major, N outer, M inner so
@@ -29,7 +35,9 @@ namespace gmm {
 constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
 constexpr int A_BYTES = BM * BK;  // 16 KB
 constexpr int B_BYTES = BK * BN;  // 32 KB
-constexpr int NUM_THREADS = 320;
+constexpr int NUM_THREADS = 384;
+constexpr int REG_CTRL = 56, REG_EPI = 224;
+static_assert(128 * REG_CTRL + 256 * REG_EPI <= NUM_THREADS * 168, "register split exceeds the launch allocation");
 constexpr int MAX_G = 1024;
 constexpr int TMEM_COLS = 512;
 
@@ -115,13 +123,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       for (int i = 0; i < 2; ++i) {
         mbar_init(&tfull[i], 1);
-        mbar_init(&tempty[i], 8);  // one arrival per epilogue warp
+        mbar_init(&tempty[i], 8);  // one arrival per promotion warp
       }
       mbar_init(drain, 1);
       *abort_flag = 0;
       fence_mbar_init();
     }
-  } else if (warp == 2) {
+  } else if (warp == 3) {
     // Group table: exclusive prefix sums of rows and tiles (warp scan).
     const int per = (G + 31) / 32;
     const int g0 = min(G, lane * per), g1 = min(G, g0 + per);
@@ -167,6 +175,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int total = *total_tiles_s;
 
   if (warp == 0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
     if (lane == 0) {
       // ------------------------------------------------------------ producer
       int it = 0;
@@ -199,6 +208,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
     if (lane == 0) {
       // ------------------------------------------------------------ MMA
       int it = 0, acc_it = 0;
@@ -231,9 +241,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     __syncwarp();
+  } else if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_EPI));
     // -------------------------------------------------------- epilogue
-    const int ew = warp - 2;
+    const int ew = warp - 4;
     const int quad = warp & 3;
     const int chalf = ew >> 2;
     const int r = quad * 32 + lane;
@@ -249,9 +262,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int nb = ncol0 >> 7;
       const float* sa_row = p.a_s + grow * KB;
       const float* sb_col = p.b_s + static_cast<int64_t>(tl.g) * KB * NB + nb;
-      float acc[128];
+      float2 acc[64];
 #pragma unroll
-      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      for (int j = 0; j < 64; ++j) acc[j] = make_float2(0.f, 0.f);
       float sa_next = row_ok ? __ldg(sa_row) : 0.f;
       float sb_next = col_ok ? __ldg(sb_col) : 0.f;
       for (int kb = 0; kb < KB; ++kb, ++acc_it) {
@@ -260,23 +273,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           sa_next = row_ok ? __ldg(sa_row + kb + 1) : 0.f;
           sb_next = col_ok ? __ldg(sb_col + static_cast<int64_t>(kb + 1) * NB) : 0.f;
         }
+        const float2 sc2 = make_float2(sc, sc);
         const int buf = acc_it & 1;
         if (!mbar_wait(&tfull[buf], (acc_it >> 1) & 1, ab)) { ok = false; break; }
         tc_fence_after();
         const uint32_t ta = lane_base + buf * BN;
+        uint32_t va[32], vb[32];
+        auto promote = [&](const uint32_t (&v)[32], int base) {
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          uint32_t v[32];
-          tmem_ld32(ta + h * 32, v);
-          tmem_ld_wait(v);
-          if (h == 3) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[buf]);
-          }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[h * 32 + j] = fmaf(__uint_as_float(v[j]), sc, acc[h * 32 + j]);
-        }
+          for (int j = 0; j < 16; ++j)
+            acc[base + j] = __ffma2_rn(make_float2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])),
+                                       sc2, acc[base + j]);
+        };
+        tmem_ld32(ta, va);
+        tmem_ld_wait(va);
+        tmem_ld32(ta + 32, vb);
+        promote(va, 0);
+        tmem_ld_wait(vb);
+        tmem_ld32(ta + 64, va);
+        promote(vb, 16);
+        tmem_ld_wait(va);
+        tmem_ld32(ta + 96, vb);
+        promote(va, 32);
+        tmem_ld_wait(vb);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        promote(vb, 48);
       }
       if (!ok) break;
       if (row_ok && col_ok) {
@@ -284,15 +307,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + grow * N + ncol0);
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+            dst[i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
         } else {
           uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + grow * N + ncol0);
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            dst[i] = make_uint4(pack_bf16x2(acc[8 * i], acc[8 * i + 1]),
-                                pack_bf16x2(acc[8 * i + 2], acc[8 * i + 3]),
-                                pack_bf16x2(acc[8 * i + 4], acc[8 * i + 5]),
-                                pack_bf16x2(acc[8 * i + 6], acc[8 * i + 7]));
+            dst[i] = make_uint4(pack_bf16x2(acc[4 * i].x, acc[4 * i].y),
+                                pack_bf16x2(acc[4 * i + 1].x, acc[4 * i + 1].y),
+                                pack_bf16x2(acc[4 * i + 2].x, acc[4 * i + 2].y),
+                                pack_bf16x2(acc[4 * i + 3].x, acc[4 * i + 3].y));
         }
       }
     }

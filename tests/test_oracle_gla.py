@@ -70,3 +70,15 @@ def test_golden_fixture_reproduces():
 def test_flop_and_byte_model():
     assert O.gla_flops(8, 4096, 16) == pytest.approx(51.54e9, rel=1e-3)
     assert O.gla_bytes(8, 4096, 16) == pytest.approx(0.814e9, rel=2e-2)
+
+
+@pytest.mark.parametrize("gate", ["per_key", "gamma"])
+def test_torch_cpu_restatement_matches_oracle(gate):
+    import torch
+    from oracle import cpu_fast
+    q, k, v, g, gg, hh = _inputs(2, 192, 3, seed=6, gate=gate, h0=True)
+    t = lambda a: None if a is None else torch.from_numpy(a)
+    o, ht = cpu_fast.chunk_gla_fwd(t(q), t(k), t(v), g=t(g), g_gamma=t(gg), h0=t(hh))
+    ro, rht = O.chunk_gla_fwd(q, k, v, g=g, g_gamma=gg, h0=hh)
+    assert_close(o.numpy(), ro, rtol=1e-3, atol_frac=1e-5, what="o")
+    assert_close(ht.numpy(), rht, rtol=1e-3, atol_frac=1e-5, what="ht")

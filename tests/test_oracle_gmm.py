@@ -107,3 +107,20 @@ def test_group_size_generators(routing):
         assert (s == 0).sum() >= 1
     if routing == "zipf_topk":
         assert s.max() <= 4096 and (s == 0).sum() >= 1
+
+
+def test_torch_cpu_restatement_matches_oracle():
+    # The BLAS-backed CPU baseline quantises bit-identically and agrees with
+    # the per-K-block promotion oracle up to fp32 summation order.
+    from oracle import cpu_fast
+    cfg = configs.GMMConfig("t", G=3, M=400, K=384, N=256, routing="uniform_one_empty")
+    lhs, rhs, gs = configs.make_gmm_inputs(cfg, device="cpu", seed=11)
+    q, s = cpu_fast.quant_act_1x128(lhs)
+    rq, rs = O.quant_act_1x128(lhs.float().numpy())
+    assert np.array_equal(q.view(torch.uint8).numpy(), rq) and np.array_equal(s.numpy(), rs)
+    q, s = cpu_fast.quant_w_128x128(rhs)
+    rq, rs = O.quant_w_128x128(rhs.float().numpy())
+    assert np.array_equal(q.view(torch.uint8).numpy(), rq) and np.array_equal(s.numpy(), rs)
+    got = cpu_fast.gmm_fp8_blockwise(lhs, rhs, gs.tolist()).numpy()
+    ref = O.gmm_fp8_blockwise(lhs.float().numpy(), rhs.float().numpy(), gs.numpy())
+    assert_close(got, ref, rtol=1e-4, atol_frac=1e-5, what="cpu_fast gmm")
