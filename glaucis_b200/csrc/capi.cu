@@ -105,6 +105,10 @@ uint32_t elem_bytes(CUtensorMapDataType dt) {
 
 }  // namespace
 
+// Records `msg` as this thread's last error and returns `code` (shared with
+// the other entry-point files).
+int gl_set_error_message(int code, const char* msg) { return fail(code, msg); }
+
 bool gl_make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, int64_t inner,
                      int64_t outer, int64_t row_stride_elems, uint32_t box_inner,
                      uint32_t box_outer, CUtensorMapSwizzle sw, const char** why) {

@@ -121,6 +121,34 @@ int gl_chunk_gla_fwd(const void* q, const void* k, const void* v, const float* g
                      int64_t chunk_size, void* o, float* ht, int* err_word,
                      void* stream);
 
+/* Largest M*K accepted by gl_gmm_fp8_act_fwd_noalloc (activation elements). */
+#define GL_NOALLOC_MAX_ACT_ELEMS (16u * 1024u * 1024u)
+
+/*
+ * Grouped matmul forward from bf16 activations that allocates no device
+ * memory.  No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory during a step (runtimes that plan every
+ * buffer up front and forbid allocation while executing, FFI callers
+ * without a device allocator).  It quantises lhs (1x128, as
+ * gl_quant_act_1x128) into a fixed device scratch array owned by the
+ * library (16 MiB of e4m3 plus 512 KiB of scales, created when the
+ * library's device code loads on a GPU and held until exit) and runs
+ * gl_gmm_fp8_fwd on it.
+ *   lhs bf16 [M, K] with M * K <= GL_NOALLOC_MAX_ACT_ELEMS (else GL_EINVAL);
+ *   b_q, b_s, group_sizes, out, out_dtype as gl_gmm_fp8_fwd.
+ *   err_word: optional caller-owned device int for device-side error codes;
+ *   with NULL they go to the scratch array's own word, which every call
+ *   clears first and which is not reported back.
+ * All calls on a device share the scratch array and it keeps the last
+ * call's contents; calls whose GPU work overlaps race on it.  The first call
+ * on each device looks up the array's device address; make it before any
+ * stream capture.
+ */
+int gl_gmm_fp8_act_fwd_noalloc(const void* lhs, const void* b_q, const float* b_s,
+                               const int32_t* group_sizes, int64_t G, int64_t M,
+                               int64_t K, int64_t N, void* out, int out_dtype,
+                               int* err_word, void* stream);
+
 /*
  * Synchronises `stream`, reads the device error word (the library word when
  * err_word is NULL) into *code and clears it.  Returns GL_OK or GL_ELAUNCH.
