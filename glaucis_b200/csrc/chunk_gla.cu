@@ -20,7 +20,7 @@
 // One CTA per (batch, head, V slice of width VS), 512 threads:
 //   warp 0        TMA producer (g chunk, then q, k, v chunk; 2-stage rings)
 //   warp 1        tcgen05.mma issuer, one chunk ahead: A_{n+1}, S_{n+1}, O_n
-//   warp 2        TMEM allocator
+//   warp 2        TMEM allocator, then TMA producer of g
 //   warps 4-7     gating (thread = key): Qs, Kg in place, e^{G_last}
 //   warps 8-15    two warpgroups, each owning VS/2 state columns and 32 of
 //                 the 64 P columns: A -> tril -> bf16 P, state update
@@ -33,6 +33,11 @@ namespace gl {
 namespace gla {
 
 constexpr int C = 64, KD = 128, NUM_THREADS = 512;
+// Register split (launch: 512 x 128): control warpgroup 56, gating 168,
+// the two state warpgroups keep 128.
+constexpr int REG_CTRL = 56, REG_GATE = 200;
+static_assert(128 * REG_CTRL + 128 * REG_GATE + 256 * 128 <= NUM_THREADS * 128,
+              "register split exceeds the launch allocation");
 
 template <int VS>
 struct Cfg {
@@ -107,8 +112,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                          const __grid_constant__ CUtensorMap tm_g, const Params p) {
   using CF = Cfg<VS>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  // 1 KB-aligned base derived by pointer arithmetic on the shared array so
+  // that every access below stays in the shared address space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + CF::OFF_BAR);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + CF::OFF_MISC);
   int* abort_flag = reinterpret_cast<int*>(smem + CF::OFF_MISC + 4);
@@ -160,6 +166,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t s_base = smem_u32(smem);
 
   if (warp == 0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
     // ------------------------------------------------------- TMA q, k, v
     if (lane == 0) {
       for (int n = 0; n < NT; ++n) {
@@ -181,6 +188,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
     // ----------------------------------------------------------------- MMA
     if (lane == 0) {
       const uint32_t p_addr = s_base + CF::OFF_P;
@@ -272,6 +280,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
   } else if (warp == 2) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
     // ----------------------------------------------------------- TMA g
     if (lane == 0 && p.has_g) {
       for (int n = 0; n < NT; ++n) {
@@ -283,7 +292,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     __syncwarp();
+  } else if (warp == 3) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
   } else if (warp >= 4 && warp < 8) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_GATE));
     // ---------------------------------------------------------- gating
     // thread = (key pair kp, token half hf): keys 2kp, 2kp+1, tokens
     // 32hf .. 32hf+31.  Second-half threads first sum the gate over the
@@ -316,25 +328,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           G0 = G1 = gamma * 32.f;
         }
       }
+      // 32 tokens in 4 batches of 8; the next batch's loads are issued
+      // before the current batch is computed and stored.
+      float2 gv[2][8];
+      uint32_t qv[2][8], kv[2][8];
+      auto load_batch = [&](int bt, int slot) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int t = hf * 32 + i;
-        if (p.has_g) {
-          const float2 gv = gsm[t * (KD / 2)];
-          G0 += gv.x;
-          G1 += gv.y;
-        } else {
-          G0 = G1 = gamma * static_cast<float>(t + 1);
+        for (int j = 0; j < 8; ++j) {
+          const int t = hf * 32 + bt * 8 + j;
+          const uint32_t off = static_cast<uint32_t>(t) * 128u + ((chunk ^ j) << 4);
+          gv[slot][j] = p.has_g ? gsm[t * (KD / 2)] : make_float2(0.f, 0.f);
+          qv[slot][j] = *reinterpret_cast<const uint32_t*>(qs + off);
+          kv[slot][j] = *reinterpret_cast<const uint32_t*>(ks + off);
         }
-        const uint32_t off = static_cast<uint32_t>(t) * 128u + ((chunk ^ (t & 7)) << 4);
-        uint32_t* qp = reinterpret_cast<uint32_t*>(qs + off);
-        uint32_t* kq = reinterpret_cast<uint32_t*>(ks + off);
-        const uint32_t qv = *qp, kv = *kq;
-        const float e0 = __expf(G0), e1 = __expf(G1);
-        const float n0 = __expf(-G0), n1 = __expf(-G1);
-        *qp = pack_bf16x2(__uint_as_float(qv << 16) * (e0 * scale),
-                          __uint_as_float(qv & 0xFFFF0000u) * (e1 * scale));
-        *kq = pack_bf16x2(__uint_as_float(kv << 16) * n0, __uint_as_float(kv & 0xFFFF0000u) * n1);
+      };
+      load_batch(0, 0);
+#pragma unroll
+      for (int bt = 0; bt < 4; ++bt) {
+        const int cur = bt & 1;
+        if (bt + 1 < 4) load_batch(bt + 1, cur ^ 1);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int t = hf * 32 + bt * 8 + j;
+          if (p.has_g) {
+            G0 += gv[cur][j].x;
+            G1 += gv[cur][j].y;
+          } else {
+            G0 = G1 = gamma * static_cast<float>(t + 1);
+          }
+          const float e0 = __expf(G0), e1 = __expf(G1);
+          const float n0 = __expf(-G0), n1 = __expf(-G1);
+          const uint32_t off = static_cast<uint32_t>(t) * 128u + ((chunk ^ j) << 4);
+          const uint32_t q2 = qv[cur][j], k2 = kv[cur][j];
+          *reinterpret_cast<uint32_t*>(qs + off) =
+              pack_bf16x2(__uint_as_float(q2 << 16) * (e0 * scale),
+                          __uint_as_float(q2 & 0xFFFF0000u) * (e1 * scale));
+          *reinterpret_cast<uint32_t*>(ks + off) =
+              pack_bf16x2(__uint_as_float(k2 << 16) * n0, __uint_as_float(k2 & 0xFFFF0000u) * n1);
+        }
       }
       if (hf == 1) {
         dec[s * KD + 2 * kp] = __expf(G0);
