@@ -19,24 +19,29 @@
 //
 // One CTA per (batch, head, V slice of width VS), 512 threads:
 //   warp 0        TMA producer (g chunk, then q, k, v chunk; 2-stage rings)
-//   warp 1        tcgen05.mma issuer, one chunk ahead: A_{n+1}, S_{n+1}, O_n
+//   warp 1        tcgen05.mma issuer (dataflow order: A/S of chunk n+1, Qs H_n
+//                 as soon as H_n is stored, P V as soon as P_n is written)
 //   warp 2        TMEM allocator, then TMA producer of g
-//   warps 4-7     gating (thread = key): Qs, Kg in place, e^{G_last}
-//   warps 8-15    two warpgroups, each owning VS/2 state columns and 32 of
-//                 the 64 P columns: A -> tril -> bf16 P, state update
-//                 (thread = key row), the O epilogue
-// Buffers: g, q, k, v double-buffered; A double-buffered in TMEM; P and the
-// bf16 state copy H single-buffered (rewritten only after O_n completed).
+//   warps 4-11    gating (thread = 2 keys x 16 tokens): chunk-local cumsum
+//                 of the gate (quarter prefixes exchanged through shared
+//                 memory), Qs, Kg in place, e^{G_last}; then the O epilogue
+//                 of the chunk two behind (TMEM -> bf16 -> HBM)
+//   warps 12-15   state warpgroup: A -> tril -> bf16 P, state update
+//                 (thread = key row, VS fp32 columns in registers)
+// Buffers: g, q, k, v double-buffered; A and O double-buffered in TMEM, S
+// single; P and the bf16 state copy H single-buffered (rewritten only after
+// O_n completed).
 #include "common.cuh"
 
 namespace gl {
 namespace gla {
 
 constexpr int C = 64, KD = 128, NUM_THREADS = 512;
-// Register split (launch: 512 x 128): control warpgroup 56, gating 168,
-// the two state warpgroups keep 128.
-constexpr int REG_CTRL = 56, REG_GATE = 200;
-static_assert(128 * REG_CTRL + 128 * REG_GATE + 256 * 128 <= NUM_THREADS * 128,
+constexpr int GATE_WARPS = 8, STATE_WARPS = 4;
+// Register split (launch: 512 x 128): control warpgroup 56, the two gating
+// warpgroups keep 128, the state warpgroup rises to 216.
+constexpr int REG_CTRL = 40, REG_STATE = 216;
+static_assert(128 * REG_CTRL + 256 * 128 + 128 * REG_STATE <= NUM_THREADS * 128,
               "register split exceeds the launch allocation");
 
 template <int VS>
@@ -54,11 +59,12 @@ struct Cfg {
   static constexpr uint32_t OFF_P = OFF_G + 2 * G_BYTES;
   static constexpr uint32_t OFF_H = OFF_P + P_BYTES;
   static constexpr uint32_t OFF_DEC = OFF_H + H_BYTES;      // 2 x 128 floats
-  static constexpr uint32_t OFF_BAR = OFF_DEC + 2 * KD * 4;
+  static constexpr uint32_t OFF_PART = OFF_DEC + 2 * KD * 4;  // [2][4][64] float2
+  static constexpr uint32_t OFF_BAR = OFF_PART + 2 * 4 * 64 * 8;
   static constexpr uint32_t OFF_MISC = OFF_BAR + 256;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;
-  // TMEM columns: A0, A1 [0,128), O [128,128+VS), S0, S1
-  static constexpr uint32_t COL_A = 0, COL_O = 128, COL_S = 128 + VS;
+  // TMEM columns: A0, A1 [0,128), O0, O1 [128,128+2VS), S [128+2VS, 128+3VS)
+  static constexpr uint32_t COL_A = 0, COL_O = 128, COL_S = 128 + 2 * VS;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t IDESC_A = idesc(1, 1, 1, 0, 0, 64, 64);    // bf16, K-major x K-major
   static constexpr uint32_t IDESC_S = idesc(1, 1, 1, 1, 1, 128, VS);  // MN-major x MN-major
@@ -81,20 +87,21 @@ enum {
   B_QKV_FULL = 0,    // [2] TMA -> gating
   B_QKV_EMPTY = 2,   // [2] O_n committed -> TMA
   B_G_FULL = 4,      // [2] TMA -> gating
-  B_G_EMPTY = 6,     // [2] gating -> TMA (4 warps)
-  B_PREP = 8,        // [2] gating -> MMA (4 warps)
-  B_DEC_FULL = 10,   // [2] gating -> state (4 warps)
-  B_DEC_EMPTY = 12,  // [2] state -> gating (8 warps)
+  B_G_EMPTY = 6,     // [2] gating -> TMA
+  B_PREP = 8,        // [2] gating -> MMA
+  B_DEC_FULL = 10,   // [2] gating -> state
+  B_DEC_EMPTY = 12,  // [2] state -> gating
   B_A_FULL = 14,     // [2] MMA A_n committed -> P epilogue
-  B_A_EMPTY = 16,    // [2] P epilogue -> MMA (8 warps)
-  B_S_FULL = 18,     // [2] MMA S_n committed -> state
-  B_S_EMPTY = 20,    // [2] state -> MMA (8 warps)
-  B_P_FULL = 22,     // P written -> MMA (8 warps)
-  B_H_FULL = 23,     // H_n written -> MMA (8 warps)
-  B_O_FULL = 24,     // MMA O_n committed -> state
-  B_O_EMPTY = 25,    // O read -> MMA (8 warps)
+  B_A_EMPTY = 16,    // [2] P epilogue -> MMA
+  B_O_FULL = 18,     // [2] MMA O_n committed -> state
+  B_O_EMPTY = 20,    // [2] O read (gating warps) -> MMA
+  B_S_FULL = 22,     // MMA S_n committed -> state
+  B_S_EMPTY = 23,    // state read S -> MMA
+  B_P_FULL = 24,     // P written -> MMA
+  B_H_FULL = 25,     // H_n written -> MMA
   B_DRAIN = 26,
-  NUM_BARS = 27
+  B_GSYNC = 27,      // [2] gating quarter sums written
+  NUM_BARS = 29
 };
 
 // Offset of bf16 element (row, col) in a K-major, 128B-swizzled tile made of
@@ -139,19 +146,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&bar[B_QKV_FULL + i], 1);
       mbar_init(&bar[B_QKV_EMPTY + i], 1);
       mbar_init(&bar[B_G_FULL + i], 1);
-      mbar_init(&bar[B_G_EMPTY + i], 4);
-      mbar_init(&bar[B_PREP + i], 4);
-      mbar_init(&bar[B_DEC_FULL + i], 4);
-      mbar_init(&bar[B_DEC_EMPTY + i], 8);
+      mbar_init(&bar[B_G_EMPTY + i], GATE_WARPS);
+      mbar_init(&bar[B_PREP + i], GATE_WARPS);
+      mbar_init(&bar[B_DEC_FULL + i], GATE_WARPS);
+      mbar_init(&bar[B_GSYNC + i], GATE_WARPS);
+      mbar_init(&bar[B_DEC_EMPTY + i], STATE_WARPS);
       mbar_init(&bar[B_A_FULL + i], 1);
-      mbar_init(&bar[B_A_EMPTY + i], 8);
-      mbar_init(&bar[B_S_FULL + i], 1);
-      mbar_init(&bar[B_S_EMPTY + i], 8);
+      mbar_init(&bar[B_A_EMPTY + i], STATE_WARPS);
+      mbar_init(&bar[B_O_FULL + i], 1);
+      mbar_init(&bar[B_O_EMPTY + i], GATE_WARPS);
     }
-    mbar_init(&bar[B_P_FULL], 8);
-    mbar_init(&bar[B_H_FULL], 8);
-    mbar_init(&bar[B_O_FULL], 1);
-    mbar_init(&bar[B_O_EMPTY], 8);
+    mbar_init(&bar[B_S_FULL], 1);
+    mbar_init(&bar[B_S_EMPTY], STATE_WARPS);
+    mbar_init(&bar[B_P_FULL], STATE_WARPS);
+    mbar_init(&bar[B_H_FULL], STATE_WARPS);
     mbar_init(&bar[B_DRAIN], 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -195,8 +203,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t h_addr = s_base + CF::OFF_H;
       // A_m = Qs Kg^T (M=64 query rows, N=64 key rows, K=128 features) into
       // TMEM buffer m%2; S_m = Kg^T V (M=128 features, N=VS, K=64 tokens).
-      // A_m = Qs Kg^T (M=64 query rows, N=64 key rows, K=128 features) into
-      // TMEM buffer m%2; S_m = Kg^T V (M=128 features, N=VS, K=64 tokens).
       auto issue_a_s = [&](int m) {
         const int s = m & 1;
         const uint32_t q_addr = s_base + CF::OFF_Q + s * CF::Q_BYTES;
@@ -211,50 +217,60 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_commit(&bar[B_A_FULL + s]);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          mma_f16(tmem + CF::COL_S + s * VS, sdesc(k_addr + kk * 2048, 8192, 1024, kSwizzle128B),
+          mma_f16(tmem + CF::COL_S, sdesc(k_addr + kk * 2048, 8192, 1024, kSwizzle128B),
                   sdesc(v_addr + kk * 2048, 8192, 1024, kSwizzle128B), CF::IDESC_S, kk > 0);
         }
-        tc_commit(&bar[B_S_FULL + s]);
+        tc_commit(&bar[B_S_FULL]);
       };
-      // O_n = Qs H_n + P V (M=64, N=VS, K=128+64); frees the q/k/v stage.
-      auto issue_o = [&](int n) {
+      // O_n (TMEM buffer n%2) = Qs H_n (issued once H_n is stored) + P V
+      // (issued once P_n is written); the second part frees the q/k/v stage.
+      auto issue_o_h = [&](int n) {
         const int s = n & 1;
         const uint32_t q_addr = s_base + CF::OFF_Q + s * CF::Q_BYTES;
-        const uint32_t v_addr = s_base + CF::OFF_V + s * CF::V_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t koff = (kk >> 2) * 8192 + (kk & 3) * 32;
-          mma_f16(tmem + CF::COL_O, sdesc(q_addr + koff, 16, 1024, kSwizzle128B),
+          mma_f16(tmem + CF::COL_O + s * VS, sdesc(q_addr + koff, 16, 1024, kSwizzle128B),
                   sdesc(h_addr + kk * 2048, 16384, 1024, kSwizzle128B), CF::IDESC_O, kk > 0);
         }
+      };
+      auto issue_o_p = [&](int n) {
+        const int s = n & 1;
+        const uint32_t v_addr = s_base + CF::OFF_V + s * CF::V_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          mma_f16(tmem + CF::COL_O, sdesc(p_addr + kk * 32, 16, 1024, kSwizzle128B),
+          mma_f16(tmem + CF::COL_O + s * VS, sdesc(p_addr + kk * 32, 16, 1024, kSwizzle128B),
                   sdesc(v_addr + kk * 2048, 8192, 1024, kSwizzle128B), CF::IDESC_O, 1);
         }
-        tc_commit(&bar[B_O_FULL]);
+        tc_commit(&bar[B_O_FULL + s]);
         tc_commit(&bar[B_QKV_EMPTY + s]);
       };
-      // Dataflow issue: A/S of chunk na (needs its gating) may run one chunk
-      // ahead of O of chunk no (needs P_no and H_no); O has priority.
-      int na = 0, no = 0;
+      // Dataflow issue.  na: next chunk for A/S (needs its gating, its A
+      // buffer free and the previous S read); nh: next chunk for Qs H (needs
+      // H_nh and its O buffer drained); no: next chunk for P V (needs P_no).
+      int na = 0, nh = 0, no = 0;
       uint64_t t0 = global_ns();
       uint32_t spins = 0;
       while (no < NT) {
         bool progressed = false;
-        if (no < na && mbar_try_wait(&bar[B_P_FULL], no & 1) &&
-            mbar_try_wait(&bar[B_H_FULL], no & 1) &&
-            mbar_try_wait(&bar[B_O_EMPTY], (no & 1) ^ 1)) {
+        if (no < nh && mbar_try_wait(&bar[B_P_FULL], no & 1)) {
           tc_fence_after();
-          issue_o(no);
+          issue_o_p(no);
           ++no;
+          progressed = true;
+        }
+        if (nh < na && nh == no && mbar_try_wait(&bar[B_H_FULL], nh & 1) &&
+            mbar_try_wait(&bar[B_O_EMPTY + (nh & 1)], ((nh >> 1) & 1) ^ 1)) {
+          tc_fence_after();
+          issue_o_h(nh);
+          ++nh;
           progressed = true;
         }
         if (na < NT && na <= no + 1) {
           const int s = na & 1;
           const uint32_t ph2 = (na >> 1) & 1;
           if (mbar_try_wait(&bar[B_PREP + s], ph2) && mbar_try_wait(&bar[B_A_EMPTY + s], ph2 ^ 1) &&
-              mbar_try_wait(&bar[B_S_EMPTY + s], ph2 ^ 1)) {
+              mbar_try_wait(&bar[B_S_EMPTY], (na & 1) ^ 1)) {
             tc_fence_after();
             issue_a_s(na);
             ++na;
@@ -294,49 +310,91 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
   } else if (warp == 3) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
-  } else if (warp >= 4 && warp < 8) {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_GATE));
+  } else if (warp >= 4 && warp < 4 + GATE_WARPS) {
     // ---------------------------------------------------------- gating
-    // thread = (key pair kp, token half hf): keys 2kp, 2kp+1, tokens
-    // 32hf .. 32hf+31.  Second-half threads first sum the gate over the
-    // first 32 tokens themselves (no cross-thread barrier), then continue the
-    // chunk-local cumsum.
-    const int tid = (warp - 4) * 32 + lane;
-    const int kp = tid & 63, hf = tid >> 6;
+    // thread = (key pair kp, token quarter tq): keys 2kp, 2kp+1, tokens
+    // 16tq .. 16tq+15.  Each thread sums the gate over its 16 tokens, the
+    // quarter sums are exchanged through shared memory, and the chunk-local
+    // cumsum continues from the sum of the preceding quarters.
+    const int gid = threadIdx.x - 128;
+    const int kp = gid & 63, tq = gid >> 6;
     const float gamma = p.has_g ? 0.f : __ldg(p.g_gamma + h);
     const float scale = p.scale;
     const uint32_t atom = (kp >> 5) * 8192u, chunk = (kp & 31) >> 2, sub = (kp & 3) * 4u;
-    for (int n = 0; n < NT; ++n) {
+    // O epilogue of chunk m (run two chunks behind the gating, when O_m is
+    // long complete): this warp reads TMEM lane quadrant warp%4, i.e. rows
+    // 16*quad .. 16*quad+15 of the M=64 accumulator, columns half*VS/2 ..
+    constexpr int OC = VS / 2;
+    const int oquad = warp & 3, ohalf = (warp - 4) >> 2;
+    const int orow = oquad * 16 + (lane & 15);
+    const uint32_t o_lane = tmem + (static_cast<uint32_t>(oquad * 32) << 16) + CF::COL_O + ohalf * OC;
+    auto o_epilogue = [&](int m) -> bool {
+      const int s = m & 1;
+      if (!mbar_wait(&bar[B_O_FULL + s], (m >> 1) & 1, ab)) return false;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(tok0) + m * C + orow;
+      uint4* dst = reinterpret_cast<uint4*>(p.o + (row * H + h) * 128 + v0 + ohalf * OC);
+#pragma unroll
+      for (int j = 0; j < OC; j += 32) {
+        uint32_t ov[32];
+        tmem_ld32(o_lane + s * VS + j, ov);
+        tmem_ld_wait(ov);
+        if (lane < 16) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[j / 8 + i] = make_uint4(
+                pack_bf16x2(__uint_as_float(ov[8 * i]), __uint_as_float(ov[8 * i + 1])),
+                pack_bf16x2(__uint_as_float(ov[8 * i + 2]), __uint_as_float(ov[8 * i + 3])),
+                pack_bf16x2(__uint_as_float(ov[8 * i + 4]), __uint_as_float(ov[8 * i + 5])),
+                pack_bf16x2(__uint_as_float(ov[8 * i + 6]), __uint_as_float(ov[8 * i + 7])));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_O_EMPTY + s]);
+      return true;
+    };
+    bool gok = true;
+    for (int n = 0; n < NT && gok; ++n) {
       const int s = n & 1;
       const uint32_t ph2 = (n >> 1) & 1;
-      if (p.has_g && !mbar_wait(&bar[B_G_FULL + s], ph2, ab)) break;
-      if (!mbar_wait(&bar[B_QKV_FULL + s], ph2, ab)) break;
-      if (!mbar_wait(&bar[B_DEC_EMPTY + s], ph2 ^ 1, ab)) break;
+      if (p.has_g && !mbar_wait(&bar[B_G_FULL + s], ph2, ab)) { gok = false; break; }
+      if (!mbar_wait(&bar[B_QKV_FULL + s], ph2, ab)) { gok = false; break; }
+      if (!mbar_wait(&bar[B_DEC_EMPTY + s], ph2 ^ 1, ab)) { gok = false; break; }
       const float2* gsm = reinterpret_cast<const float2*>(smem + CF::OFF_G + s * CF::G_BYTES) + kp;
       uint8_t* qs = smem + CF::OFF_Q + s * CF::Q_BYTES + atom + sub;
       uint8_t* ks = smem + CF::OFF_K + s * CF::Q_BYTES + atom + sub;
       float G0 = 0.f, G1 = 0.f;
-      if (hf == 1) {
-        if (p.has_g) {
-#pragma unroll 8
-          for (int t = 0; t < 32; ++t) {
-            const float2 gv = gsm[t * (KD / 2)];
-            G0 += gv.x;
-            G1 += gv.y;
-          }
-        } else {
-          G0 = G1 = gamma * 32.f;
+      if (p.has_g) {
+        float2* part = reinterpret_cast<float2*>(smem + CF::OFF_PART) + s * 256;
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 gv = gsm[(tq * 16 + i) * (KD / 2)];
+          a0 += gv.x;
+          a1 += gv.y;
         }
+        part[tq * 64 + kp] = make_float2(a0, a1);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[B_GSYNC + s]);
+        if (!mbar_wait(&bar[B_GSYNC + s], ph2, ab)) { gok = false; break; }
+        for (int q2 = 0; q2 < tq; ++q2) {
+          const float2 pv = part[q2 * 64 + kp];
+          G0 += pv.x;
+          G1 += pv.y;
+        }
+      } else {
+        G0 = G1 = gamma * static_cast<float>(16 * tq);
       }
-      // 32 tokens in 4 batches of 8; the next batch's loads are issued
-      // before the current batch is computed and stored.
-      float2 gv[2][8];
-      uint32_t qv[2][8], kv[2][8];
+      // 16 tokens in 4 batches of 4; each batch's loads are issued one
+      // batch ahead of its arithmetic and stores.
+      float2 gv[2][4];
+      uint32_t qv[2][4], kv[2][4];
       auto load_batch = [&](int bt, int slot) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int t = hf * 32 + bt * 8 + j;
-          const uint32_t off = static_cast<uint32_t>(t) * 128u + ((chunk ^ j) << 4);
+        for (int j = 0; j < 4; ++j) {
+          const int t = tq * 16 + bt * 4 + j;
+          const uint32_t off = static_cast<uint32_t>(t) * 128u + ((chunk ^ (t & 7)) << 4);
           gv[slot][j] = p.has_g ? gsm[t * (KD / 2)] : make_float2(0.f, 0.f);
           qv[slot][j] = *reinterpret_cast<const uint32_t*>(qs + off);
           kv[slot][j] = *reinterpret_cast<const uint32_t*>(ks + off);
@@ -348,8 +406,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int cur = bt & 1;
         if (bt + 1 < 4) load_batch(bt + 1, cur ^ 1);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int t = hf * 32 + bt * 8 + j;
+        for (int j = 0; j < 4; ++j) {
+          const int t = tq * 16 + bt * 4 + j;
           if (p.has_g) {
             G0 += gv[cur][j].x;
             G1 += gv[cur][j].y;
@@ -358,7 +416,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           const float e0 = __expf(G0), e1 = __expf(G1);
           const float n0 = __expf(-G0), n1 = __expf(-G1);
-          const uint32_t off = static_cast<uint32_t>(t) * 128u + ((chunk ^ j) << 4);
+          const uint32_t off = static_cast<uint32_t>(t) * 128u + ((chunk ^ (t & 7)) << 4);
           const uint32_t q2 = qv[cur][j], k2 = kv[cur][j];
           *reinterpret_cast<uint32_t*>(qs + off) =
               pack_bf16x2(__uint_as_float(q2 << 16) * (e0 * scale),
@@ -367,7 +425,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               pack_bf16x2(__uint_as_float(k2 << 16) * n0, __uint_as_float(k2 & 0xFFFF0000u) * n1);
         }
       }
-      if (hf == 1) {
+      if (tq == 3) {
         dec[s * KD + 2 * kp] = __expf(G0);
         dec[s * KD + 2 * kp + 1] = __expf(G1);
       }
@@ -378,23 +436,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_arrive(&bar[B_PREP + s]);
         mbar_arrive(&bar[B_DEC_FULL + s]);
       }
+      if (n >= 2 && !o_epilogue(n - 2)) gok = false;
     }
-  } else if (warp >= 8) {
+    for (int m = NT >= 2 ? NT - 2 : 0; m < NT && gok; ++m) gok = o_epilogue(m);
+  } else if (warp >= 4 + GATE_WARPS) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_STATE));
     // ------------------------- P epilogue, state update, O epilogue
-    constexpr int HC = VS / 2;                     // state columns per warpgroup
-    const int wg = (warp - 8) >> 2;                // 0 / 1
     const int quad = warp & 3;
     const int key = quad * 32 + lane;              // state row == TMEM lane
     const int prow = quad * 16 + (lane & 15);      // row of an M=64 accumulator
-    const int c0 = wg * HC;
     const int64_t bhi = static_cast<int64_t>(b) * H + h;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    float hreg[HC];
+    float hreg[VS];
     if (p.h0) {
-      const float4* src =
-          reinterpret_cast<const float4*>(p.h0 + (bhi * KD + key) * 128 + v0 + c0);
+      const float4* src = reinterpret_cast<const float4*>(p.h0 + (bhi * KD + key) * 128 + v0);
 #pragma unroll
-      for (int j = 0; j < HC / 4; ++j) {
+      for (int j = 0; j < VS / 4; ++j) {
         const float4 x = __ldg(src + j);
         hreg[4 * j] = x.x;
         hreg[4 * j + 1] = x.y;
@@ -403,50 +460,53 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < HC; ++j) hreg[j] = 0.f;
+      for (int j = 0; j < VS; ++j) hreg[j] = 0.f;
     }
     // H: MN-major B operand [128 keys][VS], 64-column atoms 16 KB apart.
     auto store_h = [&]() {
       uint8_t* hp = smem + CF::OFF_H;
 #pragma unroll
-      for (int c8 = 0; c8 < HC / 8; ++c8) {
-        const int col = c0 + c8 * 8;
+      for (int c8 = 0; c8 < VS / 8; ++c8) {
         const uint4 w = make_uint4(pack_bf16x2(hreg[c8 * 8], hreg[c8 * 8 + 1]),
                                    pack_bf16x2(hreg[c8 * 8 + 2], hreg[c8 * 8 + 3]),
                                    pack_bf16x2(hreg[c8 * 8 + 4], hreg[c8 * 8 + 5]),
                                    pack_bf16x2(hreg[c8 * 8 + 6], hreg[c8 * 8 + 7]));
-        *reinterpret_cast<uint4*>(hp + kmaj_off(key, col, 16384)) = w;
+        *reinterpret_cast<uint4*>(hp + kmaj_off(key, c8 * 8, 16384)) = w;
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_H_FULL]);
     };
-    // P = tril(A_m) in bf16, K-major (row = query, 128 B), this warpgroup's
-    // 32 columns.
+    // P = tril(A_m) in bf16, K-major (row = query, 128 B).
     auto p_epilogue = [&](int m) -> bool {
       const int s = m & 1;
       if (!mbar_wait(&bar[B_A_FULL + s], (m >> 1) & 1, ab)) return false;
       tc_fence_after();
-      uint32_t a[32];
-      tmem_ld32(lane_addr + CF::COL_A + s * 64 + wg * 32, a);
-      tmem_ld_wait(a);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_A_EMPTY + s]);
-      if (lane < 16) {
-        uint8_t* pp = smem + CF::OFF_P + prow * 128;
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          float f[8];
+      for (int half = 0; half < 2; ++half) {
+        uint32_t a[32];
+        tmem_ld32(lane_addr + CF::COL_A + s * 64 + half * 32, a);
+        tmem_ld_wait(a);
+        if (half == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar[B_A_EMPTY + s]);
+        }
+        if (lane < 16) {
+          uint8_t* pp = smem + CF::OFF_P + prow * 128;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int j = wg * 32 + c4 * 8 + e;
-            f[e] = j <= prow ? __uint_as_float(a[c4 * 8 + e]) : 0.f;
+          for (int c4 = 0; c4 < 4; ++c4) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int j = half * 32 + c4 * 8 + e;
+              f[e] = j <= prow ? __uint_as_float(a[c4 * 8 + e]) : 0.f;
+            }
+            const uint32_t ch = static_cast<uint32_t>(half * 4 + c4) ^ (prow & 7);
+            *reinterpret_cast<uint4*>(pp + (ch << 4)) =
+                make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                           pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
           }
-          const uint32_t chunk = static_cast<uint32_t>(wg * 4 + c4) ^ (prow & 7);
-          *reinterpret_cast<uint4*>(pp + (chunk << 4)) =
-              make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                         pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
         }
       }
       fence_proxy_async_smem();
@@ -464,50 +524,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float d = dec[s * KD + key];
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_DEC_EMPTY + s]);
-      if (!mbar_wait(&bar[B_S_FULL + s], ph2, ab)) { ok = false; break; }
+      if (!mbar_wait(&bar[B_S_FULL], n & 1, ab)) { ok = false; break; }
       tc_fence_after();
 #pragma unroll
-      for (int j = 0; j < HC; j += 32) {
+      for (int j = 0; j < VS; j += 32) {
         uint32_t sv[32];
-        tmem_ld32(lane_addr + CF::COL_S + s * VS + c0 + j, sv);
+        tmem_ld32(lane_addr + CF::COL_S + j, sv);
         tmem_ld_wait(sv);
 #pragma unroll
         for (int i = 0; i < 32; ++i) hreg[j + i] = d * (hreg[j + i] + __uint_as_float(sv[i]));
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_S_EMPTY + s]);
-      // O_n done -> H and P may be rewritten for chunk n+1
-      if (!mbar_wait(&bar[B_O_FULL], n & 1, ab)) { ok = false; break; }
+      if (lane == 0) mbar_arrive(&bar[B_S_EMPTY]);
+      // O_n done -> H and P may be rewritten for chunk n+1 (the next O
+      // accumulates into the other TMEM buffer meanwhile)
+      if (!mbar_wait(&bar[B_O_FULL + s], ph2, ab)) { ok = false; break; }
       tc_fence_after();
-      if (n + 1 < NT) store_h();
-      // O epilogue: rows 16*quad + lane (lane < 16) of the M=64 accumulator.
-      const int64_t row = static_cast<int64_t>(tok0) + n * C + prow;
-      uint4* dst = reinterpret_cast<uint4*>(p.o + (row * H + h) * 128 + v0 + c0);
-#pragma unroll
-      for (int j = 0; j < HC; j += 32) {
-        uint32_t ov[32];
-        tmem_ld32(lane_addr + CF::COL_O + c0 + j, ov);
-        tmem_ld_wait(ov);
-        if (lane < 16) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[j / 8 + i] = make_uint4(
-                pack_bf16x2(__uint_as_float(ov[8 * i]), __uint_as_float(ov[8 * i + 1])),
-                pack_bf16x2(__uint_as_float(ov[8 * i + 2]), __uint_as_float(ov[8 * i + 3])),
-                pack_bf16x2(__uint_as_float(ov[8 * i + 4]), __uint_as_float(ov[8 * i + 5])),
-                pack_bf16x2(__uint_as_float(ov[8 * i + 6]), __uint_as_float(ov[8 * i + 7])));
-        }
+      if (n + 1 < NT) {
+        store_h();
+        if (!p_epilogue(n + 1)) { ok = false; break; }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_O_EMPTY]);
-      if (n + 1 < NT && !p_epilogue(n + 1)) { ok = false; break; }
     }
     if (ok && p.ht) {
-      float4* dst = reinterpret_cast<float4*>(p.ht + (bhi * KD + key) * 128 + v0 + c0);
+      float4* dst = reinterpret_cast<float4*>(p.ht + (bhi * KD + key) * 128 + v0);
 #pragma unroll
-      for (int j = 0; j < HC / 4; ++j)
+      for (int j = 0; j < VS / 4; ++j)
         dst[j] = make_float4(hreg[4 * j], hreg[4 * j + 1], hreg[4 * j + 2], hreg[4 * j + 3]);
     }
   }
