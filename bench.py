@@ -161,13 +161,21 @@ def barrier(world):
 
 
 def max_over_ranks(x: float, world: int) -> float:
+    """Slowest rank's value (NCCL on the device, gloo on the host)."""
     if world == 1:
         return x
     import torch
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def whole_job_rate(units_per_rank: float, world: int, ms_slowest: float) -> float:
+    """Weak scaling: every rank processes `units_per_rank`; the job's rate is
+    the units of all ranks over the slowest rank's time (units per second)."""
+    return world * units_per_rank / (ms_slowest * 1e-3)
 
 
 def timed(fn, steps: int, warmup: int, world: int, sampler=None):
@@ -343,7 +351,7 @@ def run_b200(args):
     status = ops.device_status()
     if status != 0:
         raise SystemExit(f"device error word {status} after the timed region")
-    value = world * flops / (ms * 1e-3) / 1e12
+    value = whole_job_rate(flops, world, ms) / 1e12
     ai = flops / alg_bytes
     ridge = fp8_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
     bound = "hbm" if ai < ridge else "tensor"

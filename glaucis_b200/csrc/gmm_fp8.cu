@@ -5,19 +5,21 @@
 // Replaces the tokamax Pallas TPU `gmm` call made by the Glaucis template
 // (KE/examples/kernels/gmm_fp8_blockwise.py:109-119).
 //
-// Design (one persistent CTA per SM, 384 threads, warp specialised):
+// Design (one persistent CTA per SM, 384 threads, warp specialised; the tile
+// is 128 rows x BN columns with BN = 128 or 256):
 //   warp 0      TMA producer: per 128-deep K block loads the 128x128 e4m3
-//               activation tile (K-major) and the 128x256 e4m3 weight tile
-//               (N-major, two 128-byte-wide boxes) into a 4-stage ring.
-//   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (128x256x32) per K
-//               block into one of two TMEM accumulators (2 x 256 columns).
+//               activation tile (K-major) and the 128xBN e4m3 weight tile
+//               (N-major, 128-byte-wide boxes) into a STAGES-deep ring.
+//   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (128xBNx32) per K
+//               block into one of 512/BN TMEM accumulators; with BN = 128 the
+//               MMA runs up to three K blocks ahead of the promotion.
 //   warp 3      derives the ragged tile table from group_sizes.
-//   warps 4-11  promotion + epilogue (two warpgroups, 128 columns each):
+//   warps 4-11  promotion + epilogue (two warpgroups, BN/2 columns each):
 //               after every K block each thread reads its row's columns of
 //               the partial sum out of TMEM (double-buffered 32-column loads)
 //               and accumulates partial * (a_s * b_s) in fp32 registers with
-//               packed f32x2 FMAs, releasing the TMEM buffer so the next K
-//               block's MMAs overlap the promotion.  The finished row is
+//               packed f32x2 FMAs, releasing the TMEM buffer so later K
+//               blocks' MMAs overlap the promotion.  The finished row is
 //               written as bf16 (or fp32).
 //   Registers: the control warpgroup drops to 56 per thread and the two
 //   promotion warpgroups rise to 224 (128 x 56 + 256 x 224 = 384 x 168, the
@@ -32,26 +34,34 @@
 namespace gl {
 namespace gmm {
 
-constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
+constexpr int BM = 128, BK = 128;
 constexpr int A_BYTES = BM * BK;  // 16 KB
-constexpr int B_BYTES = BK * BN;  // 32 KB
 constexpr int NUM_THREADS = 384;
 constexpr int REG_CTRL = 56, REG_EPI = 224;
 static_assert(128 * REG_CTRL + 256 * REG_EPI <= NUM_THREADS * 168, "register split exceeds the launch allocation");
 constexpr int MAX_G = 1024;
 constexpr int TMEM_COLS = 512;
 
-constexpr uint32_t OFF_A = 0;
-constexpr uint32_t OFF_B = OFF_A + STAGES * A_BYTES;
-constexpr uint32_t OFF_BAR = OFF_B + STAGES * B_BYTES;  // 196608
-constexpr uint32_t OFF_MISC = OFF_BAR + 128;
-constexpr uint32_t OFF_ROWOFF = OFF_MISC + 128;
-constexpr uint32_t OFF_TILEOFF = OFF_ROWOFF + (MAX_G + 1) * 4;
-constexpr uint32_t SMEM_USED = OFF_TILEOFF + (MAX_G + 1) * 4;
-constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;  // slack for 1 KB alignment
-
-// e4m3 x e4m3 -> f32, A K-major, B MN-major, M=128, N=256.
-constexpr uint32_t IDESC = idesc(1, 0, 0, 0, 1, BM, BN);
+template <int BN>
+struct Cfg {
+  static constexpr int B_BYTES = BK * BN;                      // 16 / 32 KB
+  static constexpr int STAGES = (6 * 32768) / (A_BYTES + B_BYTES) < 6
+                                    ? (6 * 32768) / (A_BYTES + B_BYTES) : 6;  // 4 / 6
+  static constexpr int NBUF = TMEM_COLS / BN;                  // TMEM accumulators: 2 / 4
+  static constexpr int EC = BN / 2;                            // columns per promotion thread
+  static constexpr int NCH = EC / 32;                          // 32-column TMEM loads per K block
+  static constexpr uint32_t OFF_A = 0;
+  static constexpr uint32_t OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_B + STAGES * B_BYTES;
+  static constexpr uint32_t OFF_MISC = OFF_BAR + 256;
+  static constexpr uint32_t OFF_ROWOFF = OFF_MISC + 128;
+  static constexpr uint32_t OFF_TILEOFF = OFF_ROWOFF + (MAX_G + 1) * 4;
+  static constexpr uint32_t SMEM_USED = OFF_TILEOFF + (MAX_G + 1) * 4;
+  static constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;     // slack for 1 KB alignment
+  // e4m3 x e4m3 -> f32, A K-major, B MN-major, M=128, N=BN.
+  static constexpr uint32_t IDESC = idesc(1, 0, 0, 0, 1, BM, BN);
+  static_assert(2 * STAGES + 2 * NBUF + 1 <= 32, "barrier area");
+};
 
 struct Params {
   const float* a_s;
@@ -67,7 +77,8 @@ struct Tile {
   int g, m0, rows, n0;
 };
 
-__device__ __forceinline__ Tile decode_tile(int t, const int* tile_off, const int* row_off, int G) {
+__device__ __forceinline__ Tile decode_tile(int t, const int* tile_off, const int* row_off, int G,
+                                            int bn) {
   int lo = 0, hi = G - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -81,27 +92,30 @@ __device__ __forceinline__ Tile decode_tile(int t, const int* tile_off, const in
   const int i = local % mt, j = local / mt;
   r.m0 = row_off[lo] + i * BM;
   r.rows = min(BM, size - i * BM);
-  r.n0 = j * BN;
+  r.n0 = j * bn;
   return r;
 }
 
+template <int BN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gmm_fp8_fwd_kernel(const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_b, const Params p) {
+  using CF = Cfg<BN>;
+  constexpr int STAGES = CF::STAGES, NBUF = CF::NBUF, EC = CF::EC, NCH = CF::NCH;
   extern __shared__ uint8_t smem_raw[];
   // 1 KB-aligned base derived by pointer arithmetic on the shared array so
   // that every access below stays in the shared address space.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + CF::OFF_BAR);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
-  int* abort_flag = reinterpret_cast<int*>(smem + OFF_MISC + 4);
-  int* total_tiles_s = reinterpret_cast<int*>(smem + OFF_MISC + 8);
-  int* row_off = reinterpret_cast<int*>(smem + OFF_ROWOFF);
-  int* tile_off = reinterpret_cast<int*>(smem + OFF_TILEOFF);
+  uint64_t* tempty = tfull + NBUF;
+  uint64_t* drain = tempty + NBUF;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + CF::OFF_MISC);
+  int* abort_flag = reinterpret_cast<int*>(smem + CF::OFF_MISC + 4);
+  int* total_tiles_s = reinterpret_cast<int*>(smem + CF::OFF_MISC + 8);
+  int* row_off = reinterpret_cast<int*>(smem + CF::OFF_ROWOFF);
+  int* tile_off = reinterpret_cast<int*>(smem + CF::OFF_TILEOFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.G, K = p.K, N = p.N;
@@ -122,7 +136,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_init(&full[i], 1);
         mbar_init(&empty[i], 1);
       }
-      for (int i = 0; i < 2; ++i) {
+      for (int i = 0; i < NBUF; ++i) {
         mbar_init(&tfull[i], 1);
         mbar_init(&tempty[i], 8);  // one arrival per promotion warp
       }
@@ -182,18 +196,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const Tile tl = decode_tile(t, tile_off, row_off, G);
+        const Tile tl = decode_tile(t, tile_off, row_off, G, BN);
         const int brow = tl.g * K;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, ab)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
-          uint8_t* sa = smem + OFF_A + s * A_BYTES;
-          uint8_t* sb = smem + OFF_B + s * B_BYTES;
+          mbar_arrive_expect_tx(&full[s], A_BYTES + CF::B_BYTES);
+          uint8_t* sa = smem + CF::OFF_A + s * A_BYTES;
+          uint8_t* sb = smem + CF::OFF_B + s * CF::B_BYTES;
           tma_load_2d(sa, &tm_a, &full[s], kb * BK, tl.m0);
-          tma_load_2d(sb, &tm_b, &full[s], tl.n0, brow + kb * BK);
-          tma_load_2d(sb + 16384, &tm_b, &full[s], tl.n0 + 128, brow + kb * BK);
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j)
+            tma_load_2d(sb + j * 16384, &tm_b, &full[s], tl.n0 + 128 * j, brow + kb * BK);
         }
       }
       if (!ok) {
@@ -214,13 +229,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // ------------------------------------------------------------ MMA
       int it = 0, acc_it = 0;
       bool ok = true;
-      const uint32_t a_base = smem_u32(smem + OFF_A), b_base = smem_u32(smem + OFF_B);
+      const uint32_t a_base = smem_u32(smem + CF::OFF_A), b_base = smem_u32(smem + CF::OFF_B);
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         for (int kb = 0; kb < KB; ++kb, ++it, ++acc_it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          const int buf = acc_it & 1;
-          const uint32_t aph = (acc_it >> 1) & 1;
+          const int buf = acc_it % NBUF;
+          const uint32_t aph = (acc_it / NBUF) & 1;
           if (!mbar_wait(&tempty[buf], aph ^ 1, ab)) { ok = false; break; }
           if (!mbar_wait(&full[s], ph, ab)) { ok = false; break; }
           tc_fence_after();
@@ -228,8 +243,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             const uint64_t ad = sdesc(a_base + s * A_BYTES + kk * 32, 16, 1024, kSwizzle128B);
-            const uint64_t bd = sdesc(b_base + s * B_BYTES + kk * 4096, 16384, 1024, kSwizzle128B);
-            mma_f8f6f4(d, ad, bd, IDESC, kk > 0 ? 1u : 0u);
+            const uint64_t bd =
+                sdesc(b_base + s * CF::B_BYTES + kk * 4096, 16384, 1024, kSwizzle128B);
+            mma_f8f6f4(d, ad, bd, CF::IDESC, kk > 0 ? 1u : 0u);
           }
           tc_commit(&empty[s]);
           tc_commit(&tfull[buf]);
@@ -251,21 +267,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int quad = warp & 3;
     const int chalf = ew >> 2;
     const int r = quad * 32 + lane;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + chalf * 128;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + chalf * EC;
     int acc_it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      const Tile tl = decode_tile(t, tile_off, row_off, G);
+      const Tile tl = decode_tile(t, tile_off, row_off, G, BN);
       const bool row_ok = r < tl.rows;
       const int64_t grow = static_cast<int64_t>(tl.m0) + r;
-      const int ncol0 = tl.n0 + chalf * 128;
+      const int ncol0 = tl.n0 + chalf * EC;
       const bool col_ok = ncol0 < N;
       const int nb = ncol0 >> 7;
       const float* sa_row = p.a_s + grow * KB;
       const float* sb_col = p.b_s + static_cast<int64_t>(tl.g) * KB * NB + nb;
-      float2 acc[64];
+      float2 acc[EC / 2];
 #pragma unroll
-      for (int j = 0; j < 64; ++j) acc[j] = make_float2(0.f, 0.f);
+      for (int j = 0; j < EC / 2; ++j) acc[j] = make_float2(0.f, 0.f);
       float sa_next = row_ok ? __ldg(sa_row) : 0.f;
       float sb_next = col_ok ? __ldg(sb_col) : 0.f;
       for (int kb = 0; kb < KB; ++kb, ++acc_it) {
@@ -275,44 +291,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           sb_next = col_ok ? __ldg(sb_col + static_cast<int64_t>(kb + 1) * NB) : 0.f;
         }
         const float2 sc2 = make_float2(sc, sc);
-        const int buf = acc_it & 1;
-        if (!mbar_wait(&tfull[buf], (acc_it >> 1) & 1, ab)) { ok = false; break; }
+        const int buf = acc_it % NBUF;
+        if (!mbar_wait(&tfull[buf], (acc_it / NBUF) & 1, ab)) { ok = false; break; }
         tc_fence_after();
         const uint32_t ta = lane_base + buf * BN;
-        uint32_t va[32], vb[32];
-        auto promote = [&](const uint32_t (&v)[32], int base) {
+        uint32_t v[2][32];
+        auto promote = [&](const uint32_t (&x)[32], int base) {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            acc[base + j] = __ffma2_rn(make_float2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])),
+            acc[base + j] = __ffma2_rn(make_float2(__uint_as_float(x[2 * j]), __uint_as_float(x[2 * j + 1])),
                                        sc2, acc[base + j]);
         };
-        tmem_ld32(ta, va);
-        tmem_ld_wait(va);
-        tmem_ld32(ta + 32, vb);
-        promote(va, 0);
-        tmem_ld_wait(vb);
-        tmem_ld32(ta + 64, va);
-        promote(vb, 16);
-        tmem_ld_wait(va);
-        tmem_ld32(ta + 96, vb);
-        promote(va, 32);
-        tmem_ld_wait(vb);
+        // chunk c is loaded while chunk c-1 is promoted
+        tmem_ld32(ta, v[0]);
+        tmem_ld_wait(v[0]);
+#pragma unroll
+        for (int c = 1; c < NCH; ++c) {
+          tmem_ld32(ta + 32 * c, v[c & 1]);
+          promote(v[(c - 1) & 1], 16 * (c - 1));
+          tmem_ld_wait(v[c & 1]);
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[buf]);
-        promote(vb, 48);
+        promote(v[(NCH - 1) & 1], 16 * (NCH - 1));
       }
       if (!ok) break;
       if (row_ok && col_ok) {
         if (p.out_f32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + grow * N + ncol0);
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
+          for (int i = 0; i < EC / 4; ++i)
             dst[i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
         } else {
           uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + grow * N + ncol0);
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
+          for (int i = 0; i < EC / 8; ++i)
             dst[i] = make_uint4(pack_bf16x2(acc[4 * i].x, acc[4 * i].y),
                                 pack_bf16x2(acc[4 * i + 1].x, acc[4 * i + 1].y),
                                 pack_bf16x2(acc[4 * i + 2].x, acc[4 * i + 2].y),
@@ -336,7 +350,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // ---------------------------------------------------------------------------
 // Host launcher (called from capi.cu after argument validation).
 // ---------------------------------------------------------------------------
+#include <cstdlib>
+
 #include "tmap.h"
+
+template <int BN>
+static int launch_bn(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const gl::gmm::Params& p,
+                     int64_t G, int64_t M, int64_t N, cudaStream_t st, int num_sms,
+                     const char** why) {
+  using namespace gl::gmm;
+  using CF = Cfg<BN>;
+  if (!gl_set_smem_attr(reinterpret_cast<const void*>(gmm_fp8_fwd_kernel<BN>), 0,
+                        static_cast<int>(CF::SMEM_BYTES), why))
+    return -2;
+  const int64_t ntn = (N + BN - 1) / BN;
+  const int64_t max_tiles = ((M + BM - 1) / BM + G) * ntn;
+  const int grid = static_cast<int>(max_tiles < num_sms ? (max_tiles > 0 ? max_tiles : 1) : num_sms);
+  gmm_fp8_fwd_kernel<BN><<<grid, NUM_THREADS, CF::SMEM_BYTES, st>>>(tm_a, tm_b, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return -2;
+  }
+  return 0;
+}
 
 int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
                       const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
@@ -350,12 +387,6 @@ int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const 
   if (!gl_make_tmap_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, b_q, N, G * K, N, 128, 128,
                        CU_TENSOR_MAP_SWIZZLE_128B, why))
     return -1;
-  if (!gl_set_smem_attr(reinterpret_cast<const void*>(gl::gmm::gmm_fp8_fwd_kernel), 0,
-                        static_cast<int>(SMEM_BYTES), why))
-    return -2;
-  const int64_t ntn = (N + BN - 1) / BN;
-  const int64_t max_tiles = ((M + BM - 1) / BM + G) * ntn;
-  const int grid = static_cast<int>(max_tiles < num_sms ? (max_tiles > 0 ? max_tiles : 1) : num_sms);
   Params p;
   p.a_s = a_s;
   p.b_s = b_s;
@@ -367,11 +398,10 @@ int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const 
   p.K = static_cast<int>(K);
   p.N = static_cast<int>(N);
   p.out_f32 = out_f32;
-  gl::gmm::gmm_fp8_fwd_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(tm_a, tm_b, p);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    *why = cudaGetErrorString(e);
-    return -2;
-  }
-  return 0;
+  // Tile width: both instantiations are exact for any N % 128 == 0.
+  // GLAUCIS_GMM_BN=128|256 overrides the default.
+  int bn = 256;
+  if (const char* e = std::getenv("GLAUCIS_GMM_BN")) bn = std::atoi(e) == 128 ? 128 : 256;
+  return bn == 256 ? launch_bn<256>(tm_a, tm_b, p, G, M, N, st, num_sms, why)
+                   : launch_bn<128>(tm_a, tm_b, p, G, M, N, st, num_sms, why);
 }
