@@ -78,7 +78,7 @@ struct Tile {
 };
 
 __device__ __forceinline__ Tile decode_tile(int t, const int* tile_off, const int* row_off, int G,
-                                            int bn) {
+                                            int bn, int bm = BM) {
   int lo = 0, hi = G - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -88,12 +88,56 @@ __device__ __forceinline__ Tile decode_tile(int t, const int* tile_off, const in
   r.g = lo;
   const int local = t - tile_off[lo];
   const int size = row_off[lo + 1] - row_off[lo];
-  const int mt = (size + BM - 1) / BM;
+  const int mt = (size + bm - 1) / bm;
   const int i = local % mt, j = local / mt;
-  r.m0 = row_off[lo] + i * BM;
-  r.rows = min(BM, size - i * BM);
+  r.m0 = row_off[lo] + i * bm;
+  r.rows = min(bm, size - i * bm);
   r.n0 = j * bn;
   return r;
+}
+
+// Warp-scan of group_sizes into exclusive row / tile prefix sums (tiles of
+// `bm` rows x `bn` columns).  Whole warp.  Returns nothing; writes the tables
+// and the validated tile total into shared memory.
+__device__ __forceinline__ void build_group_table(const int32_t* group_sizes, int G, int M, int bm,
+                                                  int ntn, int* row_off, int* tile_off,
+                                                  int* total_tiles, int* err, int lane) {
+  const int per = (G + 31) / 32;
+  const int g0 = min(G, lane * per), g1 = min(G, g0 + per);
+  int rsum = 0, tsum = 0, bad = 0;
+  for (int g = g0; g < g1; ++g) {
+    const int sz = group_sizes[g];
+    bad |= sz < 0;
+    const int s = max(sz, 0);
+    rsum += s;
+    tsum += (s + bm - 1) / bm * ntn;
+  }
+  int rinc = rsum, tinc = tsum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int rv = __shfl_up_sync(0xffffffffu, rinc, o);
+    const int tv = __shfl_up_sync(0xffffffffu, tinc, o);
+    if (lane >= o) {
+      rinc += rv;
+      tinc += tv;
+    }
+  }
+  int r = rinc - rsum, tt = tinc - tsum;
+  for (int g = g0; g < g1; ++g) {
+    const int s = max(group_sizes[g], 0);
+    row_off[g] = r;
+    tile_off[g] = tt;
+    r += s;
+    tt += (s + bm - 1) / bm * ntn;
+  }
+  bad = __any_sync(0xffffffffu, bad);
+  if (lane == 31) {
+    row_off[G] = rinc;
+    tile_off[G] = tinc;
+    const bool ok = !bad && rinc <= M;
+    *total_tiles = ok ? tinc : 0;
+    if (!ok) atomicExch(err, GL_DEV_BAD_GROUPS);
+  }
 }
 
 template <int BN>
@@ -145,43 +189,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       fence_mbar_init();
     }
   } else if (warp == 3) {
-    // Group table: exclusive prefix sums of rows and tiles (warp scan).
-    const int per = (G + 31) / 32;
-    const int g0 = min(G, lane * per), g1 = min(G, g0 + per);
-    int rsum = 0, tsum = 0, bad = 0;
-    for (int g = g0; g < g1; ++g) {
-      const int sz = p.group_sizes[g];
-      bad |= sz < 0;
-      const int s = max(sz, 0);
-      rsum += s;
-      tsum += (s + BM - 1) / BM * ntn;
-    }
-    int rinc = rsum, tinc = tsum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int rv = __shfl_up_sync(0xffffffffu, rinc, o);
-      const int tv = __shfl_up_sync(0xffffffffu, tinc, o);
-      if (lane >= o) {
-        rinc += rv;
-        tinc += tv;
-      }
-    }
-    int r = rinc - rsum, tt = tinc - tsum;
-    for (int g = g0; g < g1; ++g) {
-      const int s = max(p.group_sizes[g], 0);
-      row_off[g] = r;
-      tile_off[g] = tt;
-      r += s;
-      tt += (s + BM - 1) / BM * ntn;
-    }
-    bad = __any_sync(0xffffffffu, bad);
-    if (lane == 31) {
-      row_off[G] = rinc;
-      tile_off[G] = tinc;
-      const bool ok = !bad && rinc <= p.M;
-      *total_tiles_s = ok ? tinc : 0;
-      if (!ok) atomicExch(p.err, GL_DEV_BAD_GROUPS);
-    }
+    build_group_table(p.group_sizes, G, p.M, BM, ntn, row_off, tile_off, total_tiles_s, p.err, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -344,6 +352,239 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ===========================================================================
+// CTA-pair variant: a cluster of two CTAs (two SMs) computes a 256 x 256
+// tile with tcgen05.mma.cta_group::2 (M=256 across the pair, N=256).  Each
+// CTA TMA-loads its own 128 activation rows and its 128-column half of the
+// weight tile (no multicast); the loads of both CTAs complete on the leader
+// CTA's stage barrier, only the leader issues MMAs and its commits arrive on
+// both CTAs' barriers; each CTA promotes its own 128 x 256 accumulator and
+// releases it on the leader's barrier.  Per SM and K block this moves 32 KB
+// instead of 48 KB into shared memory for the same MMA work.
+// ===========================================================================
+constexpr int PM = 256;                 // rows per pair tile
+constexpr int PAIR_STAGES = 6;
+constexpr int PB_BYTES = BK * 128;      // each CTA's half of the weight tile (16 KB)
+constexpr uint32_t P_OFF_A = 0;
+constexpr uint32_t P_OFF_B = P_OFF_A + PAIR_STAGES * A_BYTES;
+constexpr uint32_t P_OFF_BAR = P_OFF_B + PAIR_STAGES * PB_BYTES;
+constexpr uint32_t P_OFF_MISC = P_OFF_BAR + 256;
+constexpr uint32_t P_OFF_ROWOFF = P_OFF_MISC + 128;
+constexpr uint32_t P_OFF_TILEOFF = P_OFF_ROWOFF + (MAX_G + 1) * 4;
+constexpr uint32_t P_SMEM_BYTES = P_OFF_TILEOFF + (MAX_G + 1) * 4 + 1024;
+constexpr uint32_t P_IDESC = idesc(1, 0, 0, 0, 1, PM, 256);
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gmm_fp8_fwd_pair_kernel(const __grid_constant__ CUtensorMap tm_a,
+                            const __grid_constant__ CUtensorMap tm_b, const Params p) {
+  constexpr int STAGES = PAIR_STAGES, NBUF = 2, BN = 256, EC = 128, NCH = 4;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + NBUF;
+  uint64_t* drain = tempty + NBUF;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + P_OFF_MISC);
+  int* abort_flag = reinterpret_cast<int*>(smem + P_OFF_MISC + 4);
+  int* total_tiles_s = reinterpret_cast<int*>(smem + P_OFF_MISC + 8);
+  int* row_off = reinterpret_cast<int*>(smem + P_OFF_ROWOFF);
+  int* tile_off = reinterpret_cast<int*>(smem + P_OFF_TILEOFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cid = static_cast<int>(cluster_id_x()), ncl = static_cast<int>(num_clusters_x());
+  const int G = p.G, K = p.K, N = p.N;
+  const int KB = K / BK, NB = N / 128;
+  const int ntn = (N + BN - 1) / BN;
+  const Abort ab{abort_flag, p.err};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_a);
+      prefetch_tmap(&tm_b);
+    }
+    tmem_alloc_pair(tmem_holder, TMEM_COLS);
+    tmem_relinquish_pair();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int i = 0; i < STAGES; ++i) {
+        mbar_init(&full[i], 2);    // one arrive.expect_tx per CTA of the pair
+        mbar_init(&empty[i], 1);
+      }
+      for (int i = 0; i < NBUF; ++i) {
+        mbar_init(&tfull[i], 1);
+        mbar_init(&tempty[i], 16);  // promotion warps of both CTAs
+      }
+      mbar_init(drain, 1);
+      *abort_flag = 0;
+      fence_mbar_init();
+    }
+  } else if (warp == 3) {
+    build_group_table(p.group_sizes, G, p.M, PM, ntn, row_off, tile_off, total_tiles_s, p.err, lane);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int total = *total_tiles_s;
+
+  if (warp == 0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
+    if (lane == 0) {
+      // ------------------------------------------------- producer (both CTAs)
+      int it = 0;
+      bool ok = true;
+      for (int t = cid; t < total && ok; t += ncl) {
+        const Tile tl = decode_tile(t, tile_off, row_off, G, BN, PM);
+        const int brow = tl.g * K;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, ab)) { ok = false; break; }
+          const uint32_t fbar = mapa_shared(smem_u32(&full[s]), 0);
+          mbar_arrive_expect_tx_cluster(fbar, A_BYTES + PB_BYTES);
+          tma_load_2d_pair(smem + P_OFF_A + s * A_BYTES, &tm_a, fbar, kb * BK,
+                           tl.m0 + 128 * static_cast<int>(rank));
+          tma_load_2d_pair(smem + P_OFF_B + s * PB_BYTES, &tm_b, fbar,
+                           tl.n0 + 128 * static_cast<int>(rank), brow + kb * BK);
+        }
+      }
+      if (!ok) {
+        // Give copies already in flight time to land before the CTA exits.
+        const uint64_t t0 = global_ns();
+        while (global_ns() - t0 < 2000000ull) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
+    if (lane == 0 && leader) {
+      // ------------------------------------------------- MMA (leader CTA)
+      int it = 0, acc_it = 0;
+      bool ok = true;
+      const uint32_t a_base = smem_u32(smem + P_OFF_A), b_base = smem_u32(smem + P_OFF_B);
+      for (int t = cid; t < total && ok; t += ncl) {
+        for (int kb = 0; kb < KB; ++kb, ++it, ++acc_it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          const int buf = acc_it % NBUF;
+          const uint32_t aph = (acc_it / NBUF) & 1;
+          if (!mbar_wait(&tempty[buf], aph ^ 1, ab)) { ok = false; break; }
+          if (!mbar_wait(&full[s], ph, ab)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d = tmem + buf * BN;
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            const uint64_t ad = sdesc(a_base + s * A_BYTES + kk * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bd = sdesc(b_base + s * PB_BYTES + kk * 4096, 16384, 1024, kSwizzle128B);
+            mma_f8f6f4_pair(d, ad, bd, P_IDESC, kk > 0 ? 1u : 0u);
+          }
+          tc_commit_pair_mc(&empty[s], 0x3);
+          tc_commit_pair_mc(&tfull[buf], 0x3);
+        }
+      }
+      // Wait for every MMA issued above before TMEM can be released.
+      tc_commit_pair_mc(drain, 0x1);
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 100000000ull) {
+      }
+    }
+    __syncwarp();
+  } else if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_EPI));
+    // ------------------------------------------- promotion (both CTAs)
+    const int ew = warp - 4;
+    const int quad = warp & 3;
+    const int chalf = ew >> 2;
+    const int r = quad * 32 + lane;
+    const int prow = static_cast<int>(rank) * 128 + r;       // row within the pair tile
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + chalf * EC;
+    const uint32_t tempty_c0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    const uint32_t tempty_c1 = mapa_shared(smem_u32(&tempty[1]), 0);
+    int acc_it = 0;
+    bool ok = true;
+    for (int t = cid; t < total && ok; t += ncl) {
+      const Tile tl = decode_tile(t, tile_off, row_off, G, BN, PM);
+      const bool row_ok = prow < tl.rows;
+      const int64_t grow = static_cast<int64_t>(tl.m0) + prow;
+      const int ncol0 = tl.n0 + chalf * EC;
+      const bool col_ok = ncol0 < N;
+      const int nb = ncol0 >> 7;
+      const float* sa_row = p.a_s + grow * KB;
+      const float* sb_col = p.b_s + static_cast<int64_t>(tl.g) * KB * NB + nb;
+      float2 acc[EC / 2];
+#pragma unroll
+      for (int j = 0; j < EC / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+      float sa_next = row_ok ? __ldg(sa_row) : 0.f;
+      float sb_next = col_ok ? __ldg(sb_col) : 0.f;
+      for (int kb = 0; kb < KB; ++kb, ++acc_it) {
+        const float sc = sa_next * sb_next;
+        if (kb + 1 < KB) {
+          sa_next = row_ok ? __ldg(sa_row + kb + 1) : 0.f;
+          sb_next = col_ok ? __ldg(sb_col + static_cast<int64_t>(kb + 1) * NB) : 0.f;
+        }
+        const float2 sc2 = make_float2(sc, sc);
+        const int buf = acc_it % NBUF;
+        if (!mbar_wait(&tfull[buf], (acc_it / NBUF) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ta = lane_base + buf * BN;
+        uint32_t v[2][32];
+        auto promote = [&](const uint32_t (&x)[32], int base) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            acc[base + j] = __ffma2_rn(make_float2(__uint_as_float(x[2 * j]), __uint_as_float(x[2 * j + 1])),
+                                       sc2, acc[base + j]);
+        };
+        tmem_ld32(ta, v[0]);
+        tmem_ld_wait(v[0]);
+#pragma unroll
+        for (int c = 1; c < NCH; ++c) {
+          tmem_ld32(ta + 32 * c, v[c & 1]);
+          promote(v[(c - 1) & 1], 16 * (c - 1));
+          tmem_ld_wait(v[c & 1]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(buf ? tempty_c1 : tempty_c0);
+        promote(v[(NCH - 1) & 1], 16 * (NCH - 1));
+      }
+      if (!ok) break;
+      if (row_ok && col_ok) {
+        if (p.out_f32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + grow * N + ncol0);
+#pragma unroll
+          for (int i = 0; i < EC / 4; ++i)
+            dst[i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + grow * N + ncol0);
+#pragma unroll
+          for (int i = 0; i < EC / 8; ++i)
+            dst[i] = make_uint4(pack_bf16x2(acc[4 * i].x, acc[4 * i].y),
+                                pack_bf16x2(acc[4 * i + 1].x, acc[4 * i + 1].y),
+                                pack_bf16x2(acc[4 * i + 2].x, acc[4 * i + 2].y),
+                                pack_bf16x2(acc[4 * i + 3].x, acc[4 * i + 3].y));
+        }
+      }
+    }
+  }
+
+  // Both CTAs: every MMA of the pair is complete (the leader drained them) and
+  // every cross-CTA arrival has been made before TMEM is released.
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, TMEM_COLS);
+  }
+}
+
 }  // namespace gmm
 }  // namespace gl
 
@@ -351,6 +592,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // Host launcher (called from capi.cu after argument validation).
 // ---------------------------------------------------------------------------
 #include <cstdlib>
+#include <cstring>
 
 #include "tmap.h"
 
@@ -368,6 +610,42 @@ static int launch_bn(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const gl:
   const int grid = static_cast<int>(max_tiles < num_sms ? (max_tiles > 0 ? max_tiles : 1) : num_sms);
   gmm_fp8_fwd_kernel<BN><<<grid, NUM_THREADS, CF::SMEM_BYTES, st>>>(tm_a, tm_b, p);
   const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return -2;
+  }
+  return 0;
+}
+
+static int launch_pair(const CUtensorMap& tm_a, const CUtensorMap& tm_b,
+                       const gl::gmm::Params& p, int64_t G, int64_t M, int64_t N, cudaStream_t st,
+                       int num_sms, const char** why) {
+  using namespace gl::gmm;
+  const void* fn = reinterpret_cast<const void*>(gmm_fp8_fwd_pair_kernel);
+  if (!gl_set_smem_attr(fn, 0, static_cast<int>(P_SMEM_BYTES), why)) return -2;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = P_SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // Persistent: as many pairs as can be resident at once, capped by the work.
+  cfg.gridDim = dim3(static_cast<unsigned>(num_sms & ~1), 1, 1);
+  int max_clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&max_clusters, fn, &cfg) != cudaSuccess || max_clusters < 1) {
+    *why = "cudaOccupancyMaxActiveClusters failed for the CTA-pair kernel";
+    return -2;
+  }
+  const int64_t ntn = (N + 255) / 256;
+  const int64_t max_tiles = ((M + PM - 1) / PM + G) * ntn;
+  const int64_t clusters = max_tiles < max_clusters ? (max_tiles > 0 ? max_tiles : 1) : max_clusters;
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gmm_fp8_fwd_pair_kernel, tm_a, tm_b, p);
   if (e != cudaSuccess) {
     *why = cudaGetErrorString(e);
     return -2;
@@ -398,10 +676,13 @@ int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const 
   p.K = static_cast<int>(K);
   p.N = static_cast<int>(N);
   p.out_f32 = out_f32;
-  // Tile width: both instantiations are exact for any N % 128 == 0.
-  // GLAUCIS_GMM_BN=128|256 overrides the default.
-  int bn = 256;
-  if (const char* e = std::getenv("GLAUCIS_GMM_BN")) bn = std::atoi(e) == 128 ? 128 : 256;
-  return bn == 256 ? launch_bn<256>(tm_a, tm_b, p, G, M, N, st, num_sms, why)
-                   : launch_bn<128>(tm_a, tm_b, p, G, M, N, st, num_sms, why);
+  // Variant: GLAUCIS_GMM_VARIANT=pair|256|128 overrides the default.
+  int variant = 256;
+  if (const char* e = std::getenv("GLAUCIS_GMM_VARIANT")) {
+    if (std::strcmp(e, "pair") == 0) variant = 2;
+    else if (std::atoi(e) == 128) variant = 128;
+  }
+  if (variant == 2) return launch_pair(tm_a, tm_b, p, G, M, N, st, num_sms, why);
+  return variant == 256 ? launch_bn<256>(tm_a, tm_b, p, G, M, N, st, num_sms, why)
+                        : launch_bn<128>(tm_a, tm_b, p, G, M, N, st, num_sms, why);
 }

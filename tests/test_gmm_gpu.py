@@ -1,6 +1,9 @@
 """Parity of the sm_100a grouped FP8 matmul and its quantisers against the CPU
 oracle, through the C ABI (glaucis_b200.ops is a thin ctypes wrapper).
 
+The launcher reads GLAUCIS_GMM_VARIANT at every call, so each test runs once
+per kernel variant.
+
 Tolerances: quantisers are bit-exact (bytes and fp32 scales).  The matmul is
 checked element-wise with |gpu - ref| <= 1e-2 * |ref| + 1e-3 * rms(ref), i.e.
 within rtol 1e-2 of the dequantised fp32 reference (the atol term only covers
@@ -19,6 +22,15 @@ from tests.helpers import assert_close, rel_fro
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 RTOL, ATOL_FRAC = 1e-2, 1e-3
+VARIANTS = ["256", "128", "pair"]
+
+
+@pytest.fixture(autouse=True, params=VARIANTS)
+def kernel_variant(request, monkeypatch):
+    """Every matmul test runs on each kernel variant: the 1-SM kernel with
+    256- and 128-column tiles and the CTA-pair kernel (256 x 256 tiles)."""
+    monkeypatch.setenv("GLAUCIS_GMM_VARIANT", request.param)
+    return request.param
 
 
 def _np_bytes(t):
@@ -88,6 +100,15 @@ def test_gmm_ragged_empty_partial(cuda, out_dtype):
     sizes = [0, 1, 300, 0, 129, 127, 2, 0]
     _gmm_case(cuda, len(sizes), 600, 384, 384, sizes, seed=3, out_dtype=out_dtype,
               zero_block=True)
+
+
+def test_gmm_pair_tile_edges(cuda):
+    # 256-row tiles: a group of exactly 128 rows (second CTA of a pair has no
+    # valid row), 255 / 257 rows (second CTA partial / a 1-row second tile),
+    # several 256-row tiles, and N = 640 (the last 256-column tile is half
+    # outside the weight matrix).
+    sizes = [128, 256, 257, 255, 0, 512, 384]
+    _gmm_case(cuda, len(sizes), 1800, 256, 640, sizes, seed=5)
 
 
 def test_gmm_golden_fixture(cuda):
