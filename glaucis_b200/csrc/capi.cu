@@ -15,10 +15,10 @@
 #include "tmap.h"
 
 // Launchers defined next to their kernels.
-int gl_launch_quant_act(const void* x, int64_t M, int64_t K, void* q, float* s, cudaStream_t st,
-                        int num_sms);
-int gl_launch_quant_w(const void* w, int64_t G, int64_t K, int64_t N, void* q, float* s,
-                      cudaStream_t st, int num_sms);
+int gl_launch_quant_act(const void* x, int64_t M, int64_t K, void* q, float* s, int* err,
+                        cudaStream_t st, int num_sms, const char** why);
+int gl_launch_quant_w(const void* w, int64_t G, int64_t K, int64_t N, void* q, float* s, int* err,
+                      cudaStream_t st, int num_sms, const char** why);
 int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
                       const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
                       void* out, int out_f32, int* err, cudaStream_t st, int num_sms,
@@ -175,32 +175,36 @@ const char* gl_version(void) { return "glaucis_b200 0.1 (sm_100a)"; }
 
 int gl_quant_act_1x128(const void* x, int64_t M, int64_t K, void* q, float* s, int* err_word,
                        void* stream) {
-  (void)err_word;
   if (!x || !q || !s) return fail(GL_EINVAL, "gl_quant_act_1x128: null pointer");
   if (M < 0 || K <= 0 || K % 128 != 0)
     return fail(GL_EINVAL, "gl_quant_act_1x128: need M >= 0 and K a positive multiple of 128");
-  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u))
-    return fail(GL_EINVAL, "gl_quant_act_1x128: x must be 16-byte and q 8-byte aligned");
+  if (!aligned16(x) || !aligned16(q))
+    return fail(GL_EINVAL, "gl_quant_act_1x128: x and q must be 16-byte aligned");
   if (M == 0) return GL_OK;
   DeviceState* d = nullptr;
   if (int rc = device_state(&d)) return rc;
-  if (gl_launch_quant_act(x, M, K, q, s, static_cast<cudaStream_t>(stream), d->num_sms) != 0)
-    return fail(GL_ELAUNCH, std::string("quant_act launch: ") + cudaGetErrorString(cudaGetLastError()));
+  const char* why = "";
+  const int rc = gl_launch_quant_act(x, M, K, q, s, err_word ? err_word : d->err,
+                                     static_cast<cudaStream_t>(stream), d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string("gl_quant_act_1x128: ") + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string("quant_act launch: ") + why);
   return GL_OK;
 }
 
 int gl_quant_w_128x128(const void* w, int64_t G, int64_t K, int64_t N, void* q, float* s,
                        int* err_word, void* stream) {
-  (void)err_word;
   if (!w || !q || !s) return fail(GL_EINVAL, "gl_quant_w_128x128: null pointer");
   if (G <= 0 || K <= 0 || N <= 0 || K % 128 != 0 || N % 128 != 0)
     return fail(GL_EINVAL, "gl_quant_w_128x128: need G > 0 and K, N positive multiples of 128");
-  if (!aligned16(w) || (reinterpret_cast<uintptr_t>(q) & 7u))
-    return fail(GL_EINVAL, "gl_quant_w_128x128: w must be 16-byte and q 8-byte aligned");
+  if (!aligned16(w) || !aligned16(q))
+    return fail(GL_EINVAL, "gl_quant_w_128x128: w and q must be 16-byte aligned");
   DeviceState* d = nullptr;
   if (int rc = device_state(&d)) return rc;
-  if (gl_launch_quant_w(w, G, K, N, q, s, static_cast<cudaStream_t>(stream), d->num_sms) != 0)
-    return fail(GL_ELAUNCH, std::string("quant_w launch: ") + cudaGetErrorString(cudaGetLastError()));
+  const char* why = "";
+  const int rc = gl_launch_quant_w(w, G, K, N, q, s, err_word ? err_word : d->err,
+                                   static_cast<cudaStream_t>(stream), d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string("gl_quant_w_128x128: ") + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string("quant_w launch: ") + why);
   return GL_OK;
 }
 

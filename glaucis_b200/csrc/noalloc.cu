@@ -27,8 +27,8 @@
 
 #include "../../include/glaucis_b200.h"
 
-int gl_launch_quant_act(const void* x, int64_t M, int64_t K, void* q, float* s, cudaStream_t st,
-                        int num_sms);
+int gl_launch_quant_act(const void* x, int64_t M, int64_t K, void* q, float* s, int* err,
+                        cudaStream_t st, int num_sms, const char** why);
 int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
                       const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
                       void* out, int out_f32, int* err, cudaStream_t st, int num_sms,
@@ -125,9 +125,9 @@ extern "C" int gl_gmm_fp8_act_fwd_noalloc(const void* lhs, const void* b_q, cons
   }
   unsigned char* q = d.base + kErrBytes;
   float* s = reinterpret_cast<float*>(d.base + kErrBytes + kQBytes);
-  if (gl_launch_quant_act(lhs, M, K, q, s, st, d.num_sms) != 0)
-    return gl_set_error_message(GL_ELAUNCH, "gl_gmm_fp8_act_fwd_noalloc: quantiser launch failed");
   const char* why = "";
+  if (gl_launch_quant_act(lhs, M, K, q, s, err, st, d.num_sms, &why) != 0)
+    return gl_set_error_message(GL_ELAUNCH, (std::string("gl_gmm_fp8_act_fwd_noalloc: quantiser: ") + why).c_str());
   const int rc = gl_launch_gmm_fp8(q, s, b_q, b_s, group_sizes, G, M, K, N, out,
                                    out_dtype == GL_OUT_F32, err, st, d.num_sms, &why);
   if (rc == -1) return gl_set_error_message(GL_EINVAL, (std::string("gl_gmm_fp8_act_fwd_noalloc: ") + why).c_str());

@@ -5,9 +5,28 @@
 // replace):
 //   s = absmax(block) / 448        (1.0 when the block is all zeros)
 //   q = cvt.rn.satfinite.e4m3(x / s)
-// The division is IEEE round-to-nearest (this file must not be compiled with
-// fast-math), so the result is bit-identical to the CPU oracle.
+// x / s is the correctly rounded IEEE quotient (this file must not be compiled
+// with fast-math), so the result is bit-identical to the CPU oracle.  It is
+// computed per element from the block's correctly rounded reciprocal with
+// Markstein's FMA correction instead of a full division per element, which
+// made the weight quantiser issue-bound rather than HBM-bound.
+//
+// Data movement (both quantisers): a persistent CTA per SM takes every
+// gridDim-th 128 x 128 tile, so the CTAs running together read neighbouring
+// tiles (whole rows of the operand at a time).  One producer warp streams the
+// bf16 tiles into a shared-memory ring with TMA (32 KB per tile; up to 96 KB
+// per CTA for activations with two CTAs per SM, 128 KB for weights with
+// one); 16 consumer warps quantise out of shared memory
+// and store the e4m3 rows with coalesced 8-byte stores.  Stages are handed
+// back through per-stage mbarriers, so consumers work on different tiles at
+// the same time and no CTA-wide barrier sits on the tile path:
+//   activations: every warp owns 8 rows of every tile (a 1x128 block is one
+//                row of a tile, reduced within a half-warp);
+//   weights:     the consumer warps form 4 groups of 4 warps, group g takes
+//                the CTA's tiles g, g+4, ...; a group reduces the 128x128
+//                block maximum over one named barrier, then quantises.
 #include "common.cuh"
+#include "tmap.h"
 
 namespace gl {
 
@@ -18,116 +37,305 @@ __device__ __forceinline__ uint16_t cvt_e4m3x2(float lo, float hi) {
   return r;
 }
 
-__device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __uint_as_float(w[i] << 16);
-    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+// Division by a block scale.  With y = RN(1/s) (one IEEE division per
+// block), q = RN(x*y) lies within one ulp of x/s, the residual r = x - q*s is
+// exact in one FMA, and RN(q + r*y) is the correctly rounded quotient
+// (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Develop. 34(1), 1990).  The residual is
+// exact only while it stays above the subnormal range: with s >= 2^-64 every
+// element whose quotient can reach a non-zero e4m3 value has |x| >= 2^-74, far
+// from it.  Blocks with smaller (or non-finite) scales take the plain
+// division.  A quotient by s > 0 has the sign of x, which copysign restores
+// for x = -0.  The arithmetic runs on packed f32x2 FMAs.  Tests compare this
+// path with IEEE division for every finite bf16 block maximum and every bf16
+// element value.
+struct BlockDiv {
+  float s, y;
+  bool fast;
+  __device__ __forceinline__ explicit BlockDiv(float scale) : s(scale) {
+    fast = scale >= 0x1p-64f && scale <= 3.40282347e38f;
+    y = 1.0f / scale;
   }
+};
+
+__device__ __forceinline__ float2 bf16x2_to_f32x2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
 
-__device__ __forceinline__ uint2 quant8(const float (&f)[8], float s) {
+// Eight bf16 values (one 16-byte chunk) -> eight e4m3 bytes.
+__device__ __forceinline__ uint2 quant8(const uint4& u, const BlockDiv& d) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
   uint32_t p[4];
+  if (d.fast) {
+    const float2 y2 = make_float2(d.y, d.y), ns2 = make_float2(-d.s, -d.s);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) p[i] = cvt_e4m3x2(f[2 * i] / s, f[2 * i + 1] / s);
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = bf16x2_to_f32x2(w[i]);
+      const float2 q = __fmul2_rn(x, y2);
+      const float2 r = __ffma2_rn(q, ns2, x);
+      const float2 v = __ffma2_rn(r, y2, q);
+      p[i] = cvt_e4m3x2(copysignf(v.x, x.x), copysignf(v.y, x.y));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = bf16x2_to_f32x2(w[i]);
+      p[i] = cvt_e4m3x2(x.x / d.s, x.y / d.s);
+    }
+  }
   return make_uint2(p[0] | (p[1] << 16), p[2] | (p[3] << 16));
+}
+
+// max |x| over one chunk, on packed bf16 (exact: the maximum is one of the
+// values).
+__device__ __forceinline__ float absmax8(const uint4& u) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  const __nv_bfloat162 m = __hmax2(__hmax2(__habs2(h[0]), __habs2(h[1])),
+                                   __hmax2(__habs2(h[2]), __habs2(h[3])));
+  return fmaxf(__bfloat162float(m.x), __bfloat162float(m.y));
 }
 
 __device__ __forceinline__ float scale_of(float amax) { return amax > 0.f ? amax / 448.f : 1.f; }
 
-// One 1x128 block per half-warp (16 lanes x 8 bf16).  Both half-warps of a
-// warp always iterate together so the full-mask shuffles stay converged.
-__global__ void __launch_bounds__(256) quant_act_1x128_kernel(const __nv_bfloat16* __restrict__ x,
-                                                              int64_t M, int64_t K,
-                                                              uint8_t* __restrict__ q,
-                                                              float* __restrict__ s) {
-  const int64_t KB = K / 128;
-  const int64_t nblocks = M * KB;
-  const int lane = threadIdx.x & 31;
-  const int half = lane >> 4, sub = lane & 15;
-  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  for (int64_t pair = warp; pair * 2 < nblocks; pair += nwarps) {
-    const int64_t blk = pair * 2 + half;
-    const bool valid = blk < nblocks;
-    const int64_t m = valid ? blk / KB : 0, kb = valid ? blk % KB : 0;
-    const int64_t off = m * K + kb * 128 + sub * 8;
-    uint4 u = make_uint4(0, 0, 0, 0);
-    if (valid) u = __ldg(reinterpret_cast<const uint4*>(x + off));
-    float f[8];
-    bf16x8_to_f32(u, f);
-    float amax = 0.f;
+namespace quant {
+
+// Ring depth and CTAs per SM.  Activations: all consumer warps take every
+// tile in order, 3 stages, two CTAs per SM.  Weights: tile i goes to group
+// i % W_GROUPS and to stage i % W_STAGES; W_STAGES is a multiple of W_GROUPS,
+// so every stage is only ever used by one group, which therefore waits for
+// that stage's phases in order (a waiter that skipped a phase would see the
+// stage as full too early).
+template <bool kWeight> struct Ring;
+template <> struct Ring<false> { static constexpr int STAGES = 3, CTAS_PER_SM = 2; };
+template <> struct Ring<true> { static constexpr int STAGES = 4, CTAS_PER_SM = 1; };
+constexpr int CONSUMER_WARPS = 16;
+constexpr int THREADS = 32 * (CONSUMER_WARPS + 1);  // + producer warp
+constexpr int W_GROUPS = 4;                          // weight quantiser: tile groups
+constexpr int W_GROUP_WARPS = CONSUMER_WARPS / W_GROUPS;
+constexpr uint32_t IN_BYTES = 128 * 128 * 2;
+static_assert(Ring<true>::STAGES % W_GROUPS == 0, "a weight stage must belong to one group");
+template <bool kWeight>
+struct Layout {
+  static constexpr int STAGES = Ring<kWeight>::STAGES;
+  static constexpr uint32_t OFF_BAR = STAGES * IN_BYTES;
+  static constexpr uint32_t OFF_RED = OFF_BAR + 2 * STAGES * 8;
+  static constexpr uint32_t OFF_FLAG = OFF_RED + W_GROUPS * 2 * W_GROUP_WARPS * 4;
+  static constexpr uint32_t SMEM_BYTES = OFF_FLAG + 16 + 1024;  // + slack for 1 KB alignment
+};
+
+struct Args {
+  uint8_t* q;
+  float* s;
+  int* err;
+  int64_t rows;  // activations: M; weights: G*K
+  int64_t K;
+  int64_t N;     // weights only
+  int64_t tiles;
+};
+
+// Tile -> (x, y) element coordinates of its top-left corner.
+//   activations: tiles are (128-row slab, K block), K block fastest;
+//   weights:     tiles are (group, K block, N block), N block fastest.
+template <bool kWeight>
+__device__ __forceinline__ void tile_xy(const Args& a, int64_t t, int32_t& x, int32_t& y) {
+  if (kWeight) {
+    const int64_t NB = a.N / 128, KB = a.K / 128;
+    const int64_t g = t / (KB * NB), kb = (t / NB) % KB, nb = t % NB;
+    x = static_cast<int32_t>(nb * 128);
+    y = static_cast<int32_t>(g * a.K + kb * 128);
+  } else {
+    const int64_t KB = a.K / 128;
+    x = static_cast<int32_t>((t % KB) * 128);
+    y = static_cast<int32_t>((t / KB) * 128);
+  }
+}
+
+// OR of `v` over the `count` threads of named barrier `id` (a barrier).
+__device__ __forceinline__ bool bar_or(int id, int count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
+template <bool kWeight>
+__global__ void __launch_bounds__(THREADS, Ring<kWeight>::CTAS_PER_SM)
+    quant_kernel(const __grid_constant__ CUtensorMap tm_in, const Args a) {
+  using L = Layout<kWeight>;
+  constexpr int STAGES = L::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
+  int* abort_flag = reinterpret_cast<int*>(smem + L::OFF_FLAG);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // local tile i is global tile blockIdx.x + i * gridDim.x
+  const int64_t n = a.tiles > blockIdx.x ? (a.tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tm_in);
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kWeight ? W_GROUP_WARPS : CONSUMER_WARPS);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const Abort ab{abort_flag, a.err};
+
+  if (warp == CONSUMER_WARPS) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      int64_t i = 0;
+      for (; i < n; ++i) {
+        const int st = static_cast<int>(i % STAGES);
+        if (!mbar_wait(&empty[st], (static_cast<uint32_t>(i / STAGES) & 1u) ^ 1u, ab)) break;
+        int32_t x, y;
+        tile_xy<kWeight>(a, blockIdx.x + i * gridDim.x, x, y);
+        mbar_arrive_expect_tx(&full[st], IN_BYTES);
+        tma_load_2d(smem + st * IN_BYTES, &tm_in, &full[st], x, y);
+      }
+      if (i < n) {
+        // Aborted: let the loads in flight land before the CTA can exit.
+        for (int64_t k = i > STAGES ? i - STAGES : 0; k < i; ++k) {
+          const uint64_t w0 = global_ns();
+          while (!mbar_try_wait(&full[k % STAGES], static_cast<uint32_t>(k / STAGES) & 1u) &&
+                 global_ns() - w0 < 100000000ull) {
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  if (kWeight) {
+    // ------------------------------------------- weights: groups of 4 warps
+    const int grp = warp / W_GROUP_WARPS, gw = warp % W_GROUP_WARPS;
+    const int tg = threadIdx.x - grp * W_GROUP_WARPS * 32;  // 0..127
+    const int64_t NB = a.N / 128;
+    int par = 0;
+    for (int64_t i = grp; i < n; i += W_GROUPS, par ^= 1) {
+      const int st = static_cast<int>(i % STAGES);
+      const bool ok = mbar_wait(&full[st], static_cast<uint32_t>(i / STAGES) & 1u, ab);
+      const uint4* in = reinterpret_cast<const uint4*>(smem + st * IN_BYTES);
+      float m = 0.f;
+#pragma unroll 8
+      for (int j = 0; j < 16; ++j) m = fmaxf(m, absmax8(in[tg + 128 * j]));
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+      for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float* r = red + (grp * 2 + par) * W_GROUP_WARPS;
+      if (lane == 0) r[gw] = m;
+      if (bar_or(1 + grp, W_GROUP_WARPS * 32, !ok || *static_cast<volatile int*>(abort_flag))) break;
 #pragma unroll
-    for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float sc = scale_of(amax);
-    if (valid) {
-      *reinterpret_cast<uint2*>(q + off) = quant8(f, sc);
-      if (sub == 0) s[m * KB + kb] = sc;
+      for (int w = 0; w < W_GROUP_WARPS; ++w) m = fmaxf(m, r[w]);
+      const float sc = scale_of(m);
+      const BlockDiv div(sc);
+      int32_t x, y;
+      tile_xy<kWeight>(a, blockIdx.x + i * gridDim.x, x, y);
+      uint8_t* qbase = a.q + static_cast<int64_t>(y) * a.N + x + (tg & 15) * 8;
+#pragma unroll 4
+      for (int j = 0; j < 16; ++j) {
+        const int row = (tg >> 4) + 8 * j;
+        *reinterpret_cast<uint2*>(qbase + static_cast<int64_t>(row) * a.N) = quant8(in[tg + 128 * j], div);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      if (tg == 0) a.s[(y / 128) * NB + x / 128] = sc;  // s[g, kb, nb]; y / 128 = g * KB + kb
+    }
+  } else {
+    // ------------------------------- activations: every warp owns 8 rows
+    // Pass p covers rows 8 * warp + 4 p .. + 3, eight lanes per row; lane l
+    // of a row takes its 16-byte chunks l and l + 8 (conflict-free: the 8
+    // lanes of a row read 128 contiguous bytes per load).
+    const int64_t KB = a.K / 128;
+    const int rsub = lane >> 3, l8 = lane & 7;
+    for (int64_t i = 0; i < n; ++i) {
+      const int st = static_cast<int>(i % STAGES);
+      if (!mbar_wait(&full[st], static_cast<uint32_t>(i / STAGES) & 1u, ab)) break;
+      const uint4* in = reinterpret_cast<const uint4*>(smem + st * IN_BYTES);
+      int32_t x, y;
+      tile_xy<kWeight>(a, blockIdx.x + i * gridDim.x, x, y);
+      uint4 u[2][2];
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass)
+#pragma unroll
+        for (int k = 0; k < 2; ++k) u[pass][k] = in[(warp * 8 + 4 * pass + rsub) * 16 + l8 + 8 * k];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        float m = fmaxf(absmax8(u[pass][0]), absmax8(u[pass][1]));
+#pragma unroll
+        for (int o = 4; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float sc = scale_of(m);
+        const BlockDiv div(sc);
+        const int64_t row = y + warp * 8 + 4 * pass + rsub;
+        if (row < a.rows) {
+          uint8_t* qrow = a.q + row * a.K + x;
+#pragma unroll
+          for (int k = 0; k < 2; ++k)
+            *reinterpret_cast<uint2*>(qrow + (l8 + 8 * k) * 8) = quant8(u[pass][k], div);
+          if (l8 == 0) a.s[row * KB + x / 128] = sc;
+        }
+      }
     }
   }
 }
 
-// One 128x128 block of one group per CTA (256 threads; thread t owns the
-// 16-byte column chunk t%16 of rows (t/16)*8 .. (t/16)*8+7).
-__global__ void __launch_bounds__(256) quant_w_128x128_kernel(const __nv_bfloat16* __restrict__ w,
-                                                              int64_t G, int64_t K, int64_t N,
-                                                              uint8_t* __restrict__ q,
-                                                              float* __restrict__ s) {
-  const int64_t KB = K / 128, NB = N / 128;
-  const int64_t nblk = G * KB * NB;
-  __shared__ float red[8];
-  const int t = threadIdx.x, c = t & 15, rg = t >> 4;
-  for (int64_t b = blockIdx.x; b < nblk; b += gridDim.x) {
-    const int64_t g = b / (KB * NB), kb = (b / NB) % KB, nb = b % NB;
-    const int64_t base = (g * K + kb * 128 + rg * 8) * N + nb * 128 + c * 8;
-    float f[8][8];
-    float amax = 0.f;
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(w + base + r * N));
-      bf16x8_to_f32(u, f[r]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[r][i]));
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if ((t & 31) == 0) red[t >> 5] = amax;
-    __syncthreads();
-    amax = red[0];
-#pragma unroll
-    for (int i = 1; i < 8; ++i) amax = fmaxf(amax, red[i]);
-    __syncthreads();  // red[] is rewritten by the next block
-    const float sc = scale_of(amax);
-#pragma unroll
-    for (int r = 0; r < 8; ++r) *reinterpret_cast<uint2*>(q + base + r * N) = quant8(f[r], sc);
-    if (t == 0) s[(g * KB + kb) * NB + nb] = sc;
-  }
-}
-
+}  // namespace quant
 }  // namespace gl
 
-// Host launchers (called from capi.cu).
-int gl_launch_quant_act(const void* x, int64_t M, int64_t K, void* q, float* s,
-                        cudaStream_t st, int num_sms) {
-  const int64_t pairs = (M * (K / 128) + 1) / 2;  // one pair per warp-iteration
-  const int64_t want = (pairs + 7) / 8;           // 8 warps per CTA
-  const int grid = static_cast<int>(want < static_cast<int64_t>(num_sms) * 16
-                                        ? (want > 0 ? want : 1)
-                                        : static_cast<int64_t>(num_sms) * 16);
-  gl::quant_act_1x128_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), M, K,
-                                                   static_cast<uint8_t*>(q), s);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+namespace {
+
+template <bool kWeight>
+int launch_quant(const void* in, void* q, float* s, int* err, int64_t rows, int64_t K, int64_t N,
+                 cudaStream_t st, int num_sms, const char** why) {
+  using namespace gl::quant;
+  const int64_t inner = kWeight ? N : K;
+  CUtensorMap tm_in;
+  if (!gl_make_tmap_2d(&tm_in, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, in, inner, rows, inner, 128, 128,
+                       CU_TENSOR_MAP_SWIZZLE_NONE, why))
+    return -1;
+  Args a;
+  a.q = static_cast<uint8_t*>(q);
+  a.s = s;
+  a.err = err;
+  a.rows = rows;
+  a.K = K;
+  a.N = N;
+  a.tiles = kWeight ? (rows / 128) * (N / 128) : ((rows + 127) / 128) * (K / 128);
+  const void* fn = reinterpret_cast<const void*>(quant_kernel<kWeight>);
+  constexpr uint32_t smem_bytes = Layout<kWeight>::SMEM_BYTES;
+  if (!gl_set_smem_attr(fn, 0, static_cast<int>(smem_bytes), why)) return -2;
+  const int64_t slots = static_cast<int64_t>(num_sms) * Ring<kWeight>::CTAS_PER_SM;
+  const int64_t grid = a.tiles < slots ? a.tiles : slots;
+  quant_kernel<kWeight><<<static_cast<unsigned>(grid > 0 ? grid : 1), THREADS, smem_bytes, st>>>(
+      tm_in, a);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return -2;
+  }
+  return 0;
 }
 
-int gl_launch_quant_w(const void* w, int64_t G, int64_t K, int64_t N, void* q, float* s,
-                      cudaStream_t st, int num_sms) {
-  const int64_t nblk = G * (K / 128) * (N / 128);
-  const int64_t cap = static_cast<int64_t>(num_sms) * 8;
-  const int grid = static_cast<int>(nblk < cap ? (nblk > 0 ? nblk : 1) : cap);
-  gl::quant_w_128x128_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), G, K, N,
-                                                   static_cast<uint8_t*>(q), s);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}  // namespace
+
+// Host launchers (called from capi.cu and noalloc.cu).  0 = launched,
+// -1 = operand rejected by the tensor-map encoder, -2 = launch failure.
+int gl_launch_quant_act(const void* x, int64_t M, int64_t K, void* q, float* s, int* err,
+                        cudaStream_t st, int num_sms, const char** why) {
+  return launch_quant<false>(x, q, s, err, M, K, 0, st, num_sms, why);
+}
+
+int gl_launch_quant_w(const void* w, int64_t G, int64_t K, int64_t N, void* q, float* s, int* err,
+                      cudaStream_t st, int num_sms, const char** why) {
+  return launch_quant<true>(w, q, s, err, G * K, K, N, st, num_sms, why);
 }
