@@ -18,19 +18,19 @@
 // once and o (+ the final state) written once.
 //
 // One CTA per (batch, head, V slice of width VS), 512 threads:
-//   warp 0        TMA producer (g chunk, then q, k, v chunk; 2-stage rings)
+//   warp 0        TMA producer of q, k, v (3- or 2-stage ring)
 //   warp 1        tcgen05.mma issuer (dataflow order: A/S of chunk n+1, Qs H_n
 //                 as soon as H_n is stored, P V as soon as P_n is written)
 //   warp 2        TMEM allocator, then TMA producer of g
-//   warps 4-11    gating (thread = 2 keys x 16 tokens): chunk-local cumsum
-//                 of the gate (quarter prefixes exchanged through shared
+//   warps 4-11    gating (warp = 8 tokens, lane = 4 keys): chunk-local cumsum
+//                 of the gate (per-warp prefixes exchanged through shared
 //                 memory), Qs, Kg in place, e^{G_last}; then the O epilogue
 //                 of the chunk two behind (TMEM -> bf16 -> HBM)
 //   warps 12-15   state warpgroup: A -> tril -> bf16 P, state update
 //                 (thread = key row, VS fp32 columns in registers)
-// Buffers: g, q, k, v double-buffered; A and O double-buffered in TMEM, S
-// single; P and the bf16 state copy H single-buffered (rewritten only after
-// O_n completed).
+// Buffers: g double-buffered, q/k/v in a 3-stage (VS = 64) or 2-stage ring;
+// A and O double-buffered in TMEM, S double-buffered when VS = 64; P and the
+// bf16 state copy H single-buffered (rewritten only after O_n completed).
 #include "common.cuh"
 
 namespace gl {
@@ -40,12 +40,18 @@ constexpr int C = 64, KD = 128, NUM_THREADS = 512;
 constexpr int GATE_WARPS = 8, STATE_WARPS = 4;
 // Register split (launch: 512 x 128): control warpgroup 56, the two gating
 // warpgroups keep 128, the state warpgroup rises to 216.
-constexpr int REG_CTRL = 40, REG_STATE = 216;
+constexpr int REG_CTRL = 48, REG_STATE = 208;
 static_assert(128 * REG_CTRL + 256 * 128 + 128 * REG_STATE <= NUM_THREADS * 128,
               "register split exceeds the launch allocation");
 
 template <int VS>
 struct Cfg {
+  // q/k/v ring depth: a stage is released only once O of its chunk has
+  // completed, so with two stages the gating of chunk n+2 waits for the whole
+  // A -> P -> O chain of chunk n; VS = 64 leaves room for three.  The S
+  // accumulator is double-buffered in TMEM when its columns fit (VS = 64).
+  static constexpr int QS = VS == 64 ? 3 : 2;
+  static constexpr int NS = VS == 64 ? 2 : 1;
   static constexpr int V_BOXES = VS / 64;
   static constexpr uint32_t Q_BYTES = C * KD * 2;          // 16 KB (2 boxes of 64 features)
   static constexpr uint32_t V_BYTES = C * VS * 2;          // 8 / 16 KB
@@ -53,18 +59,20 @@ struct Cfg {
   static constexpr uint32_t P_BYTES = C * C * 2;           // 8 KB
   static constexpr uint32_t H_BYTES = KD * VS * 2;         // 16 / 32 KB
   static constexpr uint32_t OFF_Q = 0;
-  static constexpr uint32_t OFF_K = OFF_Q + 2 * Q_BYTES;
-  static constexpr uint32_t OFF_V = OFF_K + 2 * Q_BYTES;
-  static constexpr uint32_t OFF_G = OFF_V + 2 * V_BYTES;
+  static constexpr uint32_t OFF_K = OFF_Q + QS * Q_BYTES;
+  static constexpr uint32_t OFF_V = OFF_K + QS * Q_BYTES;
+  static constexpr uint32_t OFF_G = OFF_V + QS * V_BYTES;
   static constexpr uint32_t OFF_P = OFF_G + 2 * G_BYTES;
   static constexpr uint32_t OFF_H = OFF_P + P_BYTES;
   static constexpr uint32_t OFF_DEC = OFF_H + H_BYTES;      // 2 x 128 floats
-  static constexpr uint32_t OFF_PART = OFF_DEC + 2 * KD * 4;  // [2][4][64] float2
-  static constexpr uint32_t OFF_BAR = OFF_PART + 2 * 4 * 64 * 8;
-  static constexpr uint32_t OFF_MISC = OFF_BAR + 256;
+  static constexpr uint32_t OFF_PART = OFF_DEC + 2 * KD * 4;  // [2][8 warps][32 lanes] float4
+  static constexpr uint32_t OFF_BAR = OFF_PART + 2 * 8 * 32 * 16;
+  static constexpr uint32_t OFF_MISC = OFF_BAR + 512;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;
-  // TMEM columns: A0, A1 [0,128), O0, O1 [128,128+2VS), S [128+2VS, 128+3VS)
+  // TMEM columns: A0, A1 [0,128), O0, O1 [128,128+2VS), S0 (, S1) from 128+2VS
   static constexpr uint32_t COL_A = 0, COL_O = 128, COL_S = 128 + 2 * VS;
+  static_assert(COL_S + NS * VS <= 512, "TMEM columns");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t IDESC_A = idesc(1, 1, 1, 0, 0, 64, 64);    // bf16, K-major x K-major
   static constexpr uint32_t IDESC_S = idesc(1, 1, 1, 1, 1, 128, VS);  // MN-major x MN-major
@@ -78,31 +86,45 @@ struct Params {
   float* ht;             // [B,H,K,V] or null
   int* err;
   float scale;
+  float log2_scale;  // log2(scale) when scale > 0 (folded into the exponent), else 0
+  int scale_apart;   // 1: scale <= 0 or not finite, applied as a separate multiply
   int B, T, H, nsplit;
   int has_g;
 };
 
 // Barrier indices ([2] = one per buffer).
 enum {
-  B_QKV_FULL = 0,    // [2] TMA -> gating
-  B_QKV_EMPTY = 2,   // [2] O_n committed -> TMA
-  B_G_FULL = 4,      // [2] TMA -> gating
-  B_G_EMPTY = 6,     // [2] gating -> TMA
-  B_PREP = 8,        // [2] gating -> MMA
-  B_DEC_FULL = 10,   // [2] gating -> state
-  B_DEC_EMPTY = 12,  // [2] state -> gating
-  B_A_FULL = 14,     // [2] MMA A_n committed -> P epilogue
-  B_A_EMPTY = 16,    // [2] P epilogue -> MMA
-  B_O_FULL = 18,     // [2] MMA O_n committed -> state
-  B_O_EMPTY = 20,    // [2] O read (gating warps) -> MMA
-  B_S_FULL = 22,     // MMA S_n committed -> state
-  B_S_EMPTY = 23,    // state read S -> MMA
-  B_P_FULL = 24,     // P written -> MMA
-  B_H_FULL = 25,     // H_n written -> MMA
-  B_DRAIN = 26,
-  B_GSYNC = 27,      // [2] gating quarter sums written
-  NUM_BARS = 29
+  B_QKV_FULL = 0,    // [QS] TMA -> gating
+  B_QKV_EMPTY = 3,   // [QS] O_n committed -> TMA
+  B_G_FULL = 6,      // [2] TMA -> gating
+  B_G_EMPTY = 8,     // [2] gating -> TMA
+  B_PREP = 10,       // [2] gating -> MMA
+  B_DEC_FULL = 12,   // [2] gating -> state
+  B_DEC_EMPTY = 14,  // [2] state -> gating
+  B_A_FULL = 16,     // [2] MMA A_n committed -> P epilogue
+  B_A_EMPTY = 18,    // [2] P epilogue -> MMA
+  B_O_FULL = 20,     // [2] MMA O_n committed -> state
+  B_O_EMPTY = 22,    // [2] O read (gating warps) -> MMA
+  B_S_FULL = 24,     // [NS] MMA S_n committed -> state
+  B_S_EMPTY = 26,    // [NS] state read S -> MMA
+  B_P_FULL = 28,     // P written -> MMA
+  B_H_FULL = 29,     // H_n written -> MMA
+  B_DRAIN = 30,
+  B_GSYNC = 31,      // [2] gating quarter sums written
+  NUM_BARS = 33
 };
+static_assert(NUM_BARS * 8 <= 512, "barrier area");
+
+// 2^x with the hardware approximation (the same unit __expf uses).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float2 bf16x2_f32x2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
 
 // Offset of bf16 element (row, col) in a K-major, 128B-swizzled tile made of
 // 64-column atoms stacked `atom_stride` bytes apart (rows 128 B apart).
@@ -142,9 +164,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     prefetch_tmap(&tm_v);
     if (p.has_g) prefetch_tmap(&tm_g);
   } else if (warp == 1 && lane == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < CF::QS; ++i) {
       mbar_init(&bar[B_QKV_FULL + i], 1);
       mbar_init(&bar[B_QKV_EMPTY + i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&bar[B_G_FULL + i], 1);
       mbar_init(&bar[B_G_EMPTY + i], GATE_WARPS);
       mbar_init(&bar[B_PREP + i], GATE_WARPS);
@@ -156,8 +180,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&bar[B_O_FULL + i], 1);
       mbar_init(&bar[B_O_EMPTY + i], GATE_WARPS);
     }
-    mbar_init(&bar[B_S_FULL], 1);
-    mbar_init(&bar[B_S_EMPTY], STATE_WARPS);
+    for (int i = 0; i < CF::NS; ++i) {
+      mbar_init(&bar[B_S_FULL + i], 1);
+      mbar_init(&bar[B_S_EMPTY + i], STATE_WARPS);
+    }
     mbar_init(&bar[B_P_FULL], STATE_WARPS);
     mbar_init(&bar[B_H_FULL], STATE_WARPS);
     mbar_init(&bar[B_DRAIN], 1);
@@ -178,9 +204,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------- TMA q, k, v
     if (lane == 0) {
       for (int n = 0; n < NT; ++n) {
-        const int s = n & 1;
+        const int s = n % CF::QS;
         const int tok = tok0 + n * C;
-        if (!mbar_wait(&bar[B_QKV_EMPTY + s], ((n >> 1) & 1) ^ 1, ab)) break;
+        if (!mbar_wait(&bar[B_QKV_EMPTY + s], ((n / CF::QS) & 1) ^ 1, ab)) break;
         mbar_arrive_expect_tx(&bar[B_QKV_FULL + s], 2 * CF::Q_BYTES + CF::V_BYTES);
         uint8_t* qd = smem + CF::OFF_Q + s * CF::Q_BYTES;
         uint8_t* kd = smem + CF::OFF_K + s * CF::Q_BYTES;
@@ -199,15 +225,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
     // ----------------------------------------------------------------- MMA
     if (lane == 0) {
+      constexpr int QS = CF::QS, NS = CF::NS;
       const uint32_t p_addr = s_base + CF::OFF_P;
       const uint32_t h_addr = s_base + CF::OFF_H;
       // A_m = Qs Kg^T (M=64 query rows, N=64 key rows, K=128 features) into
       // TMEM buffer m%2; S_m = Kg^T V (M=128 features, N=VS, K=64 tokens).
       auto issue_a_s = [&](int m) {
-        const int s = m & 1;
-        const uint32_t q_addr = s_base + CF::OFF_Q + s * CF::Q_BYTES;
-        const uint32_t k_addr = s_base + CF::OFF_K + s * CF::Q_BYTES;
-        const uint32_t v_addr = s_base + CF::OFF_V + s * CF::V_BYTES;
+        const int s = m & 1, st = m % QS;
+        const uint32_t q_addr = s_base + CF::OFF_Q + st * CF::Q_BYTES;
+        const uint32_t k_addr = s_base + CF::OFF_K + st * CF::Q_BYTES;
+        const uint32_t v_addr = s_base + CF::OFF_V + st * CF::V_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t koff = (kk >> 2) * 8192 + (kk & 3) * 32;
@@ -215,18 +242,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   sdesc(k_addr + koff, 16, 1024, kSwizzle128B), CF::IDESC_A, kk > 0);
         }
         tc_commit(&bar[B_A_FULL + s]);
+        const int sb = m % NS;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          mma_f16(tmem + CF::COL_S, sdesc(k_addr + kk * 2048, 8192, 1024, kSwizzle128B),
+          mma_f16(tmem + CF::COL_S + sb * VS, sdesc(k_addr + kk * 2048, 8192, 1024, kSwizzle128B),
                   sdesc(v_addr + kk * 2048, 8192, 1024, kSwizzle128B), CF::IDESC_S, kk > 0);
         }
-        tc_commit(&bar[B_S_FULL]);
+        tc_commit(&bar[B_S_FULL + sb]);
       };
       // O_n (TMEM buffer n%2) = Qs H_n (issued once H_n is stored) + P V
       // (issued once P_n is written); the second part frees the q/k/v stage.
       auto issue_o_h = [&](int n) {
         const int s = n & 1;
-        const uint32_t q_addr = s_base + CF::OFF_Q + s * CF::Q_BYTES;
+        const uint32_t q_addr = s_base + CF::OFF_Q + (n % QS) * CF::Q_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t koff = (kk >> 2) * 8192 + (kk & 3) * 32;
@@ -236,14 +264,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       };
       auto issue_o_p = [&](int n) {
         const int s = n & 1;
-        const uint32_t v_addr = s_base + CF::OFF_V + s * CF::V_BYTES;
+        const uint32_t v_addr = s_base + CF::OFF_V + (n % QS) * CF::V_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           mma_f16(tmem + CF::COL_O + s * VS, sdesc(p_addr + kk * 32, 16, 1024, kSwizzle128B),
                   sdesc(v_addr + kk * 2048, 8192, 1024, kSwizzle128B), CF::IDESC_O, 1);
         }
         tc_commit(&bar[B_O_FULL + s]);
-        tc_commit(&bar[B_QKV_EMPTY + s]);
+        tc_commit(&bar[B_QKV_EMPTY + n % QS]);
       };
       // Dataflow issue.  na: next chunk for A/S (needs its gating, its A
       // buffer free and the previous S read); nh: next chunk for Qs H (needs
@@ -253,24 +281,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t spins = 0;
       while (no < NT) {
         bool progressed = false;
-        if (no < nh && mbar_try_wait(&bar[B_P_FULL], no & 1)) {
+        if (no < nh && mbar_test(&bar[B_P_FULL], no & 1)) {
           tc_fence_after();
           issue_o_p(no);
           ++no;
           progressed = true;
         }
-        if (nh < na && nh == no && mbar_try_wait(&bar[B_H_FULL], nh & 1) &&
-            mbar_try_wait(&bar[B_O_EMPTY + (nh & 1)], ((nh >> 1) & 1) ^ 1)) {
+        if (nh < na && nh == no && mbar_test(&bar[B_H_FULL], nh & 1) &&
+            mbar_test(&bar[B_O_EMPTY + (nh & 1)], ((nh >> 1) & 1) ^ 1)) {
           tc_fence_after();
           issue_o_h(nh);
           ++nh;
           progressed = true;
         }
-        if (na < NT && na <= no + 1) {
+        if (na < NT && na <= no + QS - 1) {
           const int s = na & 1;
           const uint32_t ph2 = (na >> 1) & 1;
-          if (mbar_try_wait(&bar[B_PREP + s], ph2) && mbar_try_wait(&bar[B_A_EMPTY + s], ph2 ^ 1) &&
-              mbar_try_wait(&bar[B_S_EMPTY], (na & 1) ^ 1)) {
+          if (mbar_test(&bar[B_PREP + s], ph2) && mbar_test(&bar[B_A_EMPTY + s], ph2 ^ 1) &&
+              mbar_test(&bar[B_S_EMPTY + na % NS], ((na / NS) & 1) ^ 1)) {
             tc_fence_after();
             issue_a_s(na);
             ++na;
@@ -280,7 +308,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (progressed) {
           t0 = global_ns();
           spins = 0;
-        } else if ((++spins & 255u) == 0) {
+        } else if ((++spins & 255u) != 0) {
+          __nanosleep(20);  // leave the issue slots to the gating warps
+        } else {
           if (*abort_flag) break;
           if (global_ns() - t0 > kWaitNs) {
             *abort_flag = 1;
@@ -312,15 +342,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
   } else if (warp >= 4 && warp < 4 + GATE_WARPS) {
     // ---------------------------------------------------------- gating
-    // thread = (key pair kp, token quarter tq): keys 2kp, 2kp+1, tokens
-    // 16tq .. 16tq+15.  Each thread sums the gate over its 16 tokens, the
-    // quarter sums are exchanged through shared memory, and the chunk-local
-    // cumsum continues from the sum of the preceding quarters.
-    const int gid = threadIdx.x - 128;
-    const int kp = gid & 63, tq = gid >> 6;
+    // Warp gw = warp - 4 takes tokens 8 gw .. 8 gw + 7 of the chunk, lane l
+    // keys 4 l .. 4 l + 3 (16-byte gate loads, 8-byte q / k accesses).  Each
+    // warp sums the gate over its 8 tokens, the per-warp sums are exchanged
+    // through shared memory, and the chunk-local cumsum continues from the
+    // sum of the preceding warps.
+    const int gw = warp - 4;
     const float gamma = p.has_g ? 0.f : __ldg(p.g_gamma + h);
-    const float scale = p.scale;
-    const uint32_t atom = (kp >> 5) * 8192u, chunk = (kp & 31) >> 2, sub = (kp & 3) * 4u;
+    constexpr float kLog2e = 1.4426950408889634f;
+    const float log2_scale = p.log2_scale;
+    // q / k tiles: K-major, 128B-swizzled, 64-feature atoms 8 KB apart.
+    const uint32_t qk_atom = static_cast<uint32_t>(lane >> 4) * 8192u;
+    const uint32_t qk_chunk = static_cast<uint32_t>(lane & 15) >> 1, qk_sub = (lane & 1) * 8u;
     // O epilogue of chunk m (run two chunks behind the gating, when O_m is
     // long complete): this warp reads TMEM lane quadrant warp%4, i.e. rows
     // 16*quad .. 16*quad+15 of the M=64 accumulator, columns half*VS/2 ..
@@ -359,75 +392,81 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int s = n & 1;
       const uint32_t ph2 = (n >> 1) & 1;
       if (p.has_g && !mbar_wait(&bar[B_G_FULL + s], ph2, ab)) { gok = false; break; }
-      if (!mbar_wait(&bar[B_QKV_FULL + s], ph2, ab)) { gok = false; break; }
+      if (!mbar_wait(&bar[B_QKV_FULL + n % CF::QS], (n / CF::QS) & 1, ab)) { gok = false; break; }
       if (!mbar_wait(&bar[B_DEC_EMPTY + s], ph2 ^ 1, ab)) { gok = false; break; }
-      const float2* gsm = reinterpret_cast<const float2*>(smem + CF::OFF_G + s * CF::G_BYTES) + kp;
-      uint8_t* qs = smem + CF::OFF_Q + s * CF::Q_BYTES + atom + sub;
-      uint8_t* ks = smem + CF::OFF_K + s * CF::Q_BYTES + atom + sub;
-      float G0 = 0.f, G1 = 0.f;
+      uint8_t* qs = smem + CF::OFF_Q + (n % CF::QS) * CF::Q_BYTES + qk_atom + qk_sub;
+      uint8_t* ks = smem + CF::OFF_K + (n % CF::QS) * CF::Q_BYTES + qk_atom + qk_sub;
+      float4 gv[8];
+      float4 G = make_float4(0.f, 0.f, 0.f, 0.f);
       if (p.has_g) {
-        float2* part = reinterpret_cast<float2*>(smem + CF::OFF_PART) + s * 256;
-        float a0 = 0.f, a1 = 0.f;
+        const float4* g4 = reinterpret_cast<const float4*>(smem + CF::OFF_G + s * CF::G_BYTES) + lane;
+        float4 tot = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float2 gv = gsm[(tq * 16 + i) * (KD / 2)];
-          a0 += gv.x;
-          a1 += gv.y;
+        for (int i = 0; i < 8; ++i) {
+          gv[i] = g4[(gw * 8 + i) * (KD / 4)];
+          tot.x += gv[i].x;
+          tot.y += gv[i].y;
+          tot.z += gv[i].z;
+          tot.w += gv[i].w;
         }
-        part[tq * 64 + kp] = make_float2(a0, a1);
+        float4* part = reinterpret_cast<float4*>(smem + CF::OFF_PART) + s * (GATE_WARPS * 32);
+        part[gw * 32 + lane] = tot;
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar[B_GSYNC + s]);
         if (!mbar_wait(&bar[B_GSYNC + s], ph2, ab)) { gok = false; break; }
-        for (int q2 = 0; q2 < tq; ++q2) {
-          const float2 pv = part[q2 * 64 + kp];
-          G0 += pv.x;
-          G1 += pv.y;
-        }
-      } else {
-        G0 = G1 = gamma * static_cast<float>(16 * tq);
-      }
-      // 16 tokens in 4 batches of 4; each batch's loads are issued one
-      // batch ahead of its arithmetic and stores.
-      float2 gv[2][4];
-      uint32_t qv[2][4], kv[2][4];
-      auto load_batch = [&](int bt, int slot) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int t = tq * 16 + bt * 4 + j;
-          const uint32_t off = static_cast<uint32_t>(t) * 128u + ((chunk ^ (t & 7)) << 4);
-          gv[slot][j] = p.has_g ? gsm[t * (KD / 2)] : make_float2(0.f, 0.f);
-          qv[slot][j] = *reinterpret_cast<const uint32_t*>(qs + off);
-          kv[slot][j] = *reinterpret_cast<const uint32_t*>(ks + off);
-        }
-      };
-      load_batch(0, 0);
-#pragma unroll
-      for (int bt = 0; bt < 4; ++bt) {
-        const int cur = bt & 1;
-        if (bt + 1 < 4) load_batch(bt + 1, cur ^ 1);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int t = tq * 16 + bt * 4 + j;
-          if (p.has_g) {
-            G0 += gv[cur][j].x;
-            G1 += gv[cur][j].y;
-          } else {
-            G0 = G1 = gamma * static_cast<float>(t + 1);
-          }
-          const float e0 = __expf(G0), e1 = __expf(G1);
-          const float n0 = __expf(-G0), n1 = __expf(-G1);
-          const uint32_t off = static_cast<uint32_t>(t) * 128u + ((chunk ^ (t & 7)) << 4);
-          const uint32_t q2 = qv[cur][j], k2 = kv[cur][j];
-          *reinterpret_cast<uint32_t*>(qs + off) =
-              pack_bf16x2(__uint_as_float(q2 << 16) * (e0 * scale),
-                          __uint_as_float(q2 & 0xFFFF0000u) * (e1 * scale));
-          *reinterpret_cast<uint32_t*>(ks + off) =
-              pack_bf16x2(__uint_as_float(k2 << 16) * n0, __uint_as_float(k2 & 0xFFFF0000u) * n1);
+        for (int w = 0; w < gw; ++w) {
+          const float4 pv = part[w * 32 + lane];
+          G.x += pv.x;
+          G.y += pv.y;
+          G.z += pv.z;
+          G.w += pv.w;
         }
       }
-      if (tq == 3) {
-        dec[s * KD + 2 * kp] = __expf(G0);
-        dec[s * KD + 2 * kp + 1] = __expf(G1);
+      // Qs = q * 2^(G log2e + log2 scale), Kg = k * 2^(-G log2e), packed
+      // f32x2 arithmetic, four keys per lane.
+      const float2 L2 = make_float2(kLog2e, kLog2e), NL2 = make_float2(-kLog2e, -kLog2e);
+      const float2 LS2 = make_float2(log2_scale, log2_scale);
+      float2 G01 = make_float2(G.x, G.y), G23 = make_float2(G.z, G.w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int t = gw * 8 + i;
+        float2 xa01, xa23, xb01, xb23;
+        if (p.has_g) {
+          G01 = __fadd2_rn(G01, make_float2(gv[i].x, gv[i].y));
+          G23 = __fadd2_rn(G23, make_float2(gv[i].z, gv[i].w));
+          xa01 = __ffma2_rn(G01, L2, LS2);
+          xa23 = __ffma2_rn(G23, L2, LS2);
+          xb01 = __fmul2_rn(G01, NL2);
+          xb23 = __fmul2_rn(G23, NL2);
+        } else {
+          const float Gt = gamma * static_cast<float>(t + 1);
+          G01 = G23 = make_float2(Gt, Gt);
+          xa01 = xa23 = make_float2(fmaf(Gt, kLog2e, log2_scale), fmaf(Gt, kLog2e, log2_scale));
+          xb01 = xb23 = make_float2(-Gt * kLog2e, -Gt * kLog2e);
+        }
+        const float2 a01 = make_float2(ex2_approx(xa01.x), ex2_approx(xa01.y));
+        const float2 a23 = make_float2(ex2_approx(xa23.x), ex2_approx(xa23.y));
+        const float2 b01 = make_float2(ex2_approx(xb01.x), ex2_approx(xb01.y));
+        const float2 b23 = make_float2(ex2_approx(xb23.x), ex2_approx(xb23.y));
+        const uint32_t off = static_cast<uint32_t>(t) * 128u + ((qk_chunk ^ (t & 7)) << 4);
+        const uint2 q2 = *reinterpret_cast<const uint2*>(qs + off);
+        const uint2 k2 = *reinterpret_cast<const uint2*>(ks + off);
+        float2 q01 = __fmul2_rn(bf16x2_f32x2(q2.x), a01), q23 = __fmul2_rn(bf16x2_f32x2(q2.y), a23);
+        if (p.scale_apart) {
+          q01 = __fmul2_rn(q01, make_float2(p.scale, p.scale));
+          q23 = __fmul2_rn(q23, make_float2(p.scale, p.scale));
+        }
+        const float2 k01 = __fmul2_rn(bf16x2_f32x2(k2.x), b01), k23 = __fmul2_rn(bf16x2_f32x2(k2.y), b23);
+        *reinterpret_cast<uint2*>(qs + off) =
+            make_uint2(pack_bf16x2(q01.x, q01.y), pack_bf16x2(q23.x, q23.y));
+        *reinterpret_cast<uint2*>(ks + off) =
+            make_uint2(pack_bf16x2(k01.x, k01.y), pack_bf16x2(k23.x, k23.y));
+        if (i == 7 && gw == GATE_WARPS - 1) {
+          // e^{G_last}
+          const float2 d01 = __fmul2_rn(G01, L2), d23 = __fmul2_rn(G23, L2);
+          *reinterpret_cast<float4*>(dec + s * KD + 4 * lane) =
+              make_float4(ex2_approx(d01.x), ex2_approx(d01.y), ex2_approx(d23.x), ex2_approx(d23.y));
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -462,6 +501,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int j = 0; j < VS; ++j) hreg[j] = 0.f;
     }
+    constexpr int NS = CF::NS;
     // H: MN-major B operand [128 keys][VS], 64-column atoms 16 KB apart.
     auto store_h = [&]() {
       uint8_t* hp = smem + CF::OFF_H;
@@ -524,19 +564,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float d = dec[s * KD + key];
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_DEC_EMPTY + s]);
-      if (!mbar_wait(&bar[B_S_FULL], n & 1, ab)) { ok = false; break; }
+      if (!mbar_wait(&bar[B_S_FULL + n % NS], (n / NS) & 1, ab)) { ok = false; break; }
       tc_fence_after();
 #pragma unroll
       for (int j = 0; j < VS; j += 32) {
         uint32_t sv[32];
-        tmem_ld32(lane_addr + CF::COL_S + j, sv);
+        tmem_ld32(lane_addr + CF::COL_S + (n % NS) * VS + j, sv);
         tmem_ld_wait(sv);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) hreg[j + i] = d * (hreg[j + i] + __uint_as_float(sv[i]));
+        for (int i = 0; i < 32; i += 2) {
+          const float2 hs = __fadd2_rn(make_float2(hreg[j + i], hreg[j + i + 1]),
+                                       make_float2(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])));
+          const float2 hn = __fmul2_rn(hs, make_float2(d, d));
+          hreg[j + i] = hn.x;
+          hreg[j + i + 1] = hn.y;
+        }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_S_EMPTY]);
+      if (lane == 0) mbar_arrive(&bar[B_S_EMPTY + n % NS]);
       // O_n done -> H and P may be rewritten for chunk n+1 (the next O
       // accumulates into the other TMEM buffer meanwhile)
       if (!mbar_wait(&bar[B_O_FULL + s], ph2, ab)) { ok = false; break; }
@@ -564,6 +610,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 }  // namespace gla
 }  // namespace gl
+
+#include <cmath>
+#include <cstdlib>
 
 #include "tmap.h"
 
@@ -616,12 +665,17 @@ int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float
   p.ht = ht;
   p.err = err;
   p.scale = scale;
+  p.scale_apart = !(scale > 0.f && std::isfinite(scale));
+  p.log2_scale = p.scale_apart ? 0.f : static_cast<float>(std::log2(static_cast<double>(scale)));
   p.B = static_cast<int>(B);
   p.T = static_cast<int>(T);
   p.H = static_cast<int>(H);
   p.has_g = g != nullptr;
   // Split V in two when that is needed to give every SM a sequence.
-  if (B * H * 2 <= num_sms) {
+  // GLAUCIS_GLA_VS=64|128 overrides the choice.
+  bool split = B * H * 2 <= num_sms;
+  if (const char* e = std::getenv("GLAUCIS_GLA_VS")) split = std::atoi(e) == 64;
+  if (split) {
     p.nsplit = 2;
     return launch_vs<64>(q, k, v, g, p, st, why);
   }

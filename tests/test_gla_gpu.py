@@ -1,5 +1,6 @@
 """Parity of the fused sm_100a chunked-GLA forward against the CPU oracle,
-through the C ABI.
+through the C ABI.  The launcher reads GLAUCIS_GLA_VS at every call, so
+each test runs on both kernel instances.
 
 Tolerance (o and the final state): |gpu - ref| <= 2e-2 * |ref| + 2e-2 * rms(ref)
 element-wise, plus a relative Frobenius error below 1e-2.  The kernel feeds
@@ -21,6 +22,14 @@ from tests.helpers import assert_close, rel_fro
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 RTOL, ATOL_FRAC, FRO = 2e-2, 2e-2, 1e-2
+
+
+@pytest.fixture(autouse=True, params=["64", "128"])
+def value_slice(request, monkeypatch):
+    """Every test runs on both kernel instances: V split in two 64-wide
+    slices (double-buffered state copy) and the full 128-wide V."""
+    monkeypatch.setenv("GLAUCIS_GLA_VS", request.param)
+    return request.param
 
 
 def _run(cuda, cfg: configs.GLAConfig, seed=0):
