@@ -30,6 +30,9 @@ SIGNATURES = {
     "gl_gmm_fp8_fwd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _P]),
     "gl_chunk_gla_fwd": (_I, [_P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64, _I64,
                               _P, _P, _P, _P]),
+    "gl_chunk_gla_fwd_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I64, _I64]),
+    "gl_chunk_gla_fwd_ws": (_I, [_P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64, _I64,
+                                 _P, _P, _P, ctypes.c_size_t, _P, _P]),
     "gl_gmm_fp8_act_fwd_noalloc": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _P]),
     "gl_device_status": (_I, [_P, _P, ctypes.POINTER(ctypes.c_int)]),
     "gl_last_error": (ctypes.c_char_p, []),

@@ -25,8 +25,9 @@ int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const 
                       const char** why);
 int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float* g,
                         const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
-                        int64_t H, int64_t K, int64_t V, void* o, float* ht, int* err,
-                        cudaStream_t st, int num_sms, const char** why);
+                        int64_t H, int64_t K, int64_t V, void* o, float* ht, void* ws,
+                        size_t ws_bytes, int* err, cudaStream_t st, int num_sms, const char** why);
+size_t gl_chunk_gla_ws_bytes(int64_t B, int64_t T, int64_t H, int num_sms);
 
 namespace {
 
@@ -234,31 +235,61 @@ int gl_gmm_fp8_fwd(const void* a_q, const float* a_s, const void* b_q, const flo
   return GL_OK;
 }
 
-int gl_chunk_gla_fwd(const void* q, const void* k, const void* v, const float* g,
-                     const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
-                     int64_t H, int64_t K, int64_t V, int64_t chunk_size, void* o, float* ht,
-                     int* err_word, void* stream) {
-  if (!q || !k || !v || !o) return fail(GL_EINVAL, "gl_chunk_gla_fwd: null pointer");
+static int chunk_gla_check(const char* fn, const void* q, const void* k, const void* v,
+                           const float* g, const float* g_gamma, const float* h0, int64_t B,
+                           int64_t T, int64_t H, int64_t K, int64_t V, int64_t chunk_size,
+                           const void* o, const float* ht) {
+  const std::string f(fn);
+  if (!q || !k || !v || !o) return fail(GL_EINVAL, f + ": null pointer");
   if ((g == nullptr) == (g_gamma == nullptr))
-    return fail(GL_EINVAL, "gl_chunk_gla_fwd: exactly one of g / g_gamma must be given");
-  if (K != 128 || V != 128) return fail(GL_EINVAL, "gl_chunk_gla_fwd: K and V must be 128");
-  if (chunk_size != 64) return fail(GL_EINVAL, "gl_chunk_gla_fwd: chunk_size must be 64");
+    return fail(GL_EINVAL, f + ": exactly one of g / g_gamma must be given");
+  if (K != 128 || V != 128) return fail(GL_EINVAL, f + ": K and V must be 128");
+  if (chunk_size != 64) return fail(GL_EINVAL, f + ": chunk_size must be 64");
   if (B <= 0 || H <= 0 || T <= 0 || T % 64 != 0)
-    return fail(GL_EINVAL, "gl_chunk_gla_fwd: need B, H > 0 and T a positive multiple of 64");
-  if (B * T * H > (int64_t(1) << 31) - 1)
-    return fail(GL_EINVAL, "gl_chunk_gla_fwd: B*T*H must fit in 31 bits");
+    return fail(GL_EINVAL, f + ": need B, H > 0 and T a positive multiple of 64");
+  if (B * T * H > (int64_t(1) << 31) - 1) return fail(GL_EINVAL, f + ": B*T*H must fit in 31 bits");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || (g && !aligned16(g)) ||
       (h0 && !aligned16(h0)) || (ht && !aligned16(ht)))
-    return fail(GL_EINVAL, "gl_chunk_gla_fwd: tensors must be 16-byte aligned");
+    return fail(GL_EINVAL, f + ": tensors must be 16-byte aligned");
+  return GL_OK;
+}
+
+int gl_chunk_gla_fwd_ws(const void* q, const void* k, const void* v, const float* g,
+                        const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
+                        int64_t H, int64_t K, int64_t V, int64_t chunk_size, void* o, float* ht,
+                        void* workspace, size_t workspace_bytes, int* err_word, void* stream) {
+  if (int rc = chunk_gla_check("gl_chunk_gla_fwd", q, k, v, g, g_gamma, h0, B, T, H, K, V,
+                               chunk_size, o, ht))
+    return rc;
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(GL_EINVAL, "gl_chunk_gla_fwd_ws: workspace must be 256-byte aligned");
   DeviceState* d = nullptr;
   if (int rc = device_state(&d)) return rc;
   const char* why = "";
   const int rc = gl_launch_chunk_gla(q, k, v, g, g_gamma, h0, scale, B, T, H, K, V, o, ht,
+                                     workspace, workspace ? workspace_bytes : 0,
                                      err_word ? err_word : d->err,
                                      static_cast<cudaStream_t>(stream), d->num_sms, &why);
   if (rc == -1) return fail(GL_EINVAL, std::string("gl_chunk_gla_fwd: ") + why);
   if (rc != 0) return fail(GL_ELAUNCH, std::string("gl_chunk_gla_fwd: ") + why);
   return GL_OK;
+}
+
+int gl_chunk_gla_fwd(const void* q, const void* k, const void* v, const float* g,
+                     const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
+                     int64_t H, int64_t K, int64_t V, int64_t chunk_size, void* o, float* ht,
+                     int* err_word, void* stream) {
+  return gl_chunk_gla_fwd_ws(q, k, v, g, g_gamma, h0, scale, B, T, H, K, V, chunk_size, o, ht,
+                             nullptr, 0, err_word, stream);
+}
+
+size_t gl_chunk_gla_fwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K, int64_t V,
+                                        int64_t chunk_size) {
+  if (B <= 0 || H <= 0 || T <= 0 || T % 64 != 0 || K != 128 || V != 128 || chunk_size != 64)
+    return 0;
+  DeviceState* d = nullptr;
+  if (device_state(&d)) return 0;
+  return gl_chunk_gla_ws_bytes(B, T, H, d->num_sms);
 }
 
 int gl_device_status(int* err_word, void* stream, int* code) {

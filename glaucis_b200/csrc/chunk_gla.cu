@@ -40,7 +40,7 @@ constexpr int C = 64, KD = 128, NUM_THREADS = 512;
 constexpr int GATE_WARPS = 8, STATE_WARPS = 4;
 // Register split (launch: 512 x 128): control warpgroup 56, the two gating
 // warpgroups keep 128, the state warpgroup rises to 216.
-constexpr int REG_CTRL = 48, REG_STATE = 208;
+constexpr int REG_CTRL = 40, REG_STATE = 216;
 static_assert(128 * REG_CTRL + 256 * 128 + 128 * REG_STATE <= NUM_THREADS * 128,
               "register split exceeds the launch allocation");
 
@@ -88,6 +88,15 @@ struct Params {
   float scale;
   float log2_scale;  // log2(scale) when scale > 0 (folded into the exponent), else 0
   int scale_apart;   // 1: scale <= 0 or not finite, applied as a separate multiply
+  // Sequence split: chunks [seg*NT/nseg, (seg+1)*NT/nseg) form segment seg.
+  // The state-only pass runs segments 0..nseg-2 from a zero state and writes
+  // each one's final state ws_h [B*H][nseg-1][K][V] and total decay
+  // ws_d [B*H][nseg-1][K]; the fold kernel turns record j into the initial
+  // state of segment j+1 (h0 folded with segments 0..j), which the full pass
+  // loads like h0.  nseg == 1: no split.
+  int nseg, seg_grid;  // segments in total / per (b, h, V slice) in this grid
+  float* ws_h;
+  float* ws_d;
   int B, T, H, nsplit;
   int has_g;
 };
@@ -133,7 +142,7 @@ __device__ __forceinline__ uint32_t kmaj_off(uint32_t row, uint32_t col, uint32_
          (col & 7u) * 2u;
 }
 
-template <int VS>
+template <int VS, bool kStateOnly>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     chunk_gla_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
@@ -151,11 +160,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int T = p.T, H = p.H;
-  const int NT = T / C;
-  const int bh = blockIdx.x / p.nsplit, vsl = blockIdx.x % p.nsplit;
+  const int seg = blockIdx.x % p.seg_grid, rest = blockIdx.x / p.seg_grid;
+  const int bh = rest / p.nsplit, vsl = rest % p.nsplit;
   const int b = bh / H, h = bh % H;
   const int v0 = vsl * VS;
-  const int tok0 = b * T;
+  const int c0 = static_cast<int>(static_cast<int64_t>(seg) * (T / C) / p.nseg);
+  const int c1 = static_cast<int>(static_cast<int64_t>(seg + 1) * (T / C) / p.nseg);
+  const int NT = c1 - c0;  // chunks of this CTA
+  const int tok0 = b * T + c0 * C;
   const Abort ab{abort_flag, p.err};
 
   if (warp == 0 && lane == 0) {
@@ -207,12 +219,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int s = n % CF::QS;
         const int tok = tok0 + n * C;
         if (!mbar_wait(&bar[B_QKV_EMPTY + s], ((n / CF::QS) & 1) ^ 1, ab)) break;
-        mbar_arrive_expect_tx(&bar[B_QKV_FULL + s], 2 * CF::Q_BYTES + CF::V_BYTES);
+        mbar_arrive_expect_tx(&bar[B_QKV_FULL + s], (kStateOnly ? 1 : 2) * CF::Q_BYTES + CF::V_BYTES);
         uint8_t* qd = smem + CF::OFF_Q + s * CF::Q_BYTES;
         uint8_t* kd = smem + CF::OFF_K + s * CF::Q_BYTES;
         uint8_t* vd = smem + CF::OFF_V + s * CF::V_BYTES;
-        tma_load_3d(qd, &tm_q, &bar[B_QKV_FULL + s], 0, h, tok);
-        tma_load_3d(qd + 8192, &tm_q, &bar[B_QKV_FULL + s], 64, h, tok);
+        if (!kStateOnly) {
+          tma_load_3d(qd, &tm_q, &bar[B_QKV_FULL + s], 0, h, tok);
+          tma_load_3d(qd + 8192, &tm_q, &bar[B_QKV_FULL + s], 64, h, tok);
+        }
         tma_load_3d(kd, &tm_k, &bar[B_QKV_FULL + s], 0, h, tok);
         tma_load_3d(kd + 8192, &tm_k, &bar[B_QKV_FULL + s], 64, h, tok);
 #pragma unroll
@@ -276,46 +290,64 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // Dataflow issue.  na: next chunk for A/S (needs its gating, its A
       // buffer free and the previous S read); nh: next chunk for Qs H (needs
       // H_nh and its O buffer drained); no: next chunk for P V (needs P_no).
-      int na = 0, nh = 0, no = 0;
-      uint64_t t0 = global_ns();
-      uint32_t spins = 0;
-      while (no < NT) {
-        bool progressed = false;
-        if (no < nh && mbar_test(&bar[B_P_FULL], no & 1)) {
+      if (kStateOnly) {
+        // S_n only; the q/k/v stage is free once S_n has completed.
+        for (int n = 0; n < NT; ++n) {
+          const int st = n % QS, sb = n % NS;
+          if (!mbar_wait(&bar[B_PREP + (n & 1)], (n >> 1) & 1, ab)) break;
+          if (!mbar_wait(&bar[B_S_EMPTY + sb], ((n / NS) & 1) ^ 1, ab)) break;
           tc_fence_after();
-          issue_o_p(no);
-          ++no;
-          progressed = true;
+          const uint32_t k_addr = s_base + CF::OFF_K + st * CF::Q_BYTES;
+          const uint32_t v_addr = s_base + CF::OFF_V + st * CF::V_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16(tmem + CF::COL_S + sb * VS, sdesc(k_addr + kk * 2048, 8192, 1024, kSwizzle128B),
+                    sdesc(v_addr + kk * 2048, 8192, 1024, kSwizzle128B), CF::IDESC_S, kk > 0);
+          tc_commit(&bar[B_S_FULL + sb]);
+          tc_commit(&bar[B_QKV_EMPTY + st]);
         }
-        if (nh < na && nh == no && mbar_test(&bar[B_H_FULL], nh & 1) &&
-            mbar_test(&bar[B_O_EMPTY + (nh & 1)], ((nh >> 1) & 1) ^ 1)) {
-          tc_fence_after();
-          issue_o_h(nh);
-          ++nh;
-          progressed = true;
-        }
-        if (na < NT && na <= no + QS - 1) {
-          const int s = na & 1;
-          const uint32_t ph2 = (na >> 1) & 1;
-          if (mbar_test(&bar[B_PREP + s], ph2) && mbar_test(&bar[B_A_EMPTY + s], ph2 ^ 1) &&
-              mbar_test(&bar[B_S_EMPTY + na % NS], ((na / NS) & 1) ^ 1)) {
+      } else {
+        int na = 0, nh = 0, no = 0;
+        uint64_t t0 = global_ns();
+        uint32_t spins = 0;
+        while (no < NT) {
+          bool progressed = false;
+          if (no < nh && mbar_test(&bar[B_P_FULL], no & 1)) {
             tc_fence_after();
-            issue_a_s(na);
-            ++na;
+            issue_o_p(no);
+            ++no;
             progressed = true;
           }
-        }
-        if (progressed) {
-          t0 = global_ns();
-          spins = 0;
-        } else if ((++spins & 255u) != 0) {
-          __nanosleep(20);  // leave the issue slots to the gating warps
-        } else {
-          if (*abort_flag) break;
-          if (global_ns() - t0 > kWaitNs) {
-            *abort_flag = 1;
-            atomicExch(p.err, GL_DEV_WAIT_TIMEOUT);
-            break;
+          if (nh < na && nh == no && mbar_test(&bar[B_H_FULL], nh & 1) &&
+              mbar_test(&bar[B_O_EMPTY + (nh & 1)], ((nh >> 1) & 1) ^ 1)) {
+            tc_fence_after();
+            issue_o_h(nh);
+            ++nh;
+            progressed = true;
+          }
+          if (na < NT && na <= no + QS - 1) {
+            const int s = na & 1;
+            const uint32_t ph2 = (na >> 1) & 1;
+            if (mbar_test(&bar[B_PREP + s], ph2) && mbar_test(&bar[B_A_EMPTY + s], ph2 ^ 1) &&
+                mbar_test(&bar[B_S_EMPTY + na % NS], ((na / NS) & 1) ^ 1)) {
+              tc_fence_after();
+              issue_a_s(na);
+              ++na;
+              progressed = true;
+            }
+          }
+          if (progressed) {
+            t0 = global_ns();
+            spins = 0;
+          } else if ((++spins & 255u) != 0) {
+            __nanosleep(20);  // leave the issue slots to the gating warps
+          } else {
+            if (*abort_flag) break;
+            if (global_ns() - t0 > kWaitNs) {
+              *abort_flag = 1;
+              atomicExch(p.err, GL_DEV_WAIT_TIMEOUT);
+              break;
+            }
           }
         }
       }
@@ -444,21 +476,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           xa01 = xa23 = make_float2(fmaf(Gt, kLog2e, log2_scale), fmaf(Gt, kLog2e, log2_scale));
           xb01 = xb23 = make_float2(-Gt * kLog2e, -Gt * kLog2e);
         }
-        const float2 a01 = make_float2(ex2_approx(xa01.x), ex2_approx(xa01.y));
-        const float2 a23 = make_float2(ex2_approx(xa23.x), ex2_approx(xa23.y));
         const float2 b01 = make_float2(ex2_approx(xb01.x), ex2_approx(xb01.y));
         const float2 b23 = make_float2(ex2_approx(xb23.x), ex2_approx(xb23.y));
         const uint32_t off = static_cast<uint32_t>(t) * 128u + ((qk_chunk ^ (t & 7)) << 4);
-        const uint2 q2 = *reinterpret_cast<const uint2*>(qs + off);
-        const uint2 k2 = *reinterpret_cast<const uint2*>(ks + off);
-        float2 q01 = __fmul2_rn(bf16x2_f32x2(q2.x), a01), q23 = __fmul2_rn(bf16x2_f32x2(q2.y), a23);
-        if (p.scale_apart) {
-          q01 = __fmul2_rn(q01, make_float2(p.scale, p.scale));
-          q23 = __fmul2_rn(q23, make_float2(p.scale, p.scale));
+        if (!kStateOnly) {
+          const float2 a01 = make_float2(ex2_approx(xa01.x), ex2_approx(xa01.y));
+          const float2 a23 = make_float2(ex2_approx(xa23.x), ex2_approx(xa23.y));
+          const uint2 q2 = *reinterpret_cast<const uint2*>(qs + off);
+          float2 q01 = __fmul2_rn(bf16x2_f32x2(q2.x), a01), q23 = __fmul2_rn(bf16x2_f32x2(q2.y), a23);
+          if (p.scale_apart) {
+            q01 = __fmul2_rn(q01, make_float2(p.scale, p.scale));
+            q23 = __fmul2_rn(q23, make_float2(p.scale, p.scale));
+          }
+          *reinterpret_cast<uint2*>(qs + off) =
+              make_uint2(pack_bf16x2(q01.x, q01.y), pack_bf16x2(q23.x, q23.y));
         }
+        const uint2 k2 = *reinterpret_cast<const uint2*>(ks + off);
         const float2 k01 = __fmul2_rn(bf16x2_f32x2(k2.x), b01), k23 = __fmul2_rn(bf16x2_f32x2(k2.y), b23);
-        *reinterpret_cast<uint2*>(qs + off) =
-            make_uint2(pack_bf16x2(q01.x, q01.y), pack_bf16x2(q23.x, q23.y));
         *reinterpret_cast<uint2*>(ks + off) =
             make_uint2(pack_bf16x2(k01.x, k01.y), pack_bf16x2(k23.x, k23.y));
         if (i == 7 && gw == GATE_WARPS - 1) {
@@ -475,9 +509,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_arrive(&bar[B_PREP + s]);
         mbar_arrive(&bar[B_DEC_FULL + s]);
       }
-      if (n >= 2 && !o_epilogue(n - 2)) gok = false;
+      if (!kStateOnly && n >= 2 && !o_epilogue(n - 2)) gok = false;
     }
-    for (int m = NT >= 2 ? NT - 2 : 0; m < NT && gok; ++m) gok = o_epilogue(m);
+    if (!kStateOnly)
+      for (int m = NT >= 2 ? NT - 2 : 0; m < NT && gok; ++m) gok = o_epilogue(m);
   } else if (warp >= 4 + GATE_WARPS) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_STATE));
     // ------------------------- P epilogue, state update, O epilogue
@@ -487,8 +522,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int64_t bhi = static_cast<int64_t>(b) * H + h;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     float hreg[VS];
-    if (p.h0) {
-      const float4* src = reinterpret_cast<const float4*>(p.h0 + (bhi * KD + key) * 128 + v0);
+    // Initial state: h0 for the first segment; with a sequence split, later
+    // segments start from the state the fold kernel left in the workspace.
+    const float* init = kStateOnly ? nullptr
+                        : seg == 0 ? (p.h0 ? p.h0 + bhi * KD * 128 : nullptr)
+                                   : p.ws_h + (bhi * (p.nseg - 1) + seg - 1) * KD * 128;
+    if (init) {
+      const float4* src = reinterpret_cast<const float4*>(init + static_cast<int64_t>(key) * 128 + v0);
 #pragma unroll
       for (int j = 0; j < VS / 4; ++j) {
         const float4 x = __ldg(src + j);
@@ -501,6 +541,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int j = 0; j < VS; ++j) hreg[j] = 0.f;
     }
+    float dacc = 1.f;  // state-only pass: product of the chunk decays
     constexpr int NS = CF::NS;
     // H: MN-major B operand [128 keys][VS], 64-column atoms 16 KB apart.
     auto store_h = [&]() {
@@ -554,14 +595,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) mbar_arrive(&bar[B_P_FULL]);
       return true;
     };
-    store_h();
-    bool ok = p_epilogue(0);
+    bool ok = true;
+    if (!kStateOnly) {
+      store_h();
+      ok = p_epilogue(0);
+    }
     for (int n = 0; n < NT && ok; ++n) {
       const int s = n & 1;
       const uint32_t ph2 = (n >> 1) & 1;
       // state update: h <- e^{G_last} (h + S_n)
       if (!mbar_wait(&bar[B_DEC_FULL + s], ph2, ab)) { ok = false; break; }
       const float d = dec[s * KD + key];
+      dacc *= d;
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_DEC_EMPTY + s]);
       if (!mbar_wait(&bar[B_S_FULL + n % NS], (n / NS) & 1, ab)) { ok = false; break; }
@@ -583,6 +628,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_S_EMPTY + n % NS]);
+      if (kStateOnly) continue;
       // O_n done -> H and P may be rewritten for chunk n+1 (the next O
       // accumulates into the other TMEM buffer meanwhile)
       if (!mbar_wait(&bar[B_O_FULL + s], ph2, ab)) { ok = false; break; }
@@ -592,7 +638,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!p_epilogue(n + 1)) { ok = false; break; }
       }
     }
-    if (ok && p.ht) {
+    if (ok && kStateOnly) {
+      const int64_t rec = bhi * (p.nseg - 1) + seg;
+      float4* dst = reinterpret_cast<float4*>(p.ws_h + (rec * KD + key) * 128 + v0);
+#pragma unroll
+      for (int j = 0; j < VS / 4; ++j)
+        dst[j] = make_float4(hreg[4 * j], hreg[4 * j + 1], hreg[4 * j + 2], hreg[4 * j + 3]);
+      if (vsl == 0) p.ws_d[rec * KD + key] = dacc;
+    } else if (ok && p.ht && seg == p.nseg - 1) {
       float4* dst = reinterpret_cast<float4*>(p.ht + (bhi * KD + key) * 128 + v0);
 #pragma unroll
       for (int j = 0; j < VS / 4; ++j)
@@ -608,6 +661,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// Sequence split: record j (the zero-start final state h_j and total decay
+// D_j of segment j) becomes the initial state of segment j+1,
+//   s_{j+1} = D_j * s_j + h_j,  s_0 = h0 (or 0),
+// the recurrence h_{n+1} = d_n (h_n + S_n) being linear in h_n with a per-row
+// scale.  One thread per 4 state entries of one (batch, head).
+__global__ void __launch_bounds__(256) gla_fold_kernel(const float* __restrict__ h0,
+                                                       float* __restrict__ ws_h,
+                                                       const float* __restrict__ ws_d, int BH,
+                                                       int nseg) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(BH) * KD * 32) return;
+  const int bh = static_cast<int>(i / (KD * 32));
+  const int key = static_cast<int>((i / 32) % KD), c4 = static_cast<int>(i % 32);
+  float4 h = h0 ? reinterpret_cast<const float4*>(h0)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < nseg - 1; ++j) {
+    const int64_t rec = static_cast<int64_t>(bh) * (nseg - 1) + j;
+    const float d = ws_d[rec * KD + key];
+    float4* slot = reinterpret_cast<float4*>(ws_h + (rec * KD + key) * 128) + c4;
+    const float4 x = *slot;
+    h = make_float4(fmaf(d, h.x, x.x), fmaf(d, h.y, x.y), fmaf(d, h.z, x.z), fmaf(d, h.w, x.w));
+    *slot = h;
+  }
+}
+
 }  // namespace gla
 }  // namespace gl
 
@@ -616,10 +693,51 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 #include "tmap.h"
 
+// Sequence split for few (batch, head) pairs with long sequences: how many
+// segments the launcher uses (1 = none).  Each segment keeps at least 8
+// chunks, and the full pass puts one CTA on each SM.
+static int gla_segments(int64_t B, int64_t T, int64_t H, int num_sms) {
+  const int64_t items = B * H, NT = T / 64;
+  if (const char* e = std::getenv("GLAUCIS_GLA_SEGMENTS")) {
+    const int64_t n = std::atoi(e);
+    return static_cast<int>(n < 1 ? 1 : (n > NT ? NT : n));
+  }
+  if (items * 2 > num_sms) return 1;
+  int64_t n = num_sms / items;
+  if (n > NT / 8) n = NT / 8;
+  return static_cast<int>(n < 2 ? 1 : n);
+}
+
+// Workspace of a split launch: final state [B*H][nseg-1][128][128] and total
+// decay [B*H][nseg-1][128], fp32, the decays 256-byte aligned after the states.
+static size_t gla_ws_bytes(int64_t B, int64_t H, int nseg) {
+  if (nseg <= 1) return 0;
+  const size_t rec = static_cast<size_t>(B * H) * static_cast<size_t>(nseg - 1);
+  const size_t hb = rec * 128 * 128 * 4;
+  return ((hb + 255) / 256) * 256 + rec * 128 * 4;
+}
+
+template <int VS, bool kStateOnly>
+static int launch_pass(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                       const CUtensorMap& tg, const gl::gla::Params& p, int grid, cudaStream_t st,
+                       const char** why) {
+  using CF = gl::gla::Cfg<VS>;
+  if (!gl_set_smem_attr(reinterpret_cast<const void*>(gl::gla::chunk_gla_fwd_kernel<VS, kStateOnly>), 0,
+                        static_cast<int>(CF::SMEM_BYTES), why))
+    return -2;
+  gl::gla::chunk_gla_fwd_kernel<VS, kStateOnly><<<grid, gl::gla::NUM_THREADS, CF::SMEM_BYTES, st>>>(
+      tq, tk, tv, tg, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return -2;
+  }
+  return 0;
+}
+
 template <int VS>
 static int launch_vs(const void* q, const void* k, const void* v, const float* g,
-                     const gl::gla::Params& p, cudaStream_t st, const char** why) {
-  using CF = gl::gla::Cfg<VS>;
+                     gl::gla::Params p, cudaStream_t st, const char** why) {
   const int64_t BT = static_cast<int64_t>(p.B) * p.T;
   CUtensorMap tq, tk, tv, tg;
   if (!gl_make_tmap_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, 128, p.H, BT, 128,
@@ -639,23 +757,33 @@ static int launch_vs(const void* q, const void* k, const void* v, const float* g
   } else {
     tg = tq;  // unused when the per-head gate is given
   }
-  if (!gl_set_smem_attr(reinterpret_cast<const void*>(gl::gla::chunk_gla_fwd_kernel<VS>), 0,
-                        static_cast<int>(CF::SMEM_BYTES), why))
-    return -2;
-  const int grid = p.B * p.H * p.nsplit;
-  gl::gla::chunk_gla_fwd_kernel<VS><<<grid, gl::gla::NUM_THREADS, CF::SMEM_BYTES, st>>>(tq, tk, tv, tg, p);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    *why = cudaGetErrorString(e);
-    return -2;
+  const int items = p.B * p.H * p.nsplit;
+  if (p.nseg > 1) {
+    // State-only pass over segments 0 .. nseg-2, the fold, then the full pass.
+    gl::gla::Params p1 = p;
+    p1.seg_grid = p.nseg - 1;
+    if (int rc = launch_pass<VS, true>(tq, tk, tv, tg, p1, items * p1.seg_grid, st, why)) return rc;
+    const int64_t n4 = static_cast<int64_t>(p.B) * p.H * 128 * 32;
+    gl::gla::gla_fold_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, st>>>(
+        p.h0, p.ws_h, p.ws_d, p.B * p.H, p.nseg);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      *why = cudaGetErrorString(e);
+      return -2;
+    }
   }
-  return 0;
+  p.seg_grid = p.nseg;
+  return launch_pass<VS, false>(tq, tk, tv, tg, p, items * p.nseg, st, why);
+}
+
+size_t gl_chunk_gla_ws_bytes(int64_t B, int64_t T, int64_t H, int num_sms) {
+  return gla_ws_bytes(B, H, gla_segments(B, T, H, num_sms));
 }
 
 int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float* g,
                         const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
-                        int64_t H, int64_t K, int64_t V, void* o, float* ht, int* err,
-                        cudaStream_t st, int num_sms, const char** why) {
+                        int64_t H, int64_t K, int64_t V, void* o, float* ht, void* ws,
+                        size_t ws_bytes, int* err, cudaStream_t st, int num_sms, const char** why) {
   (void)K;
   (void)V;
   gl::gla::Params p;
@@ -671,11 +799,23 @@ int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float
   p.T = static_cast<int>(T);
   p.H = static_cast<int>(H);
   p.has_g = g != nullptr;
-  // Split V in two when that is needed to give every SM a sequence.
-  // GLAUCIS_GLA_VS=64|128 overrides the choice.
-  bool split = B * H * 2 <= num_sms;
-  if (const char* e = std::getenv("GLAUCIS_GLA_VS")) split = std::atoi(e) == 64;
-  if (split) {
+  // Few (batch, head) pairs: split the sequence into segments (full V width,
+  // one CTA per SM) when the workspace allows it, else split V in two.
+  // GLAUCIS_GLA_VS=64|128 and GLAUCIS_GLA_SEGMENTS=n override the choice.
+  int nseg = gla_segments(B, T, H, num_sms);
+  while (nseg > 1 && (ws == nullptr || gla_ws_bytes(B, H, nseg) > ws_bytes)) --nseg;
+  p.nseg = nseg;
+  p.seg_grid = nseg;
+  if (nseg > 1) {
+    const size_t rec = static_cast<size_t>(B * H) * static_cast<size_t>(nseg - 1);
+    p.ws_h = static_cast<float*>(ws);
+    p.ws_d = reinterpret_cast<float*>(static_cast<char*>(ws) + ((rec * 128 * 128 * 4 + 255) / 256) * 256);
+  } else {
+    p.ws_h = p.ws_d = nullptr;
+  }
+  bool split_v = nseg == 1 && B * H * 2 <= num_sms;
+  if (const char* e = std::getenv("GLAUCIS_GLA_VS")) split_v = std::atoi(e) == 64;
+  if (split_v) {
     p.nsplit = 2;
     return launch_vs<64>(q, k, v, g, p, st, why);
   }

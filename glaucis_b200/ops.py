@@ -180,9 +180,14 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if output_final_state and ht is None:
         ht = torch.empty((B, H, K, V), dtype=torch.float32, device=q.device)
     lib = _lib.load()
-    _lib.check(lib.gl_chunk_gla_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
-                                    _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
-                                    chunk_size, o.data_ptr(), _ptr(ht), None, _stream()),
+    # Few (batch, head) pairs: the library splits the sequence and needs a
+    # workspace for the per-segment states (0 bytes otherwise).
+    ws_bytes = lib.gl_chunk_gla_fwd_workspace_bytes(B, T, H, K, V, chunk_size)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+    _lib.check(lib.gl_chunk_gla_fwd_ws(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
+                                       _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
+                                       chunk_size, o.data_ptr(), _ptr(ht), _ptr(ws), ws_bytes,
+                                       None, _stream()),
                "gl_chunk_gla_fwd")
     return GLAForward(o, ht if output_final_state else None)
 

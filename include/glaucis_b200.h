@@ -121,6 +121,28 @@ int gl_chunk_gla_fwd(const void* q, const void* k, const void* v, const float* g
                      int64_t chunk_size, void* o, float* ht, int* err_word,
                      void* stream);
 
+/*
+ * gl_chunk_gla_fwd with a caller-owned device workspace.  When B*H is small
+ * against the SM count (few heads, long sequences) the sequence is split into
+ * segments: a state-only pass computes each segment's final state from a
+ * zero state and its total decay into the workspace, and the full pass starts
+ * every segment from h0 folded with the preceding segments' records, so the
+ * recurrence runs on one CTA per SM instead of one per (batch, head).
+ * gl_chunk_gla_fwd_workspace_bytes gives the size the split wants on the
+ * current device (0: no split for this shape); a smaller workspace gives
+ * fewer segments, NULL / 0 none.  The workspace must be 256-byte aligned and
+ * not be used by another call in flight.  gl_chunk_gla_fwd is this call with
+ * no workspace.  No reference counterpart: the reference scans the sequence
+ * once per (batch, head) (KE/examples/kernels/chunk_gla.py:94-138).
+ */
+size_t gl_chunk_gla_fwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K,
+                                        int64_t V, int64_t chunk_size);
+int gl_chunk_gla_fwd_ws(const void* q, const void* k, const void* v, const float* g,
+                        const float* g_gamma, const float* h0, float scale,
+                        int64_t B, int64_t T, int64_t H, int64_t K, int64_t V,
+                        int64_t chunk_size, void* o, float* ht, void* workspace,
+                        size_t workspace_bytes, int* err_word, void* stream);
+
 /* Largest M*K accepted by gl_gmm_fp8_act_fwd_noalloc (activation elements). */
 #define GL_NOALLOC_MAX_ACT_ELEMS (16u * 1024u * 1024u)
 

@@ -13,7 +13,7 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "gl
 
 def declared_symbols():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\s*\*)\s*(gl_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\s*\*)\s*(gl_\w+)\s*\(", text, re.M)))
 
 
 def test_header_declares_the_abi():
@@ -57,6 +57,15 @@ def test_gla_rejects_bad_arguments_without_device():
     assert rc == _lib.GL_EINVAL and "multiple of 64" in _err()
     rc = lib.gl_chunk_gla_fwd(p, p, p, f, None, None, 0.1, 1, 64, 1, 128, 128, 32, p, None, None, None)
     assert rc == _lib.GL_EINVAL and "chunk_size" in _err()
+    # the workspace variant: same checks, plus a 256-byte aligned workspace
+    rc = lib.gl_chunk_gla_fwd_ws(p, p, p, f, f, None, 0.1, 1, 64, 1, 128, 128, 64, p, None,
+                                 None, 0, None, None)
+    assert rc == _lib.GL_EINVAL and "exactly one" in _err()
+    rc = lib.gl_chunk_gla_fwd_ws(p, p, p, f, None, None, 0.1, 1, 64, 1, 128, 128, 64, p, None,
+                                 ctypes.c_void_p(272), 4096, None, None)
+    assert rc == _lib.GL_EINVAL and "256-byte" in _err()
+    # workspace size query: 0 for unsupported shapes (no device needed)
+    assert lib.gl_chunk_gla_fwd_workspace_bytes(1, 100, 1, 128, 128, 64) == 0
 
 
 def test_quantisers_reject_bad_arguments_without_device():

@@ -73,6 +73,25 @@ def test_gla_gamma_gate_reference_mode(cuda):
     _check(*_run(cuda, cfg, seed=5), what="g_gamma")
 
 
+@pytest.mark.parametrize("nseg", [2, 3, 7])
+@pytest.mark.parametrize("gate", ["per_key", "gamma"])
+def test_gla_sequence_split(cuda, monkeypatch, nseg, gate):
+    # Sequence split into nseg segments (state-only pass + full pass seeded
+    # from the folded segment states), uneven segment lengths (20 chunks).
+    monkeypatch.setenv("GLAUCIS_GLA_SEGMENTS", str(nseg))
+    cfg = configs.GLAConfig("t", B=1, T=64 * 20, H=2, gate=gate,
+                            h0_std=0.1 if gate == "per_key" else 0.0)
+    _check(*_run(cuda, cfg, seed=7), what=f"split {nseg} {gate}")
+
+
+def test_gla_split_workspace_query(cuda):
+    from glaucis_b200 import _lib
+    lib = _lib.load()
+    # few heads, long sequence: split (one CTA per SM); many heads: none
+    assert lib.gl_chunk_gla_fwd_workspace_bytes(1, 32768, 32, 128, 128, 64) > 0
+    assert lib.gl_chunk_gla_fwd_workspace_bytes(8, 4096, 16, 128, 128, 64) == 0
+
+
 def test_gla_single_chunk(cuda):
     cfg = configs.GLAConfig("t", B=1, T=64, H=1, h0_std=0.1)
     _check(*_run(cuda, cfg, seed=2), what="T=C")
