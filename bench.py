@@ -41,6 +41,7 @@ sys.path.insert(0, ROOT)
 METRIC = "FP8 GMM TFLOP/s & chunk_gla fwd tokens/s at 1/2/4/8 B200, % of roofline"
 HEADLINE = "gmm_moe_up"
 GLA_WORKLOAD = "gla_b8_t4096"
+GLA_LONG_WORKLOAD = "gla_b1_t32768"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -371,8 +372,20 @@ def run_b200(args):
     roof["algorithmic_flops_per_launch"] = flops
 
     # quantiser rows (separately timed kernels of the same forward)
-    q_act_ms = timed(lambda: ops.quant_act_1x128(lhs), max(3, args.steps // 4), 2, world)
-    q_w_ms = timed(lambda: ops.quant_w_128x128(rhs), 3, 1, world)
+    # outputs preallocated: the timed region holds the quantiser kernels only
+    qa_o, sa_o = torch.empty_like(a_q), torch.empty_like(a_s)
+    qw_o, sw_o = torch.empty_like(b_q), torch.empty_like(b_s)
+    q_act_ms = timed(lambda: ops.quant_act_1x128(lhs, qa_o, sa_o), max(5, args.steps // 2), 3, world)
+    q_w_ms = timed(lambda: ops.quant_w_128x128(rhs, qw_o, sw_o), max(5, args.steps // 10), 3, world)
+    del qa_o, sa_o, qw_o, sw_o
+    # algorithmic bytes: bf16 in, e4m3 out, fp32 scales out
+    q_act_bytes = lhs.numel() * 3 + lhs.numel() // 128 * 4
+    q_w_bytes = rhs.numel() * 3 + rhs.numel() // (128 * 128) * 4
+    quantisers = {
+        name: {"ms": ms_, "achieved_gbs": by / (ms_ * 1e-3) / 1e9,
+               "frac": by / (ms_ * 1e-3) / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": by}
+        for name, ms_, by in (("quant_act_1x128", q_act_ms, q_act_bytes),
+                              ("quant_w_128x128", q_w_ms, q_w_bytes))}
 
     # ---------------------------------------------------------------- e2e
     e2e = None
@@ -403,28 +416,37 @@ def run_b200(args):
     torch.cuda.empty_cache()
 
     # ---------------------------------------------------------------- GLA
-    gcfg = configs.GLA_CONFIGS[GLA_WORKLOAD]
-    inp = configs.make_gla_inputs(gcfg, device="cuda", seed=args.seed + rank)
-    go = torch.empty_like(inp["v"])
-    ght = torch.empty((gcfg.B, gcfg.H, 128, 128), device="cuda")
+    def gla_block(workload):
+        gcfg = configs.GLA_CONFIGS[workload]
+        inp = configs.make_gla_inputs(gcfg, device="cuda", seed=args.seed + rank)
+        go = torch.empty_like(inp["v"])
+        ght = torch.empty((gcfg.B, gcfg.H, 128, 128), device="cuda")
 
-    def gla_step():
-        ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], 128 ** -0.5, 64,
-                          g=inp["g"], h0=inp["h0"], output_final_state=True, o=go, ht=ght)
+        def gla_step():
+            ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], 128 ** -0.5, 64,
+                              g=inp["g"], h0=inp["h0"], output_final_state=True, o=go, ht=ght)
 
-    gla_ms = timed(gla_step, args.steps, args.warmup, world)
-    if ops.device_status() != 0:
-        raise SystemExit("device error word set after the GLA timed region")
-    gla_bytes = GO.gla_bytes(gcfg.B, gcfg.T, gcfg.H, has_h0=gcfg.h0_std > 0)
-    gla_flops = GO.gla_flops(gcfg.B, gcfg.T, gcfg.H)
-    gla_gbs = gla_bytes / (gla_ms * 1e-3) / 1e9
-    gla = {"workload": GLA_WORKLOAD, "B": gcfg.B, "T": gcfg.T, "H": gcfg.H,
-           "tokens_per_s": world * gcfg.B * gcfg.T / (gla_ms * 1e-3), "ms_per_step": gla_ms,
-           "tflops": world * gla_flops / (gla_ms * 1e-3) / 1e12,
-           "roofline": {"bound": "hbm", "achieved": gla_gbs, "peak": peaks["hbm_gbs"],
-                        "unit": "GB/s", "frac": gla_gbs / peaks["hbm_gbs"],
-                        "bf16_tensor_frac": gla_flops / (gla_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
-                        "kernel": "chunk_gla_fwd_kernel", "peak_source": f"{peak_kind} hbm_gbs"}}
+        gla_ms = timed(gla_step, args.steps, args.warmup, world)
+        if ops.device_status() != 0:
+            raise SystemExit("device error word set after the GLA timed region")
+        gla_bytes = GO.gla_bytes(gcfg.B, gcfg.T, gcfg.H, has_h0=gcfg.h0_std > 0)
+        gla_flops = GO.gla_flops(gcfg.B, gcfg.T, gcfg.H)
+        gla_gbs = gla_bytes / (gla_ms * 1e-3) / 1e9
+        blk = {"workload": workload, "B": gcfg.B, "T": gcfg.T, "H": gcfg.H,
+               "tokens_per_s": world * gcfg.B * gcfg.T / (gla_ms * 1e-3), "ms_per_step": gla_ms,
+               "tflops": world * gla_flops / (gla_ms * 1e-3) / 1e12,
+               "roofline": {"bound": "hbm", "achieved": gla_gbs, "peak": peaks["hbm_gbs"],
+                            "unit": "GB/s", "frac": gla_gbs / peaks["hbm_gbs"],
+                            "bf16_tensor_frac": gla_flops / (gla_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+                            "kernel": "chunk_gla_fwd_kernel", "peak_source": f"{peak_kind} hbm_gbs",
+                            "algorithmic_bytes_per_step": gla_bytes,
+                            "traffic": ncu_traffic("chunk_gla_fwd_kernel", workload)}}
+        del inp, go, ght
+        torch.cuda.empty_cache()
+        return blk
+
+    gla = gla_block(GLA_WORKLOAD)
+    gla_long = gla_block(GLA_LONG_WORKLOAD)
 
     # ------------------------------------------------------- CPU baseline
     cpu = None
@@ -455,8 +477,9 @@ def run_b200(args):
             "e2e": e2e,
             "gpu_launches": args.steps,
             "clocks": sampler.summary() if sampler else None,
-            "quantisers_ms": {"quant_act_1x128": q_act_ms, "quant_w_128x128": q_w_ms},
+            "quantisers": quantisers,
             "gla": gla,
+            "gla_long": gla_long,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -468,7 +491,8 @@ def run_b200(args):
 def run_profile(args):
     """Small-footprint run of one kernel for ncu captures: the GMM on the
     headline workload with the bf16 weights freed after quantisation (about
-    2.3 GB resident), or the GLA forward on its workload."""
+    2.3 GB resident), the two quantisers on a slice of its operands, or the
+    GLA forward on its workload."""
     import torch
     from glaucis_b200 import configs, ops
     torch.cuda.set_device(0)
@@ -481,6 +505,16 @@ def run_profile(args):
         torch.cuda.empty_cache()
         out = torch.empty((cfg.M, cfg.N), dtype=torch.bfloat16, device="cuda")
         fn = lambda: ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs, out=out)
+    elif args.profile == "quant":
+        # both quantisers on a slice of the headline operands: activations
+        # [16384, 7168] (235 MB bf16) and 16 experts [16, 7168, 2048] (470 MB)
+        gen = torch.Generator(device="cuda").manual_seed(args.seed)
+        x = torch.randn((16384, 7168), device="cuda", generator=gen).to(torch.bfloat16)
+        w = (torch.randn((16, 7168, 2048), device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+
+        def fn():
+            ops.quant_act_1x128(x)
+            ops.quant_w_128x128(w)
     else:
         gcfg = configs.GLA_CONFIGS[args.gla_workload]
         inp = configs.make_gla_inputs(gcfg, device="cuda", seed=args.seed)
@@ -506,7 +540,7 @@ def main(argv=None):
     ap.add_argument("--cpu-rows", type=int, default=8192,
                     help="rows of the headline workload in one CPU-baseline step")
     ap.add_argument("--cpu-gla-tokens", type=int, default=4096)
-    ap.add_argument("--profile", choices=["gmm", "gla"], default=None,
+    ap.add_argument("--profile", choices=["gmm", "gla", "quant"], default=None,
                     help="run one kernel only, small footprint (for ncu captures)")
     ap.add_argument("--gla-workload", default=GLA_WORKLOAD)
     args = ap.parse_args(argv)

@@ -37,8 +37,19 @@ def _need_cuda(*ts: Optional[torch.Tensor]) -> None:
 # ---------------------------------------------------------------------------
 # Block-wise FP8 quantisers
 # ---------------------------------------------------------------------------
-def quant_act_1x128(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-    """bf16 [M, K] -> (e4m3 [M, K], fp32 scales [M, K/128]).
+def _out(t: Optional[torch.Tensor], shape, dtype, device, name: str) -> torch.Tensor:
+    """A preallocated contiguous output of the given shape / dtype, or a new one."""
+    if t is None:
+        return torch.empty(shape, dtype=dtype, device=device)
+    if tuple(t.shape) != tuple(shape) or t.dtype != dtype or not t.is_contiguous() or t.device != device:
+        raise ValueError(f"{name} must be a contiguous {dtype} tensor of shape {tuple(shape)} on {device}")
+    return t
+
+
+def quant_act_1x128(x: torch.Tensor, q: Optional[torch.Tensor] = None,
+                    s: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [M, K] -> (e4m3 [M, K], fp32 scales [M, K/128]); `q` / `s` may be
+    given as preallocated outputs.
 
     Replaces qwix.pallas.quantize(lhs, channelwise_axes=[0], tiled_axes={1: 128},
     absmax, fp32 scale) at KE/examples/kernels/gmm_fp8_blockwise.py:84-91.
@@ -47,16 +58,18 @@ def quant_act_1x128(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     if x.dtype != torch.bfloat16 or x.dim() != 2:
         raise ValueError("quant_act_1x128 expects a 2-D bf16 tensor")
     M, K = x.shape
-    q = torch.empty((M, K), dtype=FP8, device=x.device)
-    s = torch.empty((M, K // TILE), dtype=torch.float32, device=x.device)
+    q = _out(q, (M, K), FP8, x.device, "q")
+    s = _out(s, (M, K // TILE), torch.float32, x.device, "s")
     lib = _lib.load()
     _lib.check(lib.gl_quant_act_1x128(x.data_ptr(), M, K, q.data_ptr(), s.data_ptr(), None,
                                       _stream()), "gl_quant_act_1x128")
     return q, s
 
 
-def quant_w_128x128(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-    """bf16 [G, K, N] -> (e4m3 [G, K, N], fp32 scales [G, K/128, N/128]).
+def quant_w_128x128(w: torch.Tensor, q: Optional[torch.Tensor] = None,
+                    s: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [G, K, N] -> (e4m3 [G, K, N], fp32 scales [G, K/128, N/128]);
+    `q` / `s` may be given as preallocated outputs.
 
     Replaces qwix.pallas.quantize(rhs, channelwise_axes=[0],
     tiled_axes={1: 128, 2: 128}) at KE/examples/kernels/gmm_fp8_blockwise.py:100-107.
@@ -65,8 +78,8 @@ def quant_w_128x128(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     if w.dtype != torch.bfloat16 or w.dim() != 3:
         raise ValueError("quant_w_128x128 expects a 3-D bf16 tensor")
     G, K, N = w.shape
-    q = torch.empty((G, K, N), dtype=FP8, device=w.device)
-    s = torch.empty((G, K // TILE, N // TILE), dtype=torch.float32, device=w.device)
+    q = _out(q, (G, K, N), FP8, w.device, "q")
+    s = _out(s, (G, K // TILE, N // TILE), torch.float32, w.device, "s")
     lib = _lib.load()
     _lib.check(lib.gl_quant_w_128x128(w.data_ptr(), G, K, N, q.data_ptr(), s.data_ptr(), None,
                                       _stream()), "gl_quant_w_128x128")
