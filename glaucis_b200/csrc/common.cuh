@@ -250,6 +250,18 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
                  "+r"(r[i + 4]), "+r"(r[i + 5]), "+r"(r[i + 6]), "+r"(r[i + 7]));
 }
 
+// Waits for every outstanding tcgen05.ld of the thread; both destination
+// arrays become valid afterwards.
+__device__ __forceinline__ void tmem_ld_wait2(uint32_t (&r0)[32], uint32_t (&r1)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    asm volatile("" : "+r"(r0[i]), "+r"(r0[i + 1]), "+r"(r0[i + 2]), "+r"(r0[i + 3]),
+                 "+r"(r0[i + 4]), "+r"(r0[i + 5]), "+r"(r0[i + 6]), "+r"(r0[i + 7]));
+    asm volatile("" : "+r"(r1[i]), "+r"(r1[i + 1]), "+r"(r1[i + 2]), "+r"(r1[i + 3]),
+                 "+r"(r1[i + 4]), "+r"(r1[i + 5]), "+r"(r1[i + 6]), "+r"(r1[i + 7]));
+  }
+}
 __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll

@@ -16,7 +16,7 @@
 //   warp 3      derives the ragged tile table from group_sizes.
 //   warps 4-11  promotion + epilogue (two warpgroups, BN/2 columns each):
 //               after every K block each thread reads its row's columns of
-//               the partial sum out of TMEM (double-buffered 32-column loads)
+//               the partial sum out of TMEM (32-column loads, two in flight)
 //               and accumulates partial * (a_s * b_s) in fp32 registers with
 //               packed f32x2 FMAs, releasing the TMEM buffer so later K
 //               blocks' MMAs overlap the promotion.  The finished row is
@@ -50,6 +50,7 @@ struct Cfg {
   static constexpr int NBUF = TMEM_COLS / BN;                  // TMEM accumulators: 2 / 4
   static constexpr int EC = BN / 2;                            // columns per promotion thread
   static constexpr int NCH = EC / 32;                          // 32-column TMEM loads per K block
+  static_assert(NCH % 2 == 0, "TMEM loads go in pairs");
   static constexpr uint32_t OFF_A = 0;
   static constexpr uint32_t OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_B + STAGES * B_BYTES;
@@ -310,19 +311,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             acc[base + j] = __ffma2_rn(make_float2(__uint_as_float(x[2 * j]), __uint_as_float(x[2 * j + 1])),
                                        sc2, acc[base + j]);
         };
-        // chunk c is loaded while chunk c-1 is promoted
+        // Chunks are loaded two at a time; the next pair's loads are issued
+        // between the promotions of the current pair, and the accumulator is
+        // released as soon as the last pair has landed (the last two
+        // promotions run after the release).
         tmem_ld32(ta, v[0]);
-        tmem_ld_wait(v[0]);
+        tmem_ld32(ta + 32, v[1]);
+        tmem_ld_wait2(v[0], v[1]);
 #pragma unroll
-        for (int c = 1; c < NCH; ++c) {
-          tmem_ld32(ta + 32 * c, v[c & 1]);
-          promote(v[(c - 1) & 1], 16 * (c - 1));
-          tmem_ld_wait(v[c & 1]);
+        for (int c = 2; c < NCH; c += 2) {
+          promote(v[0], 16 * (c - 2));
+          tmem_ld32(ta + 32 * c, v[0]);
+          promote(v[1], 16 * (c - 1));
+          tmem_ld32(ta + 32 * (c + 1), v[1]);
+          tmem_ld_wait2(v[0], v[1]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[buf]);
-        promote(v[(NCH - 1) & 1], 16 * (NCH - 1));
+        promote(v[0], 16 * (NCH - 2));
+        promote(v[1], 16 * (NCH - 1));
       }
       if (!ok) break;
       if (row_ok && col_ok) {
@@ -542,17 +550,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                        sc2, acc[base + j]);
         };
         tmem_ld32(ta, v[0]);
-        tmem_ld_wait(v[0]);
+        tmem_ld32(ta + 32, v[1]);
+        tmem_ld_wait2(v[0], v[1]);
 #pragma unroll
-        for (int c = 1; c < NCH; ++c) {
-          tmem_ld32(ta + 32 * c, v[c & 1]);
-          promote(v[(c - 1) & 1], 16 * (c - 1));
-          tmem_ld_wait(v[c & 1]);
+        for (int c = 2; c < NCH; c += 2) {
+          promote(v[0], 16 * (c - 2));
+          tmem_ld32(ta + 32 * c, v[0]);
+          promote(v[1], 16 * (c - 1));
+          tmem_ld32(ta + 32 * (c + 1), v[1]);
+          tmem_ld_wait2(v[0], v[1]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(buf ? tempty_c1 : tempty_c0);
-        promote(v[(NCH - 1) & 1], 16 * (NCH - 1));
+        promote(v[0], 16 * (NCH - 2));
+        promote(v[1], 16 * (NCH - 1));
       }
       if (!ok) break;
       if (row_ok && col_ok) {

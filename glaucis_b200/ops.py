@@ -146,6 +146,122 @@ def gmm_fp8_blockwise(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.T
     return out
 
 
+_SIDE_STREAMS = {}
+
+
+def _side_streams(device: torch.device):
+    """Three per-device streams (copy-in, compute, copy-out) for the host op."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    if key not in _SIDE_STREAMS:
+        with torch.cuda.device(key):
+            _SIDE_STREAMS[key] = (torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream())
+    return _SIDE_STREAMS[key]
+
+
+def _plan_chunks(sizes, chunks: int, min_rows: int = 1024):
+    """Row ranges [r0, r1) of about equal size over the assigned rows, each
+    with the index of its first group and its per-group row counts (a group
+    may be split between consecutive chunks)."""
+    import numpy as np
+    sizes = np.asarray(sizes, dtype=np.int64)
+    off = np.concatenate([[0], np.cumsum(sizes)])
+    total = int(off[-1])
+    n = max(1, min(chunks, total // min_rows if total >= min_rows else 1))
+    bounds = [total * i // n for i in range(n + 1)]
+    plan = []
+    for r0, r1 in zip(bounds[:-1], bounds[1:]):
+        if r1 <= r0:
+            continue
+        g_a = int(np.searchsorted(off, r0, side="right") - 1)
+        g_b = int(np.searchsorted(off, r1, side="left") - 1)
+        g_a = max(g_a, 0)
+        sub = [max(0, min(int(off[g + 1]), r1) - max(int(off[g]), r0)) for g in range(g_a, g_b + 1)]
+        plan.append((r0, r1, g_a, sub))
+    return plan, total
+
+
+def gmm_fp8_blockwise_host(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.Tensor,
+                           out: Optional[torch.Tensor] = None,
+                           out_dtype: torch.dtype = torch.bfloat16,
+                           chunks: int = 16, min_chunk_rows: int = 1024) -> torch.Tensor:
+    """`gmm_fp8_blockwise` for activations that arrive in host memory (the
+    serving case): `lhs` bf16 [M, K] in pinned host memory, `rhs` bf16
+    [G, K, N] on the GPU (the weights), `group_sizes` int32 [G] (host or
+    device); returns `out` [M, N] in pinned host memory (allocated when not
+    given).  The activation rows go to the device in `chunks` row ranges on a
+    copy stream (ranges of at least `min_chunk_rows` rows) while the ranges
+    already there are quantised and multiplied on
+    a compute stream, and finished output rows go back on a third stream, so
+    the PCIe transfers overlap the kernels.  The work is ordered after the
+    current stream and the current stream waits for all of it: the result is
+    valid once the current stream has been synchronised.  Same numbers as
+    `gmm_fp8_blockwise` (row ranges are computed by the same kernel).
+    """
+    if lhs.is_cuda or not lhs.is_pinned():
+        raise ValueError("lhs must be a pinned host tensor")
+    _need_cuda(rhs)
+    if lhs.dtype != torch.bfloat16 or rhs.dtype != torch.bfloat16 or lhs.dim() != 2 or rhs.dim() != 3:
+        raise ValueError("lhs bf16 [M, K] and rhs bf16 [G, K, N] expected")
+    M, K = lhs.shape
+    G, K2, N = rhs.shape
+    if K2 != K:
+        raise ValueError(f"K mismatch: lhs {K} vs rhs {K2}")
+    if group_sizes.dtype != torch.int32 or group_sizes.numel() != G:
+        raise ValueError("group_sizes must be int32 [G]")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, pin_memory=True)
+    elif out.is_cuda or not out.is_pinned() or tuple(out.shape) != (M, N) or out.dtype != out_dtype:
+        raise ValueError("out must be a pinned host tensor [M, N] of out_dtype")
+    sizes = group_sizes.cpu().numpy()
+    if (sizes < 0).any() or int(sizes.sum()) > M:
+        raise ValueError("group_sizes must be non-negative with sum <= M")
+    plan, total = _plan_chunks(sizes, chunks, min_chunk_rows)
+    if total < M:
+        out[total:].zero_()  # rows that belong to no group
+    if total == 0:
+        return out
+    dev = rhs.device
+    s_in, s_c, s_out = _side_streams(dev)
+    cur = torch.cuda.current_stream(dev)
+    start = cur.record_event()
+    for st in (s_in, s_c, s_out):
+        st.wait_event(start)
+    tab = torch.zeros((len(plan), G), dtype=torch.int32, pin_memory=True)
+    for c, (_, _, _, sub) in enumerate(plan):
+        tab[c, :len(sub)] = torch.tensor(sub, dtype=torch.int32)
+    lhs_d = torch.empty((M, K), dtype=torch.bfloat16, device=dev)
+    a_q = torch.empty((M, K), dtype=FP8, device=dev)
+    a_s = torch.empty((M, K // TILE), dtype=torch.float32, device=dev)
+    out_d = torch.empty((M, N), dtype=out_dtype, device=dev)
+    with torch.cuda.stream(s_in):
+        tab_d = tab.to(dev, non_blocking=True)
+    tab_ready = s_in.record_event()
+    with torch.cuda.stream(s_c):
+        b_q, b_s = quant_w_128x128(rhs)
+        s_c.wait_event(tab_ready)
+    for c, (r0, r1, g_a, sub) in enumerate(plan):
+        g_b = g_a + len(sub)
+        with torch.cuda.stream(s_in):
+            lhs_d[r0:r1].copy_(lhs[r0:r1], non_blocking=True)
+            landed = s_in.record_event()
+        with torch.cuda.stream(s_c):
+            s_c.wait_event(landed)
+            quant_act_1x128(lhs_d[r0:r1], a_q[r0:r1], a_s[r0:r1])
+            gmm_fp8_fwd(a_q[r0:r1], a_s[r0:r1], b_q[g_a:g_b], b_s[g_a:g_b], tab_d[c, :len(sub)],
+                        out=out_d[r0:r1])
+            done = s_c.record_event()
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done)
+            out[r0:r1].copy_(out_d[r0:r1], non_blocking=True)
+    # keep the device buffers alive for the side streams, then join them
+    for t in (lhs_d, a_q, a_s, out_d, tab_d, b_q, b_s):
+        for st in (s_in, s_c, s_out):
+            t.record_stream(st)
+    for st in (s_in, s_c, s_out):
+        cur.wait_stream(st)
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Chunked GLA forward
 # ---------------------------------------------------------------------------

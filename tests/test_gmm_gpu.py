@@ -144,6 +144,25 @@ def test_gmm_tail_rows_zero_in_public_op(cuda):
     assert torch.count_nonzero(out[250:]) == 0
 
 
+@pytest.mark.parametrize("chunks", [1, 3, 7])
+def test_gmm_host_pipeline_matches_device_op(cuda, chunks):
+    # Activations in pinned host memory, streamed in row chunks (groups split
+    # between chunks, an empty group, rows past sum(group_sizes)): the result
+    # is the device op's result bit for bit.
+    g = torch.Generator().manual_seed(11)
+    G, M, K, N = 6, 3000, 256, 384
+    sizes = [700, 0, 1100, 64, 900, 100]          # sum 2864 < M
+    lhs = torch.randn((M, K), generator=g).to(torch.bfloat16)
+    rhs = (torch.randn((G, K, N), generator=g) * 0.02).to(torch.bfloat16).to(cuda)
+    gs = torch.tensor(sizes, dtype=torch.int32)
+    ref = ops.gmm_fp8_blockwise(lhs.to(cuda), rhs, gs.to(cuda), out_dtype=torch.bfloat16)
+    out = ops.gmm_fp8_blockwise_host(lhs.pin_memory(), rhs, gs, chunks=chunks, min_chunk_rows=128)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert out.is_pinned() and not out.is_cuda
+    assert torch.equal(out, ref.cpu())
+
+
 def test_gmm_bad_group_sizes_set_error_word(cuda):
     # The kernel validates group_sizes on the device and reports through the
     # error word instead of reading out of bounds.
