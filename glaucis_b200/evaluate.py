@@ -11,7 +11,8 @@ variant, ``EVAL_RESULT:{json}`` with status COMPILE_ERROR / INCORRECT /
 SUCCESS, fitness (= speedup), latency_ms, speedup, flops and metadata
 (benchmark statistics of the kernel and the reference).
 
-Stages (KE/docker/evaluate.py:98-424, 928-1072):
+Stages (KE/docker/evaluate.py:98-424, 928-1072), plus an optional deep
+profile (request key "deep_profile": true, KE/docker/evaluate.py:478-889):
   1. compile      exec() the template text (stage_compile :98-104)
   2. correctness  each shape: kernel fn vs reference fn; scalar results must
                   satisfy max|diff| <= atol (:107-127); array results are
@@ -19,6 +20,8 @@ Stages (KE/docker/evaluate.py:98-424, 928-1072):
   3. benchmark    3 warm-up calls, then N calls each bracketed by CUDA events
                   on the current stream (replaces jax.jit + xprof clustering)
   4. reference    the same benchmark on the reference code -> speedup
+  5. deep profile ncu counters of one call (child process) -> compute_ratio,
+                  memory_transfer_ratio, metadata.hw_utilization
 The TPU-specific stages (libtpu dumps, XPlane parsing, HLO/LLO analysis,
 GCS upload) have no counterpart here.
 """
@@ -191,6 +194,144 @@ def forward_flops(shape: dict) -> float:
     return 0.0
 
 
+# ---------------------------------------------------------------------------
+# Deep profile (replaces the TPU evaluator's xprof counters / LLO analysis,
+# KE/docker/evaluate.py:286-377, 427-475, 478-889): the kernel function runs
+# once more in a child process under ncu, restricted to a cudaProfilerStart /
+# Stop window around one call, and the per-launch counters are averaged
+# (weighted by launch time) into the result's compute_ratio /
+# memory_transfer_ratio and metadata["hw_utilization"].
+# ---------------------------------------------------------------------------
+NCU_METRICS = {
+    "gpu__time_duration.sum": "duration_ns",
+    "sm__throughput.avg.pct_of_peak_sustained_elapsed": "sm_throughput_pct",
+    "gpu__dram_throughput.avg.pct_of_peak_sustained_elapsed": "dram_util_pct",
+    "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed": "tensor_util_pct",
+    "sm__pipe_fma_cycles_active.avg.pct_of_peak_sustained_elapsed": "fma_util_pct",
+    "sm__pipe_alu_cycles_active.avg.pct_of_peak_sustained_elapsed": "alu_util_pct",
+    "sm__pipe_shared_cycles_active.avg.pct_of_peak_sustained_elapsed": "shared_pipe_util_pct",
+    "smsp__issue_active.avg.pct_of_peak_sustained_active": "issue_active_pct",
+    "l1tex__throughput.avg.pct_of_peak_sustained_elapsed": "l1_util_pct",
+    "lts__throughput.avg.pct_of_peak_sustained_elapsed": "l2_util_pct",
+    "dram__bytes_read.sum": "dram_read_bytes",
+    "dram__bytes_write.sum": "dram_write_bytes",
+}
+_UNIT_SCALE = {"byte": 1.0, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "Tbyte": 1e12,
+               "nsecond": 1.0, "usecond": 1e3, "msecond": 1e6, "second": 1e9,
+               "ns": 1.0, "us": 1e3, "ms": 1e6, "s": 1e9, "%": 1.0, "": 1.0}
+
+
+def parse_ncu_csv(text: str) -> list:
+    """ncu `--csv` output (one row per launch and metric) -> one dict per
+    launch: {"kernel": name, <NCU_METRICS keys>: value in bytes / ns / %}."""
+    import csv
+    import io
+    lines = [ln for ln in text.splitlines() if ln.startswith('"')]
+    if not lines:
+        return []
+    rows = list(csv.reader(io.StringIO("\n".join(lines))))
+    hdr = rows[0]
+    need = ("ID", "Kernel Name", "Metric Name", "Metric Unit", "Metric Value")
+    if not all(h in hdr for h in need):
+        return []
+    ix = {h: hdr.index(h) for h in need}
+    launches = {}
+    for r in rows[1:]:
+        if len(r) < len(hdr):
+            continue
+        name = r[ix["Metric Name"]]
+        if name not in NCU_METRICS:
+            continue
+        try:
+            val = float(r[ix["Metric Value"]].replace(",", ""))
+        except ValueError:
+            continue
+        val *= _UNIT_SCALE.get(r[ix["Metric Unit"]], 1.0)
+        d = launches.setdefault(r[ix["ID"]], {"kernel": r[ix["Kernel Name"]]})
+        d[NCU_METRICS[name]] = val
+    return list(launches.values())
+
+
+def summarize_launches(launches: list) -> dict:
+    """Time-weighted averages of the per-launch counters.  compute_ratio is
+    the SM share and memory_transfer_ratio the DRAM share of
+    (SM throughput % + DRAM throughput %), so the two add up to 1 as the TPU
+    evaluator's compute / memory-transfer split does."""
+    tot = sum(l.get("duration_ns", 0.0) for l in launches)
+    if not launches or tot <= 0:
+        return {"ok": False, "error": "no profiled launches"}
+    util = {}
+    for key in NCU_METRICS.values():
+        if key in ("duration_ns", "dram_read_bytes", "dram_write_bytes"):
+            continue
+        vals = [(l[key], l.get("duration_ns", 0.0)) for l in launches if key in l]
+        if vals:
+            util[key] = sum(v * w for v, w in vals) / max(sum(w for _, w in vals), 1e-30)
+    util["dram_bytes"] = sum(l.get("dram_read_bytes", 0.0) + l.get("dram_write_bytes", 0.0)
+                             for l in launches)
+    util["kernel_time_ms"] = tot / 1e6
+    util["launches"] = len(launches)
+    sm, dram = util.get("sm_throughput_pct", 0.0), util.get("dram_util_pct", 0.0)
+    share = sm / (sm + dram) if sm + dram > 0 else None
+    return {"ok": True, "compute_ratio": share,
+            "memory_transfer_ratio": None if share is None else 1.0 - share,
+            "hw_utilization": util,
+            "kernels": sorted({l["kernel"] for l in launches})}
+
+
+def profile_command(payload_b64: str, ncu: str = "ncu") -> list:
+    """ncu command that profiles the launches of one kernel call (the child
+    brackets the call with cudaProfilerStart / Stop)."""
+    return [ncu, "--profile-from-start", "off", "--clock-control", "none", "--csv",
+            "--print-units", "base", "--metrics", ",".join(NCU_METRICS), sys.executable, "-m", "glaucis_b200.evaluate",
+            "--profile-child", payload_b64]
+
+
+def _profile_child(request: dict) -> int:
+    """Child side of the deep profile: compile, one warm-up call, then one
+    call inside the profiler window."""
+    import torch
+    comp = stage_compile(request["kernel_code"])
+    if not comp["ok"]:
+        print(comp["error"], file=sys.stderr)
+        return 1
+    fn = _resolve_compute_fn(comp["globals"], allow_reference=True)
+    shape = request["shapes"][0]
+    fn(**shape)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    fn(**shape)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    return 0
+
+
+def stage_profile_deep(request: dict, runner: Optional[Callable] = None, timeout: int = 600) -> dict:
+    """Runs the child once without ncu (it must exit 0 first) and once under
+    ncu, then summarises the counters.  `runner(argv) -> (returncode, stdout,
+    stderr)` replaces subprocess for tests."""
+    import shutil
+    if runner is None:
+        ncu = shutil.which("ncu") or "/usr/local/cuda/bin/ncu"
+        if not os.path.exists(ncu):
+            return {"ok": False, "error": "ncu not found"}
+
+        def runner(argv):
+            p = subprocess.run(argv, capture_output=True, text=True, timeout=timeout)
+            return p.returncode, p.stdout, p.stderr
+    else:
+        ncu = "ncu"
+    payload = encode_request({"kernel_code": request["kernel_code"], "shapes": request["shapes"]})
+    plain = [sys.executable, "-m", "glaucis_b200.evaluate", "--profile-child", payload]
+    rc, _, err = runner(plain)
+    if rc != 0:
+        return {"ok": False, "error": f"profile child failed without ncu: {err[-500:]}"}
+    rc, out, err = runner(profile_command(payload, ncu))
+    if rc != 0:
+        return {"ok": False, "error": f"ncu failed: {err[-500:]}"}
+    return summarize_launches(parse_ncu_csv(out))
+
+
 def evaluate(request: dict, timer: Optional[Callable] = None) -> dict:
     """Runs the stages for one variant and returns the result dict."""
     job = request.get("variant_id", "unknown")
@@ -210,15 +351,22 @@ def evaluate(request: dict, timer: Optional[Callable] = None) -> dict:
                  if ref_comp["ok"] else {"ok": False})
     ref_latency = ref_bench.get("latency_ms", bench["latency_ms"])
     speedup = ref_latency / bench["latency_ms"] if bench["latency_ms"] > 0 else 0.0
+    deep = stage_profile_deep(request) if request.get("deep_profile") else None
+    deep_ok = bool(deep and deep.get("ok"))
     return {
         "status": "SUCCESS", "variant_id": job, "fitness": speedup,
         "latency_ms": bench["latency_ms"], "speedup": speedup,
-        "flops": forward_flops(request["shapes"][0]), "compute_ratio": None,
-        "memory_transfer_ratio": None, "max_diff": corr["max_diff"],
+        "flops": forward_flops(request["shapes"][0]),
+        "compute_ratio": deep["compute_ratio"] if deep_ok else None,
+        "memory_transfer_ratio": deep["memory_transfer_ratio"] if deep_ok else None,
+        "max_diff": corr["max_diff"],
         "metadata": {"reference_latency_ms": ref_latency,
                      "reference_perf_ok": ref_bench.get("ok", False),
                      "benchmark": bench.get("benchmark"),
-                     "reference_benchmark": ref_bench.get("benchmark")},
+                     "reference_benchmark": ref_bench.get("benchmark"),
+                     "hw_utilization": deep.get("hw_utilization") if deep_ok else None,
+                     "profile": None if deep is None else
+                     {k: v for k, v in deep.items() if k not in ("hw_utilization",)}},
     }
 
 
@@ -258,7 +406,10 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description="CUDA evaluator backend (EVAL_RESULT contract)")
     ap.add_argument("--eval-payload")
     ap.add_argument("--eval-payload-file")
+    ap.add_argument("--profile-child", help=argparse.SUPPRESS)
     args = ap.parse_args(argv)
+    if args.profile_child:
+        return _profile_child(decode_request(args.profile_child))
     if args.eval_payload_file:
         with open(args.eval_payload_file) as f:
             b64 = f.read().strip()

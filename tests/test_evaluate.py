@@ -121,3 +121,64 @@ def test_template_conventions(name):
     assert "def optimized_compute(" in block
     assert "def _make_test_data(" in before
     assert "import" not in block
+
+
+# ---------------------------------------------------------------------------
+# deep profile stage (ncu counters), host logic only
+# ---------------------------------------------------------------------------
+_NCU_CSV = "\n".join([
+    '==PROF== Connected to process 1',
+    '"ID","Process ID","Process Name","Host Name","Kernel Name","Context","Stream","Block Size",'
+    '"Grid Size","Device","CC","Section Name","Metric Name","Metric Unit","Metric Value"',
+] + [
+    f'"{i}","1","python3","h","{k}","1","7","(384, 1, 1)","(148, 1, 1)","0","10.0",'
+    f'"Command line profiler metrics","{m}","{u}","{v}"'
+    for i, k, rows in [
+        (0, "void gl::gmm::gmm_fp8_fwd_kernel<256>(CUtensorMap_st, CUtensorMap_st, gl::gmm::Params)",
+         [("gpu__time_duration.sum", "ns", "300000"),
+          ("sm__throughput.avg.pct_of_peak_sustained_elapsed", "%", "60"),
+          ("gpu__dram_throughput.avg.pct_of_peak_sustained_elapsed", "%", "40"),
+          ("sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed", "%", "45"),
+          ("dram__bytes_read.sum", "byte", "1,000,000")]),
+        (1, "void quant::quant_kernel<0>(CUtensorMap_st, quant::Args)",
+         [("gpu__time_duration.sum", "ns", "100000"),
+          ("sm__throughput.avg.pct_of_peak_sustained_elapsed", "%", "20"),
+          ("gpu__dram_throughput.avg.pct_of_peak_sustained_elapsed", "%", "80"),
+          ("dram__bytes_write.sum", "Kbyte", "500")]),
+    ] for m, u, v in rows])
+
+
+def test_parse_ncu_csv_and_summary():
+    ls = E.parse_ncu_csv(_NCU_CSV)
+    assert len(ls) == 2
+    assert ls[0]["duration_ns"] == 300000 and ls[0]["dram_read_bytes"] == 1e6
+    assert ls[1]["dram_write_bytes"] == 5e5
+    s = E.summarize_launches(ls)
+    assert s["ok"] and s["hw_utilization"]["launches"] == 2
+    sm = (60 * 3 + 20) / 4.0
+    dram = (40 * 3 + 80) / 4.0
+    assert abs(s["hw_utilization"]["sm_throughput_pct"] - sm) < 1e-9
+    assert abs(s["compute_ratio"] - sm / (sm + dram)) < 1e-12
+    assert abs(s["compute_ratio"] + s["memory_transfer_ratio"] - 1.0) < 1e-12
+    assert s["hw_utilization"]["tensor_util_pct"] == 45.0   # only launches that report it
+    assert s["hw_utilization"]["dram_bytes"] == 1.5e6
+    assert abs(s["hw_utilization"]["kernel_time_ms"] - 0.4) < 1e-12
+
+
+def test_stage_profile_deep_runs_plain_then_ncu():
+    calls = []
+
+    def runner(argv):
+        calls.append(argv)
+        return (0, _NCU_CSV, "") if argv[0] == "ncu" else (0, "", "")
+
+    req = {"kernel_code": "def kernel_fn(n):\n    return n\n", "shapes": [{"n": 1}]}
+    r = E.stage_profile_deep(req, runner=runner)
+    assert r["ok"] and len(calls) == 2
+    assert calls[0][1:3] == ["-m", "glaucis_b200.evaluate"] and "--profile-child" in calls[0]
+    assert calls[1][0] == "ncu" and "--clock-control" in calls[1] and "none" in calls[1]
+    assert "--profile-from-start" in calls[1]
+    # a child that fails without ncu is never profiled
+    calls.clear()
+    r = E.stage_profile_deep(req, runner=lambda argv: calls.append(argv) or (1, "", "boom"))
+    assert not r["ok"] and len(calls) == 1
