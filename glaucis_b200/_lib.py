@@ -34,6 +34,9 @@ SIGNATURES = {
     "gl_chunk_gla_fwd_ws": (_I, [_P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64, _I64,
                                  _P, _P, _P, ctypes.c_size_t, _P, _P]),
     "gl_gmm_fp8_act_fwd_noalloc": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _P]),
+    "gl_quant_col_128x1": (_I, [_P, _I64, _I64, _P, _P, _P, _P]),
+    "gl_gmm_fp8_dlhs": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _P]),
+    "gl_tgmm_fp8": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _P]),
     "gl_device_status": (_I, [_P, _P, ctypes.POINTER(ctypes.c_int)]),
     "gl_last_error": (ctypes.c_char_p, []),
     "gl_version": (ctypes.c_char_p, []),

@@ -28,6 +28,16 @@ int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float
                         int64_t H, int64_t K, int64_t V, void* o, float* ht, void* ws,
                         size_t ws_bytes, int* err, cudaStream_t st, int num_sms, const char** why);
 size_t gl_chunk_gla_ws_bytes(int64_t B, int64_t T, int64_t H, int num_sms);
+int gl_launch_quant_col(const void* x, int64_t M, int64_t C, void* q, float* s, int* err,
+                        cudaStream_t st, int num_sms, const char** why);
+int gl_launch_gmm_fp8_dlhs(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
+                           const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                           void* out, int out_f32, int* err, cudaStream_t st, int num_sms,
+                           const char** why);
+int gl_launch_tgmm_fp8(const void* lq, const float* ls, const void* dq, const float* ds,
+                       const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                       void* out, int out_f32, int* err, cudaStream_t st, int num_sms,
+                       const char** why);
 
 namespace {
 
@@ -290,6 +300,74 @@ size_t gl_chunk_gla_fwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t
   DeviceState* d = nullptr;
   if (device_state(&d)) return 0;
   return gl_chunk_gla_ws_bytes(B, T, H, d->num_sms);
+}
+
+int gl_quant_col_128x1(const void* x, int64_t M, int64_t C, void* q, float* s, int* err_word,
+                       void* stream) {
+  if (!x || !q || !s) return fail(GL_EINVAL, "gl_quant_col_128x1: null pointer");
+  if (M <= 0 || C <= 0 || M % 128 != 0 || C % 128 != 0)
+    return fail(GL_EINVAL, "gl_quant_col_128x1: need M and C positive multiples of 128");
+  if (!aligned16(x) || !aligned16(q) || !aligned16(s))
+    return fail(GL_EINVAL, "gl_quant_col_128x1: x, q and s must be 16-byte aligned");
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  const char* why = "";
+  const int rc = gl_launch_quant_col(x, M, C, q, s, err_word ? err_word : d->err,
+                                     static_cast<cudaStream_t>(stream), d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string("gl_quant_col_128x1: ") + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string("quant_col launch: ") + why);
+  return GL_OK;
+}
+
+static int gmm_bwd_check(const char* fn, const void* a, const float* as, const void* b,
+                         const float* bs, const int32_t* gs, int64_t G, int64_t M, int64_t K,
+                         int64_t N, const void* out, int out_dtype) {
+  const std::string f(fn);
+  if (!a || !as || !b || !bs || !gs || !out) return fail(GL_EINVAL, f + ": null pointer");
+  if (G <= 0 || G > 1024) return fail(GL_EINVAL, f + ": need 0 < G <= 1024");
+  if (M <= 0 || K <= 0 || N <= 0 || K % 128 != 0 || N % 128 != 0)
+    return fail(GL_EINVAL, f + ": need M > 0 and K, N positive multiples of 128");
+  if (M > (int64_t(1) << 31) - 1 || G * K > (int64_t(1) << 31) - 1)
+    return fail(GL_EINVAL, f + ": M and G*K must fit in 31 bits");
+  if (out_dtype != GL_OUT_BF16 && out_dtype != GL_OUT_F32) return fail(GL_EINVAL, f + ": bad out_dtype");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(out) || !aligned16(as) || !aligned16(bs))
+    return fail(GL_EINVAL, f + ": tensors must be 16-byte aligned");
+  return GL_OK;
+}
+
+int gl_gmm_fp8_dlhs(const void* dq, const float* ds, const void* b_q, const float* b_s,
+                    const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                    void* out, int out_dtype, int* err_word, void* stream) {
+  if (int rc = gmm_bwd_check("gl_gmm_fp8_dlhs", dq, ds, b_q, b_s, group_sizes, G, M, K, N, out,
+                             out_dtype))
+    return rc;
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  const char* why = "";
+  // kernel reduction = the weight's N, kernel output = the weight's K
+  const int rc = gl_launch_gmm_fp8_dlhs(dq, ds, b_q, b_s, group_sizes, G, M, N, K, out,
+                                        out_dtype == GL_OUT_F32, err_word ? err_word : d->err,
+                                        static_cast<cudaStream_t>(stream), d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string("gl_gmm_fp8_dlhs: ") + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string("gl_gmm_fp8_dlhs: ") + why);
+  return GL_OK;
+}
+
+int gl_tgmm_fp8(const void* lq, const float* ls, const void* dq, const float* ds,
+                const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N, void* out,
+                int out_dtype, int* err_word, void* stream) {
+  if (int rc = gmm_bwd_check("gl_tgmm_fp8", lq, ls, dq, ds, group_sizes, G, M, K, N, out, out_dtype))
+    return rc;
+  if (M % 128 != 0) return fail(GL_EINVAL, "gl_tgmm_fp8: M must be a multiple of 128");
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  const char* why = "";
+  const int rc = gl_launch_tgmm_fp8(lq, ls, dq, ds, group_sizes, G, M, K, N, out,
+                                    out_dtype == GL_OUT_F32, err_word ? err_word : d->err,
+                                    static_cast<cudaStream_t>(stream), d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string("gl_tgmm_fp8: ") + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string("gl_tgmm_fp8: ") + why);
+  return GL_OK;
 }
 
 int gl_device_status(int* err_word, void* stream, int* code) {

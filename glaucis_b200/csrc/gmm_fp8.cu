@@ -61,6 +61,8 @@ struct Cfg {
   static constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;     // slack for 1 KB alignment
   // e4m3 x e4m3 -> f32, A K-major, B MN-major, M=128, N=BN.
   static constexpr uint32_t IDESC = idesc(1, 0, 0, 0, 1, BM, BN);
+  // transposed weight (backward dlhs): B K-major (rows = output columns)
+  static constexpr uint32_t IDESC_T = idesc(1, 0, 0, 0, 0, BM, BN);
   static_assert(2 * STAGES + 2 * NBUF + 1 <= 32, "barrier area");
 };
 
@@ -141,7 +143,7 @@ __device__ __forceinline__ void build_group_table(const int32_t* group_sizes, in
   }
 }
 
-template <int BN>
+template <int BN, bool kTransB>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gmm_fp8_fwd_kernel(const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_b, const Params p) {
@@ -216,8 +218,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* sb = smem + CF::OFF_B + s * CF::B_BYTES;
           tma_load_2d(sa, &tm_a, &full[s], kb * BK, tl.m0);
 #pragma unroll
-          for (int j = 0; j < BN / 128; ++j)
-            tma_load_2d(sb + j * 16384, &tm_b, &full[s], tl.n0 + 128 * j, brow + kb * BK);
+          for (int j = 0; j < BN / 128; ++j) {
+            if (kTransB)  // rows = output columns of weight group g, 128 reduction bytes each
+              tma_load_2d(sb + j * 16384, &tm_b, &full[s], kb * BK, tl.g * N + tl.n0 + 128 * j);
+            else          // rows = reduction index, 128 output columns each
+              tma_load_2d(sb + j * 16384, &tm_b, &full[s], tl.n0 + 128 * j, brow + kb * BK);
+          }
         }
       }
       if (!ok) {
@@ -253,8 +259,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int kk = 0; kk < BK / 32; ++kk) {
             const uint64_t ad = sdesc(a_base + s * A_BYTES + kk * 32, 16, 1024, kSwizzle128B);
             const uint64_t bd =
-                sdesc(b_base + s * CF::B_BYTES + kk * 4096, 16384, 1024, kSwizzle128B);
-            mma_f8f6f4(d, ad, bd, CF::IDESC, kk > 0 ? 1u : 0u);
+                kTransB ? sdesc(b_base + s * CF::B_BYTES + kk * 32, 16, 1024, kSwizzle128B)
+                        : sdesc(b_base + s * CF::B_BYTES + kk * 4096, 16384, 1024, kSwizzle128B);
+            mma_f8f6f4(d, ad, bd, kTransB ? CF::IDESC_T : CF::IDESC, kk > 0 ? 1u : 0u);
           }
           tc_commit(&empty[s]);
           tc_commit(&tfull[buf]);
@@ -287,7 +294,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool col_ok = ncol0 < N;
       const int nb = ncol0 >> 7;
       const float* sa_row = p.a_s + grow * KB;
-      const float* sb_col = p.b_s + static_cast<int64_t>(tl.g) * KB * NB + nb;
+      // weight scale of (K block kb, output block nb): b_s[g, kb, nb], or for
+      // the transposed weight (output = weight rows) b_s[g, nb, kb]
+      const int64_t sb_step = kTransB ? 1 : NB;
+      const float* sb_col = p.b_s + (kTransB ? (static_cast<int64_t>(tl.g) * NB + nb) * KB
+                                             : static_cast<int64_t>(tl.g) * KB * NB + nb);
       float2 acc[EC / 2];
 #pragma unroll
       for (int j = 0; j < EC / 2; ++j) acc[j] = make_float2(0.f, 0.f);
@@ -297,7 +308,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float sc = sa_next * sb_next;
         if (kb + 1 < KB) {
           sa_next = row_ok ? __ldg(sa_row + kb + 1) : 0.f;
-          sb_next = col_ok ? __ldg(sb_col + static_cast<int64_t>(kb + 1) * NB) : 0.f;
+          sb_next = col_ok ? __ldg(sb_col + static_cast<int64_t>(kb + 1) * sb_step) : 0.f;
         }
         const float2 sc2 = make_float2(sc, sc);
         const int buf = acc_it % NBUF;
@@ -597,6 +608,334 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ===========================================================================
+// Backward drhs = lhs^T x dout per group (tokamax tgmm):
+//   drhs[g, k, n] = sum over the global 128-row blocks mb touched by group g of
+//                   ls[mb, k] * ds[mb, n] * sum_{m in g and mb} lq[m, k] dq[m, n]
+// with lhs and dout quantised in 128x1 column blocks (lq [M, K], ls [M/128, K],
+// dq [M, N], ds [M/128, N]).  One tile = 128 rows k x 256 columns n of one
+// group; the reduction runs over the group's rows one 128-row block at a
+// time.  A = lq^T (k contiguous: MN-major), B = dq (n contiguous: MN-major);
+// rows of a partial block that belong to other groups are zeroed in the A
+// tile before its MMAs.  Empty groups get zero tiles.  Same warp roles,
+// pipeline and bounded waits as the forward kernel.
+// ===========================================================================
+struct TParams {
+  const float* ls;
+  const float* ds;
+  const int32_t* group_sizes;
+  void* out;
+  int* err;
+  int G, M, K, N;
+  int out_f32;
+};
+
+constexpr int T_STAGES = 4;
+constexpr uint32_t T_A_BYTES = 128 * 128;  // lq block: 128 rows m x 128 bytes k
+constexpr uint32_t T_B_BYTES = 128 * 256;  // dq block: 128 rows m x 256 bytes n
+constexpr uint32_t T_OFF_A = 0;
+constexpr uint32_t T_OFF_B = T_OFF_A + T_STAGES * T_A_BYTES;
+constexpr uint32_t T_OFF_DS = T_OFF_B + T_STAGES * T_B_BYTES;  // [2 halves][2 buffers][128] floats
+constexpr uint32_t T_OFF_BAR = T_OFF_DS + 2 * 2 * 128 * 4;
+constexpr uint32_t T_OFF_MISC = T_OFF_BAR + 256;
+constexpr uint32_t T_OFF_ROWOFF = T_OFF_MISC + 128;
+constexpr uint32_t T_SMEM_BYTES = T_OFF_ROWOFF + (MAX_G + 1) * 4 + 1024;
+constexpr uint32_t T_IDESC = idesc(1, 0, 0, 1, 1, 128, 256);  // A and B MN-major
+
+// OR of `v` over the 128 threads of named barrier `id` (a barrier).
+__device__ __forceinline__ bool tgmm_bar_or(int id, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void tgmm_tile(int t, int KT, int NT, int& g, int& k0, int& n0) {
+  const int per = KT * NT;
+  g = t / per;
+  const int r = t % per;
+  n0 = (r / KT) * 256;
+  k0 = (r % KT) * 128;
+}
+
+// Blocks mb0 .. mb0 + nblk - 1 of rows [r0, r1).
+__device__ __forceinline__ void tgmm_blocks(const int* row_off, int g, int& r0, int& r1, int& mb0,
+                                            int& nblk) {
+  r0 = row_off[g];
+  r1 = row_off[g + 1];
+  mb0 = r0 / 128;
+  nblk = r1 > r0 ? (r1 - 1) / 128 - mb0 + 1 : 0;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tgmm_fp8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                    const TParams p) {
+  constexpr int STAGES = T_STAGES, NBUF = 2, BN = 256, EC = 128, NCH = 4;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + T_OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + NBUF;
+  uint64_t* drain = tempty + NBUF;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + T_OFF_MISC);
+  int* abort_flag = reinterpret_cast<int*>(smem + T_OFF_MISC + 4);
+  int* valid_s = reinterpret_cast<int*>(smem + T_OFF_MISC + 8);
+  int* row_off = reinterpret_cast<int*>(smem + T_OFF_ROWOFF);
+  float* dsbuf = reinterpret_cast<float*>(smem + T_OFF_DS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G, K = p.K, N = p.N;
+  const int KT = K / 128, NT = (N + BN - 1) / BN;
+  const Abort ab{abort_flag, p.err};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_a);
+      prefetch_tmap(&tm_b);
+    }
+    tmem_alloc(tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int i = 0; i < STAGES; ++i) {
+        mbar_init(&full[i], 1);
+        mbar_init(&empty[i], 1);
+      }
+      for (int i = 0; i < NBUF; ++i) {
+        mbar_init(&tfull[i], 1);
+        mbar_init(&tempty[i], 8);
+      }
+      mbar_init(drain, 1);
+      *abort_flag = 0;
+      fence_mbar_init();
+    }
+  } else if (warp == 3) {
+    // row offsets (exclusive prefix sum of group_sizes) and validation
+    const int per = (G + 31) / 32;
+    const int g0 = min(G, lane * per), g1 = min(G, g0 + per);
+    int sum = 0, bad = 0;
+    for (int g = g0; g < g1; ++g) {
+      const int sz = p.group_sizes[g];
+      bad |= sz < 0;
+      sum += max(sz, 0);
+    }
+    int inc = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += v;
+    }
+    int r = inc - sum;
+    for (int g = g0; g < g1; ++g) {
+      row_off[g] = r;
+      r += max(p.group_sizes[g], 0);
+    }
+    bad = __any_sync(0xffffffffu, bad);
+    if (lane == 31) {
+      row_off[G] = inc;
+      const bool ok = !bad && inc <= p.M;
+      *valid_s = ok;
+      if (!ok) atomicExch(p.err, GL_DEV_BAD_GROUPS);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int total = *valid_s ? G * KT * NT : 0;
+
+  if (warp == 0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int g, k0, n0, r0, r1, mb0, nblk;
+        tgmm_tile(t, KT, NT, g, k0, n0);
+        tgmm_blocks(row_off, g, r0, r1, mb0, nblk);
+        for (int b = 0; b < nblk; ++b, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, ab)) { ok = false; break; }
+          const int m0 = (mb0 + b) * 128;
+          mbar_arrive_expect_tx(&full[s], T_A_BYTES + T_B_BYTES);
+          uint8_t* sa = smem + T_OFF_A + s * T_A_BYTES;
+          uint8_t* sb = smem + T_OFF_B + s * T_B_BYTES;
+          tma_load_2d(sa, &tm_a, &full[s], k0, m0);
+          tma_load_2d(sb, &tm_b, &full[s], n0, m0);
+          tma_load_2d(sb + 16384, &tm_b, &full[s], n0 + 128, m0);
+        }
+      }
+      if (!ok) {
+        const int first = it > STAGES ? it - STAGES : 0;
+        for (int j = first; j < it; ++j) {
+          const uint64_t t0 = global_ns();
+          while (!mbar_try_wait(&full[j % STAGES], (j / STAGES) & 1) && global_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
+    // --------------------------------------------------- masking + MMA
+    int it = 0, acc_it = 0;
+    bool ok = true;
+    const uint32_t a_base = smem_u32(smem + T_OFF_A), b_base = smem_u32(smem + T_OFF_B);
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      int g, k0, n0, r0, r1, mb0, nblk;
+      tgmm_tile(t, KT, NT, g, k0, n0);
+      tgmm_blocks(row_off, g, r0, r1, mb0, nblk);
+      for (int b = 0; b < nblk; ++b, ++it, ++acc_it) {
+        const int s = it % STAGES;
+        const int buf = acc_it % NBUF;
+        bool got = true;
+        if (lane == 0)
+          got = mbar_wait(&tempty[buf], ((acc_it / NBUF) & 1) ^ 1, ab) &&
+                mbar_wait(&full[s], (it / STAGES) & 1, ab);
+        if (!__shfl_sync(0xffffffffu, got, 0)) { ok = false; break; }  // the whole warp leaves
+        // rows of this block that belong to other groups: zero them in A
+        const int m0 = (mb0 + b) * 128;
+        const int lo = max(r0 - m0, 0), hi = min(r1 - m0, 128);
+        if (lo > 0 || hi < 128) {
+          uint4* a4 = reinterpret_cast<uint4*>(smem + T_OFF_A + s * T_A_BYTES);
+          const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+          for (int i = lane; i < 128 * 8; i += 32) {
+            const int row = i >> 3;
+            if (row < lo || row >= hi) a4[i] = z;
+          }
+          fence_proxy_async_smem();
+        }
+        __syncwarp();
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t d = tmem + buf * BN;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = sdesc(a_base + s * T_A_BYTES + kk * 4096, 16384, 1024, kSwizzle128B);
+            const uint64_t bd = sdesc(b_base + s * T_B_BYTES + kk * 4096, 16384, 1024, kSwizzle128B);
+            mma_f8f6f4(d, ad, bd, T_IDESC, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+          tc_commit(&tfull[buf]);
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0) {
+      tc_commit(drain);
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 100000000ull) {
+      }
+    }
+    __syncwarp();
+  } else if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_EPI));
+    // -------------------------------------------------------- epilogue
+    const int ew = warp - 4;
+    const int quad = warp & 3;
+    const int chalf = ew >> 2;
+    const int r = quad * 32 + lane;                     // row k0 + r of the tile
+    const int ht = threadIdx.x - 128 - chalf * 128;     // 0..127 within the half
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + chalf * EC;
+    int acc_it = 0;
+    bool ok = true;     // this thread's accumulators are valid
+    bool stop = false;  // set only by the half's vote: the same in all its threads
+    for (int t = blockIdx.x; t < total && !stop; t += gridDim.x) {
+      int g, k0, n0, r0, r1, mb0, nblk;
+      tgmm_tile(t, KT, NT, g, k0, n0);
+      tgmm_blocks(row_off, g, r0, r1, mb0, nblk);
+      const int ncol0 = n0 + chalf * EC;
+      const bool col_ok = ncol0 < N;
+      float2 acc[EC / 2];
+#pragma unroll
+      for (int j = 0; j < EC / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+      for (int b = 0; b < nblk; ++b, ++acc_it) {
+        const int mb = mb0 + b;
+        const int buf = acc_it % NBUF;
+        // column scales of this block: one per thread of the half, via smem
+        float* dsb = dsbuf + (chalf * 2 + buf) * 128;
+        dsb[ht] = col_ok ? __ldg(p.ds + static_cast<int64_t>(mb) * N + ncol0 + ht) : 0.f;
+        const float lsr = __ldg(p.ls + static_cast<int64_t>(mb) * K + k0 + r);
+        // a barrier of this half that also votes: once any role gave up,
+        // every thread of the half leaves here together
+        if (tgmm_bar_or(1 + chalf, *static_cast<volatile int*>(abort_flag) != 0)) { stop = true; break; }
+        // a wait that gives up sets the abort flag: the next vote stops the half
+        if (!mbar_wait(&tfull[buf], (acc_it / NBUF) & 1, ab)) { ok = false; continue; }
+        tc_fence_after();
+        const uint32_t ta = lane_base + buf * BN;
+        const float2 ls2 = make_float2(lsr, lsr);
+        uint32_t v[2][32];
+        auto promote = [&](const uint32_t (&x)[32], int base) {
+          const float4* d4 = reinterpret_cast<const float4*>(dsb) + base / 2;
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const float4 dd = d4[j / 2];
+            const float2 s01 = __fmul2_rn(make_float2(dd.x, dd.y), ls2);
+            const float2 s23 = __fmul2_rn(make_float2(dd.z, dd.w), ls2);
+            acc[base + j] = __ffma2_rn(make_float2(__uint_as_float(x[2 * j]), __uint_as_float(x[2 * j + 1])),
+                                       s01, acc[base + j]);
+            acc[base + j + 1] = __ffma2_rn(make_float2(__uint_as_float(x[2 * j + 2]), __uint_as_float(x[2 * j + 3])),
+                                           s23, acc[base + j + 1]);
+          }
+        };
+        tmem_ld32(ta, v[0]);
+        tmem_ld32(ta + 32, v[1]);
+        tmem_ld_wait2(v[0], v[1]);
+#pragma unroll
+        for (int c = 2; c < NCH; c += 2) {
+          promote(v[0], 16 * (c - 2));
+          tmem_ld32(ta + 32 * c, v[0]);
+          promote(v[1], 16 * (c - 1));
+          tmem_ld32(ta + 32 * (c + 1), v[1]);
+          tmem_ld_wait2(v[0], v[1]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        promote(v[0], 16 * (NCH - 2));
+        promote(v[1], 16 * (NCH - 1));
+        // dsb of this buffer is rewritten two blocks later, after this
+        // half's next barrier: every thread has read it by then
+      }
+      if (stop) break;
+      if (ok && col_ok) {
+        const int64_t orow = (static_cast<int64_t>(g) * K + k0 + r) * N + ncol0;
+        if (p.out_f32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow);
+#pragma unroll
+          for (int i = 0; i < EC / 4; ++i)
+            dst[i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + orow);
+#pragma unroll
+          for (int i = 0; i < EC / 8; ++i)
+            dst[i] = make_uint4(pack_bf16x2(acc[4 * i].x, acc[4 * i].y),
+                                pack_bf16x2(acc[4 * i + 1].x, acc[4 * i + 1].y),
+                                pack_bf16x2(acc[4 * i + 2].x, acc[4 * i + 2].y),
+                                pack_bf16x2(acc[4 * i + 3].x, acc[4 * i + 3].y));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 }  // namespace gmm
 }  // namespace gl
 
@@ -608,19 +947,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 #include "tmap.h"
 
-template <int BN>
+template <int BN, bool kTransB = false>
 static int launch_bn(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const gl::gmm::Params& p,
                      int64_t G, int64_t M, int64_t N, cudaStream_t st, int num_sms,
                      const char** why) {
   using namespace gl::gmm;
   using CF = Cfg<BN>;
-  if (!gl_set_smem_attr(reinterpret_cast<const void*>(gmm_fp8_fwd_kernel<BN>), 0,
+  if (!gl_set_smem_attr(reinterpret_cast<const void*>(gmm_fp8_fwd_kernel<BN, kTransB>), 0,
                         static_cast<int>(CF::SMEM_BYTES), why))
     return -2;
   const int64_t ntn = (N + BN - 1) / BN;
   const int64_t max_tiles = ((M + BM - 1) / BM + G) * ntn;
   const int grid = static_cast<int>(max_tiles < num_sms ? (max_tiles > 0 ? max_tiles : 1) : num_sms);
-  gmm_fp8_fwd_kernel<BN><<<grid, NUM_THREADS, CF::SMEM_BYTES, st>>>(tm_a, tm_b, p);
+  gmm_fp8_fwd_kernel<BN, kTransB><<<grid, NUM_THREADS, CF::SMEM_BYTES, st>>>(tm_a, tm_b, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     *why = cudaGetErrorString(e);
@@ -695,6 +1034,76 @@ int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const 
     else if (std::atoi(e) == 128) variant = 128;
   }
   if (variant == 2) return launch_pair(tm_a, tm_b, p, G, M, N, st, num_sms, why);
-  return variant == 256 ? launch_bn<256>(tm_a, tm_b, p, G, M, N, st, num_sms, why)
-                        : launch_bn<128>(tm_a, tm_b, p, G, M, N, st, num_sms, why);
+  return variant == 256 ? launch_bn<256, false>(tm_a, tm_b, p, G, M, N, st, num_sms, why)
+                        : launch_bn<128, false>(tm_a, tm_b, p, G, M, N, st, num_sms, why);
+}
+
+// Backward dlhs = dout x rhs^T per group (tokamax gmm with transpose_rhs=True):
+// the same kernel with the weight read K-major.  Kernel dimensions: reduction
+// K = the weight's N, output N = the weight's K; a_q / a_s = dout quantised
+// 1x128 along the weight's N; b_q [G, N, K] / b_s [G, N/128, K/128] are the
+// forward's weight QArray [G, K_w, N_w] / [G, K_w/128, N_w/128].
+int gl_launch_gmm_fp8_dlhs(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
+                           const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                           void* out, int out_f32, int* err, cudaStream_t st, int num_sms,
+                           const char** why) {
+  using namespace gl::gmm;
+  CUtensorMap tm_a, tm_b;
+  if (!gl_make_tmap_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, a_q, K, M, K, 128, 128,
+                       CU_TENSOR_MAP_SWIZZLE_128B, why))
+    return -1;
+  // weight as [G * N rows, K columns]: row = output column, K contiguous
+  if (!gl_make_tmap_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, b_q, K, G * N, K, 128, 128,
+                       CU_TENSOR_MAP_SWIZZLE_128B, why))
+    return -1;
+  Params p;
+  p.a_s = a_s;
+  p.b_s = b_s;
+  p.group_sizes = group_sizes;
+  p.out = out;
+  p.err = err;
+  p.G = static_cast<int>(G);
+  p.M = static_cast<int>(M);
+  p.K = static_cast<int>(K);
+  p.N = static_cast<int>(N);
+  p.out_f32 = out_f32;
+  return launch_bn<256, true>(tm_a, tm_b, p, G, M, N, st, num_sms, why);
+}
+
+// Backward drhs (tgmm): lq [M, K] / ls [M/128, K] and dq [M, N] / ds [M/128, N]
+// quantised in 128x1 column blocks; out [G, K, N].  M % 128 == 0.
+int gl_launch_tgmm_fp8(const void* lq, const float* ls, const void* dq, const float* ds,
+                       const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                       void* out, int out_f32, int* err, cudaStream_t st, int num_sms,
+                       const char** why) {
+  using namespace gl::gmm;
+  CUtensorMap tm_a, tm_b;
+  if (!gl_make_tmap_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, lq, K, M, K, 128, 128,
+                       CU_TENSOR_MAP_SWIZZLE_128B, why))
+    return -1;
+  if (!gl_make_tmap_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, dq, N, M, N, 128, 128,
+                       CU_TENSOR_MAP_SWIZZLE_128B, why))
+    return -1;
+  TParams p;
+  p.ls = ls;
+  p.ds = ds;
+  p.group_sizes = group_sizes;
+  p.out = out;
+  p.err = err;
+  p.G = static_cast<int>(G);
+  p.M = static_cast<int>(M);
+  p.K = static_cast<int>(K);
+  p.N = static_cast<int>(N);
+  p.out_f32 = out_f32;
+  const void* fn = reinterpret_cast<const void*>(tgmm_fp8_kernel);
+  if (!gl_set_smem_attr(fn, 0, static_cast<int>(T_SMEM_BYTES), why)) return -2;
+  const int64_t tiles = G * (K / 128) * ((N + 255) / 256);
+  const int grid = static_cast<int>(tiles < num_sms ? (tiles > 0 ? tiles : 1) : num_sms);
+  tgmm_fp8_kernel<<<grid, NUM_THREADS, T_SMEM_BYTES, st>>>(tm_a, tm_b, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return -2;
+  }
+  return 0;
 }

@@ -52,6 +52,7 @@ __device__ __forceinline__ uint16_t cvt_e4m3x2(float lo, float hi) {
 struct BlockDiv {
   float s, y;
   bool fast;
+  BlockDiv() = default;
   __device__ __forceinline__ explicit BlockDiv(float scale) : s(scale) {
     fast = scale >= 0x1p-64f && scale <= 3.40282347e38f;
     y = 1.0f / scale;
@@ -86,6 +87,34 @@ __device__ __forceinline__ uint2 quant8(const uint4& u, const BlockDiv& d) {
   return make_uint2(p[0] | (p[1] << 16), p[2] | (p[3] << 16));
 }
 
+__device__ __forceinline__ float div1(float x, const BlockDiv& d) {
+  if (!d.fast) return x / d.s;
+  const float q = __fmul_rn(x, d.y);
+  return copysignf(__fmaf_rn(__fmaf_rn(-q, d.s, x), d.y, q), x);
+}
+
+// Eight bf16 values of eight different columns (one scale each) -> e4m3.
+__device__ __forceinline__ uint2 quant8_cols(const uint4& u, const BlockDiv (&d)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  uint32_t p[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = bf16x2_to_f32x2(w[i]);
+    const BlockDiv& d0 = d[2 * i];
+    const BlockDiv& d1 = d[2 * i + 1];
+    if (d0.fast && d1.fast) {
+      const float2 y2 = make_float2(d0.y, d1.y), ns2 = make_float2(-d0.s, -d1.s);
+      const float2 q = __fmul2_rn(x, y2);
+      const float2 r = __ffma2_rn(q, ns2, x);
+      const float2 v = __ffma2_rn(r, y2, q);
+      p[i] = cvt_e4m3x2(copysignf(v.x, x.x), copysignf(v.y, x.y));
+    } else {
+      p[i] = cvt_e4m3x2(div1(x.x, d0), div1(x.y, d1));
+    }
+  }
+  return make_uint2(p[0] | (p[1] << 16), p[2] | (p[3] << 16));
+}
+
 // max |x| over one chunk, on packed bf16 (exact: the maximum is one of the
 // values).
 __device__ __forceinline__ float absmax8(const uint4& u) {
@@ -105,21 +134,26 @@ namespace quant {
 // so every stage is only ever used by one group, which therefore waits for
 // that stage's phases in order (a waiter that skipped a phase would see the
 // stage as full too early).
-template <bool kWeight> struct Ring;
-template <> struct Ring<false> { static constexpr int STAGES = 3, CTAS_PER_SM = 2; };
-template <> struct Ring<true> { static constexpr int STAGES = 4, CTAS_PER_SM = 1; };
+// Modes: ACT (1x128 blocks along a row), WEIGHT (128x128 blocks), COL (128x1
+// blocks: 128 rows of one column, the backward's layouts of lhs and grad).
+enum Mode : int { ACT = 0, WEIGHT = 1, COL = 2 };
+template <int kMode> struct Ring { static constexpr int STAGES = 4, CTAS_PER_SM = 1; };
+template <> struct Ring<ACT> { static constexpr int STAGES = 3, CTAS_PER_SM = 2; };
 constexpr int CONSUMER_WARPS = 16;
 constexpr int THREADS = 32 * (CONSUMER_WARPS + 1);  // + producer warp
 constexpr int W_GROUPS = 4;                          // weight quantiser: tile groups
 constexpr int W_GROUP_WARPS = CONSUMER_WARPS / W_GROUPS;
 constexpr uint32_t IN_BYTES = 128 * 128 * 2;
-static_assert(Ring<true>::STAGES % W_GROUPS == 0, "a weight stage must belong to one group");
-template <bool kWeight>
+static_assert(Ring<WEIGHT>::STAGES % W_GROUPS == 0 && Ring<COL>::STAGES % W_GROUPS == 0,
+              "a grouped stage must belong to one group");
+template <int kMode>
 struct Layout {
-  static constexpr int STAGES = Ring<kWeight>::STAGES;
+  static constexpr int STAGES = Ring<kMode>::STAGES;
+  // per group and parity: one float per warp (WEIGHT) or per warp and column (COL)
+  static constexpr int RED_PER_WARP = kMode == COL ? 128 : 1;
   static constexpr uint32_t OFF_BAR = STAGES * IN_BYTES;
   static constexpr uint32_t OFF_RED = OFF_BAR + 2 * STAGES * 8;
-  static constexpr uint32_t OFF_FLAG = OFF_RED + W_GROUPS * 2 * W_GROUP_WARPS * 4;
+  static constexpr uint32_t OFF_FLAG = OFF_RED + W_GROUPS * 2 * W_GROUP_WARPS * RED_PER_WARP * 4;
   static constexpr uint32_t SMEM_BYTES = OFF_FLAG + 16 + 1024;  // + slack for 1 KB alignment
 };
 
@@ -127,18 +161,18 @@ struct Args {
   uint8_t* q;
   float* s;
   int* err;
-  int64_t rows;  // activations: M; weights: G*K
-  int64_t K;
-  int64_t N;     // weights only
+  int64_t rows;  // ACT / COL: M; WEIGHT: G*K
+  int64_t K;     // ACT / COL: row length; WEIGHT: K
+  int64_t N;     // WEIGHT only
   int64_t tiles;
 };
 
 // Tile -> (x, y) element coordinates of its top-left corner.
-//   activations: tiles are (128-row slab, K block), K block fastest;
-//   weights:     tiles are (group, K block, N block), N block fastest.
-template <bool kWeight>
+//   ACT / COL: tiles are (128-row slab, 128-column block), column block fastest;
+//   WEIGHT:    tiles are (group, K block, N block), N block fastest.
+template <int kMode>
 __device__ __forceinline__ void tile_xy(const Args& a, int64_t t, int32_t& x, int32_t& y) {
-  if (kWeight) {
+  if (kMode == WEIGHT) {
     const int64_t NB = a.N / 128, KB = a.K / 128;
     const int64_t g = t / (KB * NB), kb = (t / NB) % KB, nb = t % NB;
     x = static_cast<int32_t>(nb * 128);
@@ -164,10 +198,10 @@ __device__ __forceinline__ bool bar_or(int id, int count, bool v) {
   return r != 0;
 }
 
-template <bool kWeight>
-__global__ void __launch_bounds__(THREADS, Ring<kWeight>::CTAS_PER_SM)
+template <int kMode>
+__global__ void __launch_bounds__(THREADS, Ring<kMode>::CTAS_PER_SM)
     quant_kernel(const __grid_constant__ CUtensorMap tm_in, const Args a) {
-  using L = Layout<kWeight>;
+  using L = Layout<kMode>;
   constexpr int STAGES = L::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -182,7 +216,7 @@ __global__ void __launch_bounds__(THREADS, Ring<kWeight>::CTAS_PER_SM)
     prefetch_tmap(&tm_in);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kWeight ? W_GROUP_WARPS : CONSUMER_WARPS);
+      mbar_init(&empty[i], kMode == ACT ? CONSUMER_WARPS : W_GROUP_WARPS);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -198,7 +232,7 @@ __global__ void __launch_bounds__(THREADS, Ring<kWeight>::CTAS_PER_SM)
         const int st = static_cast<int>(i % STAGES);
         if (!mbar_wait(&empty[st], (static_cast<uint32_t>(i / STAGES) & 1u) ^ 1u, ab)) break;
         int32_t x, y;
-        tile_xy<kWeight>(a, blockIdx.x + i * gridDim.x, x, y);
+        tile_xy<kMode>(a, blockIdx.x + i * gridDim.x, x, y);
         mbar_arrive_expect_tx(&full[st], IN_BYTES);
         tma_load_2d(smem + st * IN_BYTES, &tm_in, &full[st], x, y);
       }
@@ -215,8 +249,8 @@ __global__ void __launch_bounds__(THREADS, Ring<kWeight>::CTAS_PER_SM)
     return;
   }
 
-  if (kWeight) {
-    // ------------------------------------------- weights: groups of 4 warps
+  if (kMode != ACT) {
+    // -------------------------------- WEIGHT / COL: groups of 4 warps
     const int grp = warp / W_GROUP_WARPS, gw = warp % W_GROUP_WARPS;
     const int tg = threadIdx.x - grp * W_GROUP_WARPS * 32;  // 0..127
     const int64_t NB = a.N / 128;
@@ -225,29 +259,88 @@ __global__ void __launch_bounds__(THREADS, Ring<kWeight>::CTAS_PER_SM)
       const int st = static_cast<int>(i % STAGES);
       const bool ok = mbar_wait(&full[st], static_cast<uint32_t>(i / STAGES) & 1u, ab);
       const uint4* in = reinterpret_cast<const uint4*>(smem + st * IN_BYTES);
-      float m = 0.f;
+      float* r = red + (grp * 2 + par) * W_GROUP_WARPS * L::RED_PER_WARP;
+      const int c16 = tg & 15;  // this thread's 8-column chunk of the tile
+      if (kMode == WEIGHT) {
+        float m = 0.f;
 #pragma unroll 8
-      for (int j = 0; j < 16; ++j) m = fmaxf(m, absmax8(in[tg + 128 * j]));
+        for (int j = 0; j < 16; ++j) m = fmaxf(m, absmax8(in[tg + 128 * j]));
 #pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      float* r = red + (grp * 2 + par) * W_GROUP_WARPS;
-      if (lane == 0) r[gw] = m;
-      if (bar_or(1 + grp, W_GROUP_WARPS * 32, !ok || *static_cast<volatile int*>(abort_flag))) break;
+        for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) r[gw] = m;
+      } else {
+        // per-column maxima over this thread's 16 rows, then over the two
+        // row groups of the warp (lanes l and l ^ 16 share the chunk)
+        float cm[8];
 #pragma unroll
-      for (int w = 0; w < W_GROUP_WARPS; ++w) m = fmaxf(m, r[w]);
-      const float sc = scale_of(m);
-      const BlockDiv div(sc);
-      int32_t x, y;
-      tile_xy<kWeight>(a, blockIdx.x + i * gridDim.x, x, y);
-      uint8_t* qbase = a.q + static_cast<int64_t>(y) * a.N + x + (tg & 15) * 8;
+        for (int e = 0; e < 8; ++e) cm[e] = 0.f;
 #pragma unroll 4
-      for (int j = 0; j < 16; ++j) {
-        const int row = (tg >> 4) + 8 * j;
-        *reinterpret_cast<uint2*>(qbase + static_cast<int64_t>(row) * a.N) = quant8(in[tg + 128 * j], div);
+        for (int j = 0; j < 16; ++j) {
+          const uint4 u = in[tg + 128 * j];
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float2 v = bf16x2_to_f32x2(w[h]);
+            cm[2 * h] = fmaxf(cm[2 * h], fabsf(v.x));
+            cm[2 * h + 1] = fmaxf(cm[2 * h + 1], fabsf(v.y));
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) cm[e] = fmaxf(cm[e], __shfl_xor_sync(0xffffffffu, cm[e], 16));
+        if (lane < 16) {
+          float4* rc = reinterpret_cast<float4*>(r + gw * 128 + c16 * 8);
+          rc[0] = make_float4(cm[0], cm[1], cm[2], cm[3]);
+          rc[1] = make_float4(cm[4], cm[5], cm[6], cm[7]);
+        }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-      if (tg == 0) a.s[(y / 128) * NB + x / 128] = sc;  // s[g, kb, nb]; y / 128 = g * KB + kb
+      if (bar_or(1 + grp, W_GROUP_WARPS * 32, !ok || *static_cast<volatile int*>(abort_flag))) break;
+      int32_t x, y;
+      tile_xy<kMode>(a, blockIdx.x + i * gridDim.x, x, y);
+      const int64_t ld = kMode == WEIGHT ? a.N : a.K;  // row length of the operand
+      uint8_t* qbase = a.q + static_cast<int64_t>(y) * ld + x + c16 * 8;
+      if (kMode == WEIGHT) {
+        float m = 0.f;
+#pragma unroll
+        for (int w = 0; w < W_GROUP_WARPS; ++w) m = fmaxf(m, r[w]);
+        const float sc = scale_of(m);
+        const BlockDiv div(sc);
+#pragma unroll 4
+        for (int j = 0; j < 16; ++j) {
+          const int row = (tg >> 4) + 8 * j;
+          *reinterpret_cast<uint2*>(qbase + static_cast<int64_t>(row) * ld) = quant8(in[tg + 128 * j], div);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        if (tg == 0) a.s[(y / 128) * NB + x / 128] = sc;  // s[g, kb, nb]; y / 128 = g * KB + kb
+      } else {
+        float cm[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) cm[e] = r[c16 * 8 + e];
+#pragma unroll
+        for (int w = 1; w < W_GROUP_WARPS; ++w)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) cm[e] = fmaxf(cm[e], r[w * 128 + c16 * 8 + e]);
+        float sc[8];
+        BlockDiv div[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          sc[e] = scale_of(cm[e]);
+          div[e] = BlockDiv(sc[e]);
+        }
+#pragma unroll 4
+        for (int j = 0; j < 16; ++j) {
+          const int row = (tg >> 4) + 8 * j;
+          *reinterpret_cast<uint2*>(qbase + static_cast<int64_t>(row) * ld) =
+              quant8_cols(in[tg + 128 * j], div);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        if (tg < 16) {  // s[row block, column]
+          float4* sd = reinterpret_cast<float4*>(a.s + static_cast<int64_t>(y / 128) * a.K + x + c16 * 8);
+          sd[0] = make_float4(sc[0], sc[1], sc[2], sc[3]);
+          sd[1] = make_float4(sc[4], sc[5], sc[6], sc[7]);
+        }
+      }
     }
   } else {
     // ------------------------------- activations: every warp owns 8 rows
@@ -261,7 +354,7 @@ __global__ void __launch_bounds__(THREADS, Ring<kWeight>::CTAS_PER_SM)
       if (!mbar_wait(&full[st], static_cast<uint32_t>(i / STAGES) & 1u, ab)) break;
       const uint4* in = reinterpret_cast<const uint4*>(smem + st * IN_BYTES);
       int32_t x, y;
-      tile_xy<kWeight>(a, blockIdx.x + i * gridDim.x, x, y);
+      tile_xy<kMode>(a, blockIdx.x + i * gridDim.x, x, y);
       uint4 u[2][2];
 #pragma unroll
       for (int pass = 0; pass < 2; ++pass)
@@ -294,11 +387,11 @@ __global__ void __launch_bounds__(THREADS, Ring<kWeight>::CTAS_PER_SM)
 
 namespace {
 
-template <bool kWeight>
+template <int kMode>
 int launch_quant(const void* in, void* q, float* s, int* err, int64_t rows, int64_t K, int64_t N,
                  cudaStream_t st, int num_sms, const char** why) {
   using namespace gl::quant;
-  const int64_t inner = kWeight ? N : K;
+  const int64_t inner = kMode == WEIGHT ? N : K;
   CUtensorMap tm_in;
   if (!gl_make_tmap_2d(&tm_in, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, in, inner, rows, inner, 128, 128,
                        CU_TENSOR_MAP_SWIZZLE_NONE, why))
@@ -310,13 +403,13 @@ int launch_quant(const void* in, void* q, float* s, int* err, int64_t rows, int6
   a.rows = rows;
   a.K = K;
   a.N = N;
-  a.tiles = kWeight ? (rows / 128) * (N / 128) : ((rows + 127) / 128) * (K / 128);
-  const void* fn = reinterpret_cast<const void*>(quant_kernel<kWeight>);
-  constexpr uint32_t smem_bytes = Layout<kWeight>::SMEM_BYTES;
+  a.tiles = kMode == WEIGHT ? (rows / 128) * (N / 128) : ((rows + 127) / 128) * (K / 128);
+  const void* fn = reinterpret_cast<const void*>(quant_kernel<kMode>);
+  constexpr uint32_t smem_bytes = Layout<kMode>::SMEM_BYTES;
   if (!gl_set_smem_attr(fn, 0, static_cast<int>(smem_bytes), why)) return -2;
-  const int64_t slots = static_cast<int64_t>(num_sms) * Ring<kWeight>::CTAS_PER_SM;
+  const int64_t slots = static_cast<int64_t>(num_sms) * Ring<kMode>::CTAS_PER_SM;
   const int64_t grid = a.tiles < slots ? a.tiles : slots;
-  quant_kernel<kWeight><<<static_cast<unsigned>(grid > 0 ? grid : 1), THREADS, smem_bytes, st>>>(
+  quant_kernel<kMode><<<static_cast<unsigned>(grid > 0 ? grid : 1), THREADS, smem_bytes, st>>>(
       tm_in, a);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -332,10 +425,16 @@ int launch_quant(const void* in, void* q, float* s, int* err, int64_t rows, int6
 // -1 = operand rejected by the tensor-map encoder, -2 = launch failure.
 int gl_launch_quant_act(const void* x, int64_t M, int64_t K, void* q, float* s, int* err,
                         cudaStream_t st, int num_sms, const char** why) {
-  return launch_quant<false>(x, q, s, err, M, K, 0, st, num_sms, why);
+  return launch_quant<gl::quant::ACT>(x, q, s, err, M, K, 0, st, num_sms, why);
 }
 
 int gl_launch_quant_w(const void* w, int64_t G, int64_t K, int64_t N, void* q, float* s, int* err,
                       cudaStream_t st, int num_sms, const char** why) {
-  return launch_quant<true>(w, q, s, err, G * K, K, N, st, num_sms, why);
+  return launch_quant<gl::quant::WEIGHT>(w, q, s, err, G * K, K, N, st, num_sms, why);
+}
+
+// 128x1 column blocks of x [M, C] (M % 128 == 0): q [M, C], s [M/128, C].
+int gl_launch_quant_col(const void* x, int64_t M, int64_t C, void* q, float* s, int* err,
+                        cudaStream_t st, int num_sms, const char** why) {
+  return launch_quant<gl::quant::COL>(x, q, s, err, M, C, 0, st, num_sms, why);
 }

@@ -138,12 +138,120 @@ def gmm_fp8_blockwise(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.T
     compatibility; the B200 kernel's tiles are fixed (128x256x128).
     """
     del tiling
+    if torch.is_grad_enabled() and (lhs.requires_grad or rhs.requires_grad):
+        # differentiable path: backward = gmm_fp8_blockwise_bwd
+        return _GmmFp8Blockwise.apply(lhs, rhs, group_sizes, out_dtype)
     a_q, a_s = quant_act_1x128(lhs)
     b_q, b_s = quant_w_128x128(rhs)
     out = gmm_fp8_fwd(a_q, a_s, b_q, b_s, group_sizes, out_dtype=out_dtype)
     if zero_unassigned_rows:
         _zero_tail_rows(out, group_sizes)
     return out
+
+
+# ---------------------------------------------------------------------------
+# Grouped matmul backward (KE/examples/kernels/gmm_fp8_blockwise.py:123-169)
+# ---------------------------------------------------------------------------
+def quant_col_128x1(x: torch.Tensor, q: Optional[torch.Tensor] = None,
+                    s: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [M, C] (M, C multiples of 128) -> (e4m3 [M, C], fp32 scales
+    [M/128, C]): one absmax scale per 128 rows of a column.  Replaces
+    qpl.quantize(grad, channelwise_axes=[1], tiled_axes={0: 128}) (:135-141)
+    and, untransposed, the lhs_t quantisation of the forward (:92-99)."""
+    _need_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise ValueError("quant_col_128x1 expects a 2-D bf16 tensor")
+    M, C = x.shape
+    q = _out(q, (M, C), FP8, x.device, "q")
+    s = _out(s, (M // TILE, C), torch.float32, x.device, "s")
+    lib = _lib.load()
+    _lib.check(lib.gl_quant_col_128x1(x.data_ptr(), M, C, q.data_ptr(), s.data_ptr(), None,
+                                      _stream()), "gl_quant_col_128x1")
+    return q, s
+
+
+def gmm_fp8_dlhs(dq: torch.Tensor, ds: torch.Tensor, b_q: torch.Tensor, b_s: torch.Tensor,
+                 group_sizes: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """dlhs [M, K] = dout x rhs^T per group from dout quantised 1x128 along N
+    (quant_act_1x128 of grad [M, N]) and the forward's weight QArray; replaces
+    tokamax gmm(..., transpose_rhs=True) (:143-153).  Rows at or beyond
+    sum(group_sizes) are left as they are in `out` (zeroed when allocated)."""
+    _need_cuda(dq, ds, b_q, b_s, group_sizes)
+    M, N = dq.shape
+    G, K, N2 = b_q.shape
+    if N2 != N:
+        raise ValueError(f"N mismatch: dout {N} vs rhs {N2}")
+    if out is None:
+        out = torch.zeros((M, K), dtype=out_dtype, device=dq.device)
+    code = _lib.GL_OUT_F32 if out.dtype == torch.float32 else _lib.GL_OUT_BF16
+    lib = _lib.load()
+    _lib.check(lib.gl_gmm_fp8_dlhs(dq.data_ptr(), ds.data_ptr(), b_q.data_ptr(), b_s.data_ptr(),
+                                   group_sizes.data_ptr(), G, M, K, N, out.data_ptr(), code, None,
+                                   _stream()), "gl_gmm_fp8_dlhs")
+    return out
+
+
+def tgmm_fp8(lq: torch.Tensor, ls: torch.Tensor, dq: torch.Tensor, ds: torch.Tensor,
+             group_sizes: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
+             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """drhs [G, K, N] = per group lhs^T x dout over the group's rows, both
+    quantised by quant_col_128x1; replaces tokamax tgmm (:155-165).  Empty
+    groups give zeros."""
+    _need_cuda(lq, ls, dq, ds, group_sizes)
+    M, K = lq.shape
+    N = dq.shape[1]
+    G = group_sizes.numel()
+    if group_sizes.dtype != torch.int32:
+        raise ValueError("group_sizes must be int32")
+    if out is None:
+        out = torch.empty((G, K, N), dtype=out_dtype, device=lq.device)
+    code = _lib.GL_OUT_F32 if out.dtype == torch.float32 else _lib.GL_OUT_BF16
+    lib = _lib.load()
+    _lib.check(lib.gl_tgmm_fp8(lq.data_ptr(), ls.data_ptr(), dq.data_ptr(), ds.data_ptr(),
+                               group_sizes.data_ptr(), G, M, K, N, out.data_ptr(), code, None,
+                               _stream()), "gl_tgmm_fp8")
+    return out
+
+
+def gmm_fp8_blockwise_bwd(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.Tensor,
+                          grad: torch.Tensor, rhs_q: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
+                          ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(dlhs, drhs) of `gmm_fp8_blockwise(lhs, rhs, group_sizes)` for the
+    output gradient `grad` [M, N] (KE/examples/kernels/gmm_fp8_blockwise.py
+    :123-169): dout quantised 1x128 along N for dlhs and 128x1 along M for
+    drhs, lhs quantised 128x1 along M, the forward's weight QArray (passed as
+    `rhs_q` or recomputed).  dlhs has lhs's dtype, drhs rhs's (bf16)."""
+    if grad.dtype != torch.bfloat16:
+        grad = grad.to(torch.bfloat16)
+    grad = grad.contiguous()
+    b_q, b_s = rhs_q if rhs_q is not None else quant_w_128x128(rhs)
+    dq1, ds1 = quant_act_1x128(grad)
+    dlhs = gmm_fp8_dlhs(dq1, ds1, b_q, b_s, group_sizes, out_dtype=lhs.dtype)
+    del dq1, ds1
+    lq, ls = quant_col_128x1(lhs)
+    dq2, ds2 = quant_col_128x1(grad)
+    drhs = tgmm_fp8(lq, ls, dq2, ds2, group_sizes, out_dtype=rhs.dtype)
+    return dlhs, drhs
+
+
+class _GmmFp8Blockwise(torch.autograd.Function):
+    """custom-VJP pair of the template (gmm_fp8_blockwise.py:71-78)."""
+
+    @staticmethod
+    def forward(ctx, lhs, rhs, group_sizes, out_dtype):
+        a_q, a_s = quant_act_1x128(lhs)
+        b_q, b_s = quant_w_128x128(rhs)
+        out = gmm_fp8_fwd(a_q, a_s, b_q, b_s, group_sizes, out_dtype=out_dtype)
+        _zero_tail_rows(out, group_sizes)
+        ctx.save_for_backward(lhs, rhs, group_sizes, b_q, b_s)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        lhs, rhs, group_sizes, b_q, b_s = ctx.saved_tensors
+        dlhs, drhs = gmm_fp8_blockwise_bwd(lhs, rhs, group_sizes, grad, rhs_q=(b_q, b_s))
+        return dlhs, drhs, None, None
 
 
 _SIDE_STREAMS = {}

@@ -143,6 +143,32 @@ int gl_chunk_gla_fwd_ws(const void* q, const void* k, const void* v, const float
                         int64_t chunk_size, void* o, float* ht, void* workspace,
                         size_t workspace_bytes, int* err_word, void* stream);
 
+/*
+ * Backward of the grouped matmul (KE/examples/kernels/gmm_fp8_blockwise.py:123-169).
+ *
+ * gl_quant_col_128x1: 128x1 column blocks of x bf16 [M, C] (M, C multiples
+ *   of 128): q e4m3 [M, C], s fp32 [M/128, C], s = absmax of 128 rows of one
+ *   column / 448.  Replaces qpl.quantize(grad, channelwise_axes=[1],
+ *   tiled_axes={0:128}) :135-141 and, untransposed, qpl.quantize(lhs^T,
+ *   channelwise_axes=[0], tiled_axes={1:128}) :92-99 (lhs_t = (q^T, s^T)).
+ * gl_gmm_fp8_dlhs: dlhs [M, K] = dout x rhs^T per group: dq / ds = dout
+ *   quantised 1x128 along N (gl_quant_act_1x128 of grad [M, N]); b_q / b_s the
+ *   forward's weight QArray [G, K, N] / [G, K/128, N/128].  Replaces
+ *   tokamax gmm(dlhs_dout, rhs, transpose_rhs=True) :143-153.  Rows at or
+ *   beyond sum(group_sizes) are not written.
+ * gl_tgmm_fp8: drhs [G, K, N] = per group lhs^T x dout over the group's rows:
+ *   lq / ls and dq / ds quantised by gl_quant_col_128x1 (M % 128 == 0).
+ *   Empty groups get zeros.  Replaces tokamax tgmm(lhs_t, drhs_dout) :155-165.
+ */
+int gl_quant_col_128x1(const void* x, int64_t M, int64_t C, void* q, float* s, int* err_word,
+                       void* stream);
+int gl_gmm_fp8_dlhs(const void* dq, const float* ds, const void* b_q, const float* b_s,
+                    const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                    void* out, int out_dtype, int* err_word, void* stream);
+int gl_tgmm_fp8(const void* lq, const float* ls, const void* dq, const float* ds,
+                const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                void* out, int out_dtype, int* err_word, void* stream);
+
 /* Largest M*K accepted by gl_gmm_fp8_act_fwd_noalloc (activation elements). */
 #define GL_NOALLOC_MAX_ACT_ELEMS (16u * 1024u * 1024u)
 

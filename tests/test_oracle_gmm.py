@@ -124,3 +124,32 @@ def test_torch_cpu_restatement_matches_oracle():
     got = cpu_fast.gmm_fp8_blockwise(lhs, rhs, gs.tolist()).numpy()
     ref = O.gmm_fp8_blockwise(lhs.float().numpy(), rhs.float().numpy(), gs.numpy())
     assert_close(got, ref, rtol=1e-4, atol_frac=1e-5, what="cpu_fast gmm")
+
+
+# ---------------------------------------------------------------------------
+# backward oracle (oracle/gmm_bwd_oracle.py)
+# ---------------------------------------------------------------------------
+def test_bwd_oracle_quant_col_is_act_quant_of_transpose():
+    from oracle import gmm_bwd_oracle as B
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((256, 384)).astype(np.float32)
+    q, s = B.quant_col_128x1(x)
+    qt, st = O.quant_act_1x128(np.ascontiguousarray(x.T))   # 1x128 along M of x^T
+    assert np.array_equal(q, qt.T) and np.array_equal(s, st.T)
+
+
+def test_bwd_oracle_close_to_exact_gradients():
+    from oracle import gmm_bwd_oracle as B
+    rng = np.random.default_rng(6)
+    M, K, N = 512, 256, 256
+    sizes = [100, 0, 200, 150, 62]
+    bf = lambda a: (a.astype(np.float32).view(np.uint32) & 0xFFFF0000).view(np.float32)
+    lhs = bf(rng.standard_normal((M, K)))
+    rhs = bf(rng.standard_normal((len(sizes), K, N)) * 0.02)
+    grad = bf(rng.standard_normal((M, N)))
+    dl, dr = B.gmm_fp8_blockwise_bwd(lhs, rhs, sizes, grad)
+    ul, ur = B.gmm_bwd_unquantised(lhs, rhs, sizes, grad)
+    rel = lambda a, b: np.linalg.norm(a - b) / np.linalg.norm(b)
+    assert rel(dl, ul) < 0.06 and rel(dr, ur) < 0.06
+    assert not dr[1].any()                      # empty group
+    assert not dl[sum(sizes):].any()            # rows past sum(group_sizes)
