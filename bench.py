@@ -388,6 +388,44 @@ def run_b200(args):
                               ("quant_w_128x128", q_w_ms, q_w_bytes))}
 
     # ---------------------------------------------------------------- e2e
+    # ------------------------------------------------- GMM backward rows
+    # dlhs (grouped kernel, weight transposed) and drhs (tgmm) on the same
+    # workload with a synthetic output gradient, quantised inputs resident.
+    gen = torch.Generator(device="cuda").manual_seed(args.seed + 7 + rank)
+    grad = torch.randn((cfg.M, cfg.N), device="cuda", generator=gen).to(torch.bfloat16)
+    dq1, ds1 = ops.quant_act_1x128(grad)
+    dq2, ds2 = ops.quant_col_128x1(grad)
+    lq, ls = ops.quant_col_128x1(lhs)
+    dlhs = torch.zeros((cfg.M, cfg.K), dtype=torch.bfloat16, device="cuda")
+    drhs = torch.empty((cfg.G, cfg.K, cfg.N), dtype=torch.bfloat16, device="cuda")
+    dl_ms = timed(lambda: ops.gmm_fp8_dlhs(dq1, ds1, b_q, b_s, gs, out=dlhs), max(5, args.steps // 2), 3, world)
+    tg_ms = timed(lambda: ops.tgmm_fp8(lq, ls, dq2, ds2, gs, out=drhs), max(5, args.steps // 2), 3, world)
+    qc_ms = timed(lambda: ops.quant_col_128x1(grad, dq2, ds2), max(5, args.steps // 2), 3, world)
+    if ops.device_status() != 0:
+        raise SystemExit("device error word set after the backward rows")
+    dl_bytes = (cfg.M * cfg.N + 4 * cfg.M * cfg.N / 128 + g_nz * cfg.K * cfg.N
+                + 4 * g_nz * (cfg.K / 128) * (cfg.N / 128) + 2 * cfg.M * cfg.K)
+    tg_bytes = (cfg.M * cfg.K + 4 * cfg.M * cfg.K / 128 + cfg.M * cfg.N + 4 * cfg.M * cfg.N / 128
+                + 2 * cfg.G * cfg.K * cfg.N)
+    qc_bytes = grad.numel() * 3 + grad.numel() // 128 * 4
+
+    def row(ms_, by, fl):
+        gbs = by / (ms_ * 1e-3) / 1e9
+        r = {"ms": ms_, "achieved_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"],
+             "algorithmic_bytes": by}
+        if fl:
+            r["tflops"] = world * fl / (ms_ * 1e-3) / 1e12
+            r["fp8_tensor_frac"] = fl / (ms_ * 1e-3) / 1e12 / fp8_peak
+        return r
+
+    gmm_bwd = {"workload": args.workload,
+               "dlhs": row(dl_ms, dl_bytes, flops), "tgmm": row(tg_ms, tg_bytes, flops),
+               "quant_col_128x1": row(qc_ms, qc_bytes, 0.0),
+               "note": "dlhs = gl_gmm_fp8_dlhs (grouped kernel, K-major weight); tgmm writes "
+                       "drhs [G, K, N] bf16 for every group (empty ones as zeros)"}
+    del grad, dq1, ds1, dq2, ds2, lq, ls, dlhs, drhs
+    torch.cuda.empty_cache()
+
     e2e = None
     if not args.skip_e2e:
         lhs_h = lhs.cpu().pin_memory()
@@ -476,6 +514,7 @@ def run_b200(args):
             "gpu_launches": args.steps,
             "clocks": sampler.summary() if sampler else None,
             "quantisers": quantisers,
+            "gmm_bwd": gmm_bwd,
             "gla": gla,
             "gla_long": gla_long,
         }

@@ -7,9 +7,10 @@ KE/examples/kernels/gmm_fp8_blockwise.py: `_make_test_data`,
 `gmm_fp8_blockwise(lhs, rhs, group_sizes, tiling)` and
 `optimized_compute(M, K, N, G)`.
 
-optimized_compute runs the FORWARD pass and returns the scalar loss
-out.sum(); the reference template also runs the backward (gmm with
-transpose_rhs and tgmm), which is not built on B200 yet.
+optimized_compute runs the forward and the backward (dlhs by the grouped
+kernel with the weight transposed, drhs by tgmm) and returns the scalar loss
+out.sum(), as the reference's jax.value_and_grad does; mode="fwd" runs the
+forward only.
 """
 
 import torch
@@ -49,9 +50,16 @@ def gmm_fp8_blockwise(
     return ops.gmm_fp8_blockwise(lhs, rhs, group_sizes, tiling, out_dtype=torch.float32)
 
 
-def optimized_compute(M=8192, K=2048, N=512, G=32):
-    """Forward GMM with FP8 block-wise quantisation; returns the loss scalar."""
+def optimized_compute(M=8192, K=2048, N=512, G=32, mode="fwd_bwd"):
+    """Forward + backward GMM with FP8 block-wise quantisation (gradients
+    of lhs and rhs computed, as the reference's value_and_grad); returns the
+    loss scalar."""
     lhs, rhs, group_sizes = _make_test_data(M, K, N, G)
-    out = gmm_fp8_blockwise(lhs, rhs, group_sizes)
-    return out.sum().cpu()
+    if mode == "fwd":
+        return gmm_fp8_blockwise(lhs, rhs, group_sizes).sum().cpu()
+    lhs.requires_grad_(True)
+    rhs.requires_grad_(True)
+    loss = gmm_fp8_blockwise(lhs, rhs, group_sizes).sum()
+    loss.backward()
+    return loss.detach().cpu()
 # EVOLVE-BLOCK-END
