@@ -375,17 +375,22 @@ def run_b200(args):
     # outputs preallocated: the timed region holds the quantiser kernels only
     qa_o, sa_o = torch.empty_like(a_q), torch.empty_like(a_s)
     qw_o, sw_o = torch.empty_like(b_q), torch.empty_like(b_s)
-    q_act_ms = timed(lambda: ops.quant_act_1x128(lhs, qa_o, sa_o), max(5, args.steps // 2), 3, world)
-    q_w_ms = timed(lambda: ops.quant_w_128x128(rhs, qw_o, sw_o), max(5, args.steps // 10), 3, world)
+    qs_act = ClockSampler(local) if rank == 0 else None
+    q_act_ms = timed(lambda: ops.quant_act_1x128(lhs, qa_o, sa_o), max(5, args.steps // 2), 3, world,
+                     qs_act)
+    qs_w = ClockSampler(local) if rank == 0 else None
+    q_w_ms = timed(lambda: ops.quant_w_128x128(rhs, qw_o, sw_o), max(5, args.steps // 10), 3, world,
+                   qs_w)
     del qa_o, sa_o, qw_o, sw_o
     # algorithmic bytes: bf16 in, e4m3 out, fp32 scales out
     q_act_bytes = lhs.numel() * 3 + lhs.numel() // 128 * 4
     q_w_bytes = rhs.numel() * 3 + rhs.numel() // (128 * 128) * 4
     quantisers = {
         name: {"ms": ms_, "achieved_gbs": by / (ms_ * 1e-3) / 1e9,
-               "frac": by / (ms_ * 1e-3) / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": by}
-        for name, ms_, by in (("quant_act_1x128", q_act_ms, q_act_bytes),
-                              ("quant_w_128x128", q_w_ms, q_w_bytes))}
+               "frac": by / (ms_ * 1e-3) / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": by,
+               "sm_mhz": cs.summary()["sm_mhz"] if cs else None}
+        for name, ms_, by, cs in (("quant_act_1x128", q_act_ms, q_act_bytes, qs_act),
+                                  ("quant_w_128x128", q_w_ms, q_w_bytes, qs_w))}
 
     # ---------------------------------------------------------------- e2e
     # ------------------------------------------------- GMM backward rows

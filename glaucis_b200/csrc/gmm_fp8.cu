@@ -630,17 +630,26 @@ struct TParams {
   int out_f32;
 };
 
-constexpr int T_STAGES = 4;
+constexpr int T_STAGES = 3;
 constexpr uint32_t T_A_BYTES = 128 * 128;  // lq block: 128 rows m x 128 bytes k
 constexpr uint32_t T_B_BYTES = 128 * 256;  // dq block: 128 rows m x 256 bytes n
+constexpr uint32_t T_OUT_BYTES = 128 * 256 * 2;  // bf16 output tile: 4 atoms of 64 columns
 constexpr uint32_t T_OFF_A = 0;
 constexpr uint32_t T_OFF_B = T_OFF_A + T_STAGES * T_A_BYTES;
-constexpr uint32_t T_OFF_DS = T_OFF_B + T_STAGES * T_B_BYTES;  // [2 halves][2 buffers][128] floats
+constexpr uint32_t T_OFF_OUT = T_OFF_B + T_STAGES * T_B_BYTES;
+constexpr uint32_t T_OFF_DS = T_OFF_OUT + T_OUT_BYTES;  // [2 halves][2 buffers][128] floats
 constexpr uint32_t T_OFF_BAR = T_OFF_DS + 2 * 2 * 128 * 4;
 constexpr uint32_t T_OFF_MISC = T_OFF_BAR + 256;
 constexpr uint32_t T_OFF_ROWOFF = T_OFF_MISC + 128;
 constexpr uint32_t T_SMEM_BYTES = T_OFF_ROWOFF + (MAX_G + 1) * 4 + 1024;
 constexpr uint32_t T_IDESC = idesc(1, 0, 0, 1, 1, 128, 256);  // A and B MN-major
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int32_t x,
+                                             int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(m),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
 
 // OR of `v` over the 128 threads of named barrier `id` (a barrier).
 __device__ __forceinline__ bool tgmm_bar_or(int id, bool v) {
@@ -675,7 +684,7 @@ __device__ __forceinline__ void tgmm_blocks(const int* row_off, int g, int& r0, 
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tgmm_fp8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                    const TParams p) {
+                    const __grid_constant__ CUtensorMap tm_o, const TParams p) {
   constexpr int STAGES = T_STAGES, NBUF = 2, BN = 256, EC = 128, NCH = 4;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -908,24 +917,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // half's next barrier: every thread has read it by then
       }
       if (stop) break;
-      if (ok && col_ok) {
-        const int64_t orow = (static_cast<int64_t>(g) * K + k0 + r) * N + ncol0;
-        if (p.out_f32) {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow);
+      if (p.out_f32) {
+        if (ok && col_ok) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
+                                                  (static_cast<int64_t>(g) * K + k0 + r) * N + ncol0);
 #pragma unroll
           for (int i = 0; i < EC / 4; ++i)
             dst[i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
-        } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + orow);
+        }
+      } else {
+        // bf16: this half's two 64-column atoms of the shared-memory output
+        // tile (128B-swizzled rows), then one TMA store per atom.  Every
+        // thread of the half takes part (the condition is the half's vote).
+        const bool leader = ht == 0;
+        if (leader) bulk_wait_read<0>();  // the previous tile's stores have read the tile
+        asm volatile("bar.sync %0, 128;" ::"r"(3 + chalf) : "memory");
+        uint8_t* ot = smem + T_OFF_OUT + chalf * 2 * 16384;
 #pragma unroll
-          for (int i = 0; i < EC / 8; ++i)
-            dst[i] = make_uint4(pack_bf16x2(acc[4 * i].x, acc[4 * i].y),
-                                pack_bf16x2(acc[4 * i + 1].x, acc[4 * i + 1].y),
-                                pack_bf16x2(acc[4 * i + 2].x, acc[4 * i + 2].y),
-                                pack_bf16x2(acc[4 * i + 3].x, acc[4 * i + 3].y));
+        for (int i = 0; i < EC / 8; ++i) {
+          const int atom = i >> 3, c = i & 7;
+          *reinterpret_cast<uint4*>(ot + atom * 16384 + r * 128 + ((c ^ (r & 7)) << 4)) =
+              make_uint4(pack_bf16x2(acc[4 * i].x, acc[4 * i].y),
+                         pack_bf16x2(acc[4 * i + 1].x, acc[4 * i + 1].y),
+                         pack_bf16x2(acc[4 * i + 2].x, acc[4 * i + 2].y),
+                         pack_bf16x2(acc[4 * i + 3].x, acc[4 * i + 3].y));
+        }
+        fence_proxy_async_smem();
+        asm volatile("bar.sync %0, 128;" ::"r"(3 + chalf) : "memory");
+        if (leader && col_ok) {  // (N is a multiple of 128: both atoms are in range)
+          tma_store_2d(&tm_o, ot, ncol0, g * K + k0);
+          tma_store_2d(&tm_o, ot + 16384, ncol0 + 64, g * K + k0);
+          bulk_commit();
         }
       }
     }
+    if (ht == 0) bulk_wait<0>();  // stores complete before the CTA exits
   }
 
   tc_fence_before();
@@ -1084,6 +1110,13 @@ int gl_launch_tgmm_fp8(const void* lq, const float* ls, const void* dq, const fl
   if (!gl_make_tmap_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, dq, N, M, N, 128, 128,
                        CU_TENSOR_MAP_SWIZZLE_128B, why))
     return -1;
+  CUtensorMap tm_o;
+  if (out_f32) {
+    tm_o = tm_a;  // unused: fp32 output is stored directly
+  } else if (!gl_make_tmap_2d(&tm_o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, N, G * K, N, 64, 128,
+                              CU_TENSOR_MAP_SWIZZLE_128B, why)) {
+    return -1;
+  }
   TParams p;
   p.ls = ls;
   p.ds = ds;
@@ -1099,7 +1132,7 @@ int gl_launch_tgmm_fp8(const void* lq, const float* ls, const void* dq, const fl
   if (!gl_set_smem_attr(fn, 0, static_cast<int>(T_SMEM_BYTES), why)) return -2;
   const int64_t tiles = G * (K / 128) * ((N + 255) / 256);
   const int grid = static_cast<int>(tiles < num_sms ? (tiles > 0 ? tiles : 1) : num_sms);
-  tgmm_fp8_kernel<<<grid, NUM_THREADS, T_SMEM_BYTES, st>>>(tm_a, tm_b, p);
+  tgmm_fp8_kernel<<<grid, NUM_THREADS, T_SMEM_BYTES, st>>>(tm_a, tm_b, tm_o, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     *why = cudaGetErrorString(e);
