@@ -82,3 +82,36 @@ def test_torch_cpu_restatement_matches_oracle(gate):
     ro, rht = O.chunk_gla_fwd(q, k, v, g=g, g_gamma=gg, h0=hh)
     assert_close(o.numpy(), ro, rtol=1e-3, atol_frac=1e-5, what="o")
     assert_close(ht.numpy(), rht, rtol=1e-3, atol_frac=1e-5, what="ht")
+
+
+def test_gla_bwd_oracle_against_finite_differences():
+    # the autograd oracle of the backward, pinned by central differences
+    from oracle.gla_bwd_oracle import gla_bwd_reference
+    from oracle import gla_oracle as GO
+    rng = np.random.default_rng(9)
+    B, T, H, K, V = 1, 6, 1, 4, 3
+    q = rng.standard_normal((B, T, H, K))
+    k = rng.standard_normal((B, T, H, K))
+    v = rng.standard_normal((B, T, H, V))
+    g = -np.abs(rng.standard_normal((B, T, H, K))) * 0.3
+    h0 = rng.standard_normal((B, H, K, V)) * 0.1
+    do = rng.standard_normal((B, T, H, V))
+    dq, dk, dv, dh0 = gla_bwd_reference(q, k, v, do, g=g, h0=h0, scale=0.5)
+
+    def loss(q_, k_, v_, h0_):
+        o, _ = GO.naive_recurrence(q_, k_, v_, g=g, h0=h0_, scale=0.5)
+        return float((o * do).sum())
+
+    eps = 1e-6
+    args = {"q": q, "k": k, "v": v, "h0": h0}
+    grads = {"q": dq, "k": dk, "v": dv, "h0": dh0}
+    idxs = {"q": [(0, 0, 0, 0), (0, T - 1, 0, 3)], "k": [(0, 1, 0, 2), (0, T - 1, 0, 0)],
+            "v": [(0, 0, 0, 1), (0, 3, 0, 2)], "h0": [(0, 0, 1, 2), (0, 0, 3, 0)]}
+    for name, lst in idxs.items():
+        for idx in lst:
+            ap = {n: a.copy() for n, a in args.items()}
+            am = {n: a.copy() for n, a in args.items()}
+            ap[name][idx] += eps
+            am[name][idx] -= eps
+            fd = (loss(ap["q"], ap["k"], ap["v"], ap["h0"]) - loss(am["q"], am["k"], am["v"], am["h0"])) / (2 * eps)
+            assert abs(fd - grads[name][idx]) < 1e-6 * max(1.0, abs(fd)), (name, idx, fd, grads[name][idx])
