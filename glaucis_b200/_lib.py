@@ -33,6 +33,11 @@ SIGNATURES = {
     "gl_chunk_gla_fwd_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I64, _I64]),
     "gl_chunk_gla_fwd_ws": (_I, [_P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64, _I64,
                                  _P, _P, _P, ctypes.c_size_t, _P, _P]),
+    "gl_chunk_gla_fwd_states": (_I, [_P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64,
+                                     _I64, _P, _P, _P, _P, ctypes.c_size_t, _P, _P]),
+    "gl_chunk_gla_bwd_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I64, _I64]),
+    "gl_chunk_gla_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64,
+                              _I64, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P]),
     "gl_gmm_fp8_act_fwd_noalloc": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _P]),
     "gl_quant_col_128x1": (_I, [_P, _I64, _I64, _P, _P, _P, _P]),
     "gl_gmm_fp8_dlhs": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _P]),

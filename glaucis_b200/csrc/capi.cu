@@ -25,9 +25,17 @@ int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const 
                       const char** why);
 int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float* g,
                         const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
-                        int64_t H, int64_t K, int64_t V, void* o, float* ht, void* ws,
+                        int64_t H, int64_t K, int64_t V, void* o, float* ht, void* h_out, void* ws,
                         size_t ws_bytes, int* err, cudaStream_t st, int num_sms, const char** why);
 size_t gl_chunk_gla_ws_bytes(int64_t B, int64_t T, int64_t H, int num_sms);
+int gl_launch_chunk_gla_dh(const void* q, const void* dout, const float* g, const float* g_gamma,
+                           const float* dht, float scale, int64_t B, int64_t T, int64_t H,
+                           void* e_out, float* dh0, void* ws, size_t ws_bytes, int* err,
+                           cudaStream_t st, int num_sms, const char** why);
+int gl_launch_chunk_gla_grads(const void* q, const void* k, const void* v, const void* dout,
+                              const float* g, const float* g_gamma, const void* h, const void* e,
+                              float scale, int64_t B, int64_t T, int64_t H, void* dq, void* dk,
+                              void* dv, int* err, cudaStream_t st, int num_sms, const char** why);
 int gl_launch_quant_col(const void* x, int64_t M, int64_t C, void* q, float* s, int* err,
                         cudaStream_t st, int num_sms, const char** why);
 int gl_launch_gmm_fp8_dlhs(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
@@ -64,6 +72,11 @@ int device_state(DeviceState** out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return fail(GL_ELAUNCH, "device ordinal out of range");
+  // Make the device's primary context current on this thread: the tensor-map
+  // encoder is a driver call, and a thread that has made no runtime call yet
+  // (autograd's backward worker, for one) has no current context.
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
   std::lock_guard<std::mutex> lk(g_mu);
   DeviceState& d = g_dev[dev];
   if (d.num_sms == 0) {
@@ -134,7 +147,13 @@ bool gl_make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, in
                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    *why = "cuTensorMapEncodeTiled (2-D) rejected the operand (alignment / stride / box)";
+    thread_local char msg[256];
+    std::snprintf(msg, sizeof msg,
+                  "cuTensorMapEncodeTiled (2-D) rejected the operand (alignment / stride / box): "
+                  "ptr %p dims [%lld, %lld] row stride %lld B box [%u, %u] (error %d)",
+                  ptr, static_cast<long long>(inner), static_cast<long long>(outer),
+                  static_cast<long long>(strides[0]), box_inner, box_outer, static_cast<int>(r));
+    *why = msg;
     return false;
   }
   return true;
@@ -156,7 +175,14 @@ bool gl_make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, in
                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    *why = "cuTensorMapEncodeTiled (3-D) rejected the operand (alignment / stride / box)";
+    thread_local char msg[256];
+    std::snprintf(msg, sizeof msg,
+                  "cuTensorMapEncodeTiled (3-D) rejected the operand (alignment / stride / box): "
+                  "ptr %p dims [%lld, %lld, %lld] strides %lld, %lld B box [%u, %u, %u] (error %d)",
+                  ptr, static_cast<long long>(d0), static_cast<long long>(d1),
+                  static_cast<long long>(d2), static_cast<long long>(strides[0]),
+                  static_cast<long long>(strides[1]), b0, b1, b2, static_cast<int>(r));
+    *why = msg;
     return false;
   }
   return true;
@@ -277,7 +303,7 @@ int gl_chunk_gla_fwd_ws(const void* q, const void* k, const void* v, const float
   if (int rc = device_state(&d)) return rc;
   const char* why = "";
   const int rc = gl_launch_chunk_gla(q, k, v, g, g_gamma, h0, scale, B, T, H, K, V, o, ht,
-                                     workspace, workspace ? workspace_bytes : 0,
+                                     nullptr, workspace, workspace ? workspace_bytes : 0,
                                      err_word ? err_word : d->err,
                                      static_cast<cudaStream_t>(stream), d->num_sms, &why);
   if (rc == -1) return fail(GL_EINVAL, std::string("gl_chunk_gla_fwd: ") + why);
@@ -300,6 +326,83 @@ size_t gl_chunk_gla_fwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t
   DeviceState* d = nullptr;
   if (device_state(&d)) return 0;
   return gl_chunk_gla_ws_bytes(B, T, H, d->num_sms);
+}
+
+// Per-chunk state rows (B * T/64 * H * 128) are TMA row coordinates (int32).
+static bool gla_states_fit(int64_t B, int64_t T, int64_t H) {
+  return B * (T / 64) * H * 128 <= (int64_t(1) << 31) - 1;
+}
+
+int gl_chunk_gla_fwd_states(const void* q, const void* k, const void* v, const float* g,
+                            const float* g_gamma, const float* h0, float scale, int64_t B,
+                            int64_t T, int64_t H, int64_t K, int64_t V, int64_t chunk_size,
+                            void* o, float* ht, void* h_states, void* workspace,
+                            size_t workspace_bytes, int* err_word, void* stream) {
+  const char* f = "gl_chunk_gla_fwd_states";
+  if (int rc = chunk_gla_check(f, q, k, v, g, g_gamma, h0, B, T, H, K, V, chunk_size, o, ht))
+    return rc;
+  if (!h_states || !aligned16(h_states)) return fail(GL_EINVAL, std::string(f) + ": h_states must be a 16-byte aligned pointer");
+  if (!gla_states_fit(B, T, H)) return fail(GL_EINVAL, std::string(f) + ": B*T/64*H*128 must fit in 31 bits");
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(GL_EINVAL, std::string(f) + ": workspace must be 256-byte aligned");
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  const char* why = "";
+  const int rc = gl_launch_chunk_gla(q, k, v, g, g_gamma, h0, scale, B, T, H, K, V, o, ht,
+                                     h_states, workspace, workspace ? workspace_bytes : 0,
+                                     err_word ? err_word : d->err,
+                                     static_cast<cudaStream_t>(stream), d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string(f) + ": " + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string(f) + ": " + why);
+  return GL_OK;
+}
+
+// Backward workspace: E (bf16, as h_states) then the reverse scan's split
+// records, 256-byte aligned.
+static size_t gla_e_bytes(int64_t B, int64_t T, int64_t H) {
+  return ((static_cast<size_t>(B * (T / 64) * H) * 128 * 128 * 2 + 255) / 256) * 256;
+}
+
+size_t gl_chunk_gla_bwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K, int64_t V,
+                                        int64_t chunk_size) {
+  if (B <= 0 || H <= 0 || T <= 0 || T % 64 != 0 || K != 128 || V != 128 || chunk_size != 64)
+    return 0;
+  DeviceState* d = nullptr;
+  if (device_state(&d)) return 0;
+  return gla_e_bytes(B, T, H) + gl_chunk_gla_ws_bytes(B, T, H, d->num_sms);
+}
+
+int gl_chunk_gla_bwd(const void* q, const void* k, const void* v, const float* g,
+                     const float* g_gamma, const void* h_states, const void* dout,
+                     const float* dht, float scale, int64_t B, int64_t T, int64_t H, int64_t K,
+                     int64_t V, int64_t chunk_size, void* dq, void* dk, void* dv, float* dh0,
+                     void* workspace, size_t workspace_bytes, int* err_word, void* stream) {
+  const char* f = "gl_chunk_gla_bwd";
+  if (int rc = chunk_gla_check(f, q, k, v, g, g_gamma, dht, B, T, H, K, V, chunk_size, dout, dh0))
+    return rc;
+  if (!h_states || !dq || !dk || !dv) return fail(GL_EINVAL, std::string(f) + ": null pointer");
+  if (!aligned16(h_states) || !aligned16(dq) || !aligned16(dk) || !aligned16(dv))
+    return fail(GL_EINVAL, std::string(f) + ": tensors must be 16-byte aligned");
+  if (!gla_states_fit(B, T, H)) return fail(GL_EINVAL, std::string(f) + ": B*T/64*H*128 must fit in 31 bits");
+  const size_t eb = gla_e_bytes(B, T, H);
+  if (!workspace || workspace_bytes < eb)
+    return fail(GL_EINVAL, std::string(f) + ": workspace smaller than gl_chunk_gla_bwd_workspace_bytes");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(GL_EINVAL, std::string(f) + ": workspace must be 256-byte aligned");
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  int* err = err_word ? err_word : d->err;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const char* why = "";
+  int rc = gl_launch_chunk_gla_dh(q, dout, g, g_gamma, dht, scale, B, T, H, workspace, dh0,
+                                  static_cast<char*>(workspace) + eb, workspace_bytes - eb, err, st,
+                                  d->num_sms, &why);
+  if (rc == 0)
+    rc = gl_launch_chunk_gla_grads(q, k, v, dout, g, g_gamma, h_states, workspace, scale, B, T, H,
+                                   dq, dk, dv, err, st, d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string(f) + ": " + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string(f) + ": " + why);
+  return GL_OK;
 }
 
 int gl_quant_col_128x1(const void* x, int64_t M, int64_t C, void* q, float* s, int* err_word,

@@ -79,11 +79,19 @@ struct Cfg {
   static constexpr uint32_t IDESC_O = idesc(1, 1, 1, 0, 1, 64, VS);   // K-major x MN-major
 };
 
+// Kernel modes.  FWD: the forward (o, ht, optionally the per-chunk states
+// h_n).  FWD_STATE: state-only pre-pass of a sequence split.  DH: the reverse
+// state-gradient scan of the backward, over the chunks in reverse order with
+// q in the k slot and do in the v slot: D_NT = dht, and per chunk
+// E_n = e^{G_last(n)} D_{n+1} (written, bf16), D_n = E_n + Qs_n^T do_n, with
+// D_0 = dh0.  DH_STATE: its state-only pre-pass.
+enum { MODE_FWD = 0, MODE_FWD_STATE = 1, MODE_DH_STATE = 2, MODE_DH = 3 };
+
 struct Params {
   const float* g_gamma;  // [H] or null
-  const float* h0;       // [B,H,K,V] or null
+  const float* h0;       // [B,H,K,V] or null (DH: the final-state gradient dht, or null)
   __nv_bfloat16* o;      // [B,T,H,V]
-  float* ht;             // [B,H,K,V] or null
+  float* ht;             // [B,H,K,V] or null (DH: dh0)
   int* err;
   float scale;
   float log2_scale;  // log2(scale) when scale > 0 (folded into the exponent), else 0
@@ -94,7 +102,13 @@ struct Params {
   // ws_d [B*H][nseg-1][K]; the fold kernel turns record j into the initial
   // state of segment j+1 (h0 folded with segments 0..j), which the full pass
   // loads like h0.  nseg == 1: no split.
-  int nseg, seg_grid;  // segments in total / per (b, h, V slice) in this grid
+  // The reverse scan (DH) uses the same records for segments 1..nseg-1 (its
+  // partial state-gradient at the segment start from a zero gradient at the
+  // segment end, and the total decay); the reverse fold turns record j into
+  // the gradient at the end of segment j.  A state-only grid covers segments
+  // seg_base .. seg_base + seg_grid - 1.
+  int nseg, seg_grid, seg_base;  // segments in total / per (b, h, V slice) in this grid / first
+  int has_hout;  // FWD: write h_n (bf16, [B,NT,H,K,V]) through tm_h; DH: E_n (always)
   float* ws_h;
   float* ws_d;
   int B, T, H, nsplit;
@@ -120,7 +134,8 @@ enum {
   B_H_FULL = 29,     // H_n written -> MMA
   B_DRAIN = 30,
   B_GSYNC = 31,      // [2] gating quarter sums written
-  NUM_BARS = 33
+  B_HST = 33,        // the TMA store of the previous state tile has read shared memory
+  NUM_BARS = 34
 };
 static_assert(NUM_BARS * 8 <= 512, "barrier area");
 
@@ -142,13 +157,18 @@ __device__ __forceinline__ uint32_t kmaj_off(uint32_t row, uint32_t col, uint32_
          (col & 7u) * 2u;
 }
 
-template <int VS, bool kStateOnly>
+template <int VS, int kMode>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     chunk_gla_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v,
-                         const __grid_constant__ CUtensorMap tm_g, const Params p) {
+                         const __grid_constant__ CUtensorMap tm_g,
+                         const __grid_constant__ CUtensorMap tm_h, const Params p) {
   using CF = Cfg<VS>;
+  // kStateOnly: S_n = (k slot)^T (v slot) only (no q, A, O).  kRev: chunks
+  // in reverse order, the k slot scaled like q (Qs) instead of k (Kg).
+  constexpr bool kStateOnly = kMode != MODE_FWD;
+  constexpr bool kRev = kMode == MODE_DH || kMode == MODE_DH_STATE;
   extern __shared__ uint8_t smem_raw[];
   // 1 KB-aligned base derived by pointer arithmetic on the shared array so
   // that every access below stays in the shared address space.
@@ -160,7 +180,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int T = p.T, H = p.H;
-  const int seg = blockIdx.x % p.seg_grid, rest = blockIdx.x / p.seg_grid;
+  const int seg = p.seg_base + static_cast<int>(blockIdx.x) % p.seg_grid;
+  const int rest = blockIdx.x / p.seg_grid;
   const int bh = rest / p.nsplit, vsl = rest % p.nsplit;
   const int b = bh / H, h = bh % H;
   const int v0 = vsl * VS;
@@ -168,6 +189,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int c1 = static_cast<int>(static_cast<int64_t>(seg + 1) * (T / C) / p.nseg);
   const int NT = c1 - c0;  // chunks of this CTA
   const int tok0 = b * T + c0 * C;
+  // Sequence position of the n-th chunk this CTA processes.
+  auto chunk_of = [&](int n) { return kRev ? NT - 1 - n : n; };
   const Abort ab{abort_flag, p.err};
 
   if (warp == 0 && lane == 0) {
@@ -175,6 +198,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
     if (p.has_g) prefetch_tmap(&tm_g);
+    if (p.has_hout) prefetch_tmap(&tm_h);
   } else if (warp == 1 && lane == 0) {
     for (int i = 0; i < CF::QS; ++i) {
       mbar_init(&bar[B_QKV_FULL + i], 1);
@@ -199,6 +223,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(&bar[B_P_FULL], STATE_WARPS);
     mbar_init(&bar[B_H_FULL], STATE_WARPS);
     mbar_init(&bar[B_DRAIN], 1);
+    mbar_init(&bar[B_HST], 1);
     *abort_flag = 0;
     fence_mbar_init();
   } else if (warp == 2) {
@@ -217,7 +242,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       for (int n = 0; n < NT; ++n) {
         const int s = n % CF::QS;
-        const int tok = tok0 + n * C;
+        const int tok = tok0 + chunk_of(n) * C;
         if (!mbar_wait(&bar[B_QKV_EMPTY + s], ((n / CF::QS) & 1) ^ 1, ab)) break;
         mbar_arrive_expect_tx(&bar[B_QKV_FULL + s], (kStateOnly ? 1 : 2) * CF::Q_BYTES + CF::V_BYTES);
         uint8_t* qd = smem + CF::OFF_Q + s * CF::Q_BYTES;
@@ -366,7 +391,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!mbar_wait(&bar[B_G_EMPTY + s], ((n >> 1) & 1) ^ 1, ab)) break;
         mbar_arrive_expect_tx(&bar[B_G_FULL + s], CF::G_BYTES);
         tma_load_3d(smem + CF::OFF_G + s * CF::G_BYTES, &tm_g, &bar[B_G_FULL + s], 0, h,
-                    tok0 + n * C);
+                    tok0 + chunk_of(n) * C);
       }
     }
     __syncwarp();
@@ -476,8 +501,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           xa01 = xa23 = make_float2(fmaf(Gt, kLog2e, log2_scale), fmaf(Gt, kLog2e, log2_scale));
           xb01 = xb23 = make_float2(-Gt * kLog2e, -Gt * kLog2e);
         }
-        const float2 b01 = make_float2(ex2_approx(xb01.x), ex2_approx(xb01.y));
-        const float2 b23 = make_float2(ex2_approx(xb23.x), ex2_approx(xb23.y));
+        // k slot: Kg = k e^-G, or in the reverse scan Qs = scale q e^G.
+        const float2 xk01 = kRev ? xa01 : xb01, xk23 = kRev ? xa23 : xb23;
+        const float2 b01 = make_float2(ex2_approx(xk01.x), ex2_approx(xk01.y));
+        const float2 b23 = make_float2(ex2_approx(xk23.x), ex2_approx(xk23.y));
         const uint32_t off = static_cast<uint32_t>(t) * 128u + ((qk_chunk ^ (t & 7)) << 4);
         if (!kStateOnly) {
           const float2 a01 = make_float2(ex2_approx(xa01.x), ex2_approx(xa01.y));
@@ -492,7 +519,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               make_uint2(pack_bf16x2(q01.x, q01.y), pack_bf16x2(q23.x, q23.y));
         }
         const uint2 k2 = *reinterpret_cast<const uint2*>(ks + off);
-        const float2 k01 = __fmul2_rn(bf16x2_f32x2(k2.x), b01), k23 = __fmul2_rn(bf16x2_f32x2(k2.y), b23);
+        float2 k01 = __fmul2_rn(bf16x2_f32x2(k2.x), b01), k23 = __fmul2_rn(bf16x2_f32x2(k2.y), b23);
+        if (kRev && p.scale_apart) {
+          k01 = __fmul2_rn(k01, make_float2(p.scale, p.scale));
+          k23 = __fmul2_rn(k23, make_float2(p.scale, p.scale));
+        }
         *reinterpret_cast<uint2*>(ks + off) =
             make_uint2(pack_bf16x2(k01.x, k01.y), pack_bf16x2(k23.x, k23.y));
         if (i == 7 && gw == GATE_WARPS - 1) {
@@ -522,11 +553,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int64_t bhi = static_cast<int64_t>(b) * H + h;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     float hreg[VS];
-    // Initial state: h0 for the first segment; with a sequence split, later
-    // segments start from the state the fold kernel left in the workspace.
-    const float* init = kStateOnly ? nullptr
-                        : seg == 0 ? (p.h0 ? p.h0 + bhi * KD * 128 : nullptr)
-                                   : p.ws_h + (bhi * (p.nseg - 1) + seg - 1) * KD * 128;
+    // Initial state: h0 for the first segment (DH: dht for the last); with a
+    // sequence split, the other segments start from the state the fold
+    // kernel left in the workspace.
+    const float* init = nullptr;
+    if (kMode == MODE_FWD)
+      init = seg == 0 ? (p.h0 ? p.h0 + bhi * KD * 128 : nullptr)
+                      : p.ws_h + (bhi * (p.nseg - 1) + seg - 1) * KD * 128;
+    else if (kMode == MODE_DH)
+      init = seg == p.nseg - 1 ? (p.h0 ? p.h0 + bhi * KD * 128 : nullptr)
+                               : p.ws_h + (bhi * (p.nseg - 1) + seg) * KD * 128;
     if (init) {
       const float4* src = reinterpret_cast<const float4*>(init + static_cast<int64_t>(key) * 128 + v0);
 #pragma unroll
@@ -543,8 +579,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     float dacc = 1.f;  // state-only pass: product of the chunk decays
     constexpr int NS = CF::NS;
-    // H: MN-major B operand [128 keys][VS], 64-column atoms 16 KB apart.
-    auto store_h = [&]() {
+    // H: MN-major B operand [128 keys][VS], 64-column atoms 16 KB apart,
+    // which is also the layout of a 128B-swizzled TMA box of 64 x 128: with
+    // has_hout, thread 0 of warp 12 stores it to row ((b NT + chunk) H + h)
+    // 128 of the state output once all four warps wrote it (B_H_FULL), and
+    // releases the buffer (B_HST) when the store has read it.
+    const bool st_issuer = warp == 4 + GATE_WARPS && lane == 0;
+    int nstore = 0;
+    auto store_h = [&](int chunk) -> bool {
+      if (p.has_hout && nstore > 0) {
+        if (st_issuer) {
+          bulk_wait_read<0>();
+          mbar_arrive(&bar[B_HST]);
+        }
+        if (!mbar_wait(&bar[B_HST], (nstore - 1) & 1, ab)) return false;
+      }
       uint8_t* hp = smem + CF::OFF_H;
 #pragma unroll
       for (int c8 = 0; c8 < VS / 8; ++c8) {
@@ -557,6 +606,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_H_FULL]);
+      if (p.has_hout) {
+        bool sok = true;
+        if (st_issuer) {
+          sok = mbar_wait(&bar[B_H_FULL], nstore & 1, ab);
+          if (sok) {
+            const int32_t row = ((b * (T / C) + c0 + chunk) * H + h) * KD;
+#pragma unroll
+            for (int j = 0; j < CF::V_BOXES; ++j) tma_store_2d(&tm_h, hp + j * 16384, v0 + 64 * j, row);
+            bulk_commit();
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, sok, 0)) return false;
+      }
+      ++nstore;
+      return true;
     };
     // P = tril(A_m) in bf16, K-major (row = query, 128 B).
     auto p_epilogue = [&](int m) -> bool {
@@ -596,10 +660,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       return true;
     };
     bool ok = true;
-    if (!kStateOnly) {
-      store_h();
-      ok = p_epilogue(0);
-    }
+    if (!kStateOnly) ok = store_h(0) && p_epilogue(0);
     for (int n = 0; n < NT && ok; ++n) {
       const int s = n & 1;
       const uint32_t ph2 = (n >> 1) & 1;
@@ -609,6 +670,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       dacc *= d;
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_DEC_EMPTY + s]);
+      if (kRev) {
+        // E_n = e^{G_last} D_{n+1} (written in the DH pass), then D_n = E_n + S_n.
+#pragma unroll
+        for (int j = 0; j < VS; j += 2) {
+          const float2 e = __fmul2_rn(make_float2(hreg[j], hreg[j + 1]), make_float2(d, d));
+          hreg[j] = e.x;
+          hreg[j + 1] = e.y;
+        }
+        if (kMode == MODE_DH && !store_h(chunk_of(n))) { ok = false; break; }
+      }
       if (!mbar_wait(&bar[B_S_FULL + n % NS], (n / NS) & 1, ab)) { ok = false; break; }
       tc_fence_after();
 #pragma unroll
@@ -620,9 +691,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int i = 0; i < 32; i += 2) {
           const float2 hs = __fadd2_rn(make_float2(hreg[j + i], hreg[j + i + 1]),
                                        make_float2(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])));
-          const float2 hn = __fmul2_rn(hs, make_float2(d, d));
-          hreg[j + i] = hn.x;
-          hreg[j + i + 1] = hn.y;
+          if (kRev) {
+            hreg[j + i] = hs.x;
+            hreg[j + i + 1] = hs.y;
+          } else {
+            const float2 hn = __fmul2_rn(hs, make_float2(d, d));
+            hreg[j + i] = hn.x;
+            hreg[j + i + 1] = hn.y;
+          }
         }
       }
       tc_fence_before();
@@ -633,19 +709,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // accumulates into the other TMEM buffer meanwhile)
       if (!mbar_wait(&bar[B_O_FULL + s], ph2, ab)) { ok = false; break; }
       tc_fence_after();
-      if (n + 1 < NT) {
-        store_h();
-        if (!p_epilogue(n + 1)) { ok = false; break; }
-      }
+      if (n + 1 < NT && !(store_h(n + 1) && p_epilogue(n + 1))) { ok = false; break; }
     }
-    if (ok && kStateOnly) {
-      const int64_t rec = bhi * (p.nseg - 1) + seg;
+    if (st_issuer && p.has_hout) bulk_wait<0>();
+    if (ok && (kMode == MODE_FWD_STATE || kMode == MODE_DH_STATE)) {
+      const int64_t rec = bhi * (p.nseg - 1) + seg - p.seg_base;
       float4* dst = reinterpret_cast<float4*>(p.ws_h + (rec * KD + key) * 128 + v0);
 #pragma unroll
       for (int j = 0; j < VS / 4; ++j)
         dst[j] = make_float4(hreg[4 * j], hreg[4 * j + 1], hreg[4 * j + 2], hreg[4 * j + 3]);
       if (vsl == 0) p.ws_d[rec * KD + key] = dacc;
-    } else if (ok && p.ht && seg == p.nseg - 1) {
+    } else if (ok && p.ht && seg == (kMode == MODE_DH ? 0 : p.nseg - 1)) {
       float4* dst = reinterpret_cast<float4*>(p.ht + (bhi * KD + key) * 128 + v0);
 #pragma unroll
       for (int j = 0; j < VS / 4; ++j)
@@ -665,17 +739,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // D_j of segment j) becomes the initial state of segment j+1,
 //   s_{j+1} = D_j * s_j + h_j,  s_0 = h0 (or 0),
 // the recurrence h_{n+1} = d_n (h_n + S_n) being linear in h_n with a per-row
-// scale.  One thread per 4 state entries of one (batch, head).
+// scale.  reverse (the DH scan): record j holds segment j+1's zero-start
+// gradient and decay, folded from the last segment down, starting from dht
+// (passed as h0).  One thread per 4 state entries of one (batch, head).
 __global__ void __launch_bounds__(256) gla_fold_kernel(const float* __restrict__ h0,
                                                        float* __restrict__ ws_h,
                                                        const float* __restrict__ ws_d, int BH,
-                                                       int nseg) {
+                                                       int nseg, int reverse) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<int64_t>(BH) * KD * 32) return;
   const int bh = static_cast<int>(i / (KD * 32));
   const int key = static_cast<int>((i / 32) % KD), c4 = static_cast<int>(i % 32);
   float4 h = h0 ? reinterpret_cast<const float4*>(h0)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int j = 0; j < nseg - 1; ++j) {
+  for (int i = 0; i < nseg - 1; ++i) {
+    const int j = reverse ? nseg - 2 - i : i;
     const int64_t rec = static_cast<int64_t>(bh) * (nseg - 1) + j;
     const float d = ws_d[rec * KD + key];
     float4* slot = reinterpret_cast<float4*>(ws_h + (rec * KD + key) * 128) + c4;
@@ -717,16 +794,16 @@ static size_t gla_ws_bytes(int64_t B, int64_t H, int nseg) {
   return ((hb + 255) / 256) * 256 + rec * 128 * 4;
 }
 
-template <int VS, bool kStateOnly>
+template <int VS, int kMode>
 static int launch_pass(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                       const CUtensorMap& tg, const gl::gla::Params& p, int grid, cudaStream_t st,
-                       const char** why) {
+                       const CUtensorMap& tg, const CUtensorMap& th, const gl::gla::Params& p,
+                       int grid, cudaStream_t st, const char** why) {
   using CF = gl::gla::Cfg<VS>;
-  if (!gl_set_smem_attr(reinterpret_cast<const void*>(gl::gla::chunk_gla_fwd_kernel<VS, kStateOnly>), 0,
+  if (!gl_set_smem_attr(reinterpret_cast<const void*>(gl::gla::chunk_gla_fwd_kernel<VS, kMode>), 0,
                         static_cast<int>(CF::SMEM_BYTES), why))
     return -2;
-  gl::gla::chunk_gla_fwd_kernel<VS, kStateOnly><<<grid, gl::gla::NUM_THREADS, CF::SMEM_BYTES, st>>>(
-      tq, tk, tv, tg, p);
+  gl::gla::chunk_gla_fwd_kernel<VS, kMode><<<grid, gl::gla::NUM_THREADS, CF::SMEM_BYTES, st>>>(
+      tq, tk, tv, tg, th, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     *why = cudaGetErrorString(e);
@@ -735,37 +812,60 @@ static int launch_pass(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
   return 0;
 }
 
+// One forward (rev = false: q, k slot = k, v slot = v, state output h_n) or
+// reverse state-gradient scan (rev = true: k slot = q, v slot = do, state
+// output E_n), with the state-only pre-pass and the fold of a sequence split.
 template <int VS>
-static int launch_vs(const void* q, const void* k, const void* v, const float* g,
-                     gl::gla::Params p, cudaStream_t st, const char** why) {
+static int launch_vs(const void* q, const void* kslot, const void* vslot, const float* g,
+                     void* sout, gl::gla::Params p, bool rev, cudaStream_t st, const char** why) {
   const int64_t BT = static_cast<int64_t>(p.B) * p.T;
-  CUtensorMap tq, tk, tv, tg;
-  if (!gl_make_tmap_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, 128, p.H, BT, 128,
+  CUtensorMap tq, tk, tv, tg, th;
+  if (!gl_make_tmap_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kslot, 128, p.H, BT, 128,
                        static_cast<int64_t>(p.H) * 128, 64, 1, 64, CU_TENSOR_MAP_SWIZZLE_128B, why))
     return -1;
-  if (!gl_make_tmap_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, 128, p.H, BT, 128,
+  if (!gl_make_tmap_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, vslot, 128, p.H, BT, 128,
                        static_cast<int64_t>(p.H) * 128, 64, 1, 64, CU_TENSOR_MAP_SWIZZLE_128B, why))
     return -1;
-  if (!gl_make_tmap_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, v, 128, p.H, BT, 128,
-                       static_cast<int64_t>(p.H) * 128, 64, 1, 64, CU_TENSOR_MAP_SWIZZLE_128B, why))
-    return -1;
+  if (q) {
+    if (!gl_make_tmap_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, 128, p.H, BT, 128,
+                         static_cast<int64_t>(p.H) * 128, 64, 1, 64, CU_TENSOR_MAP_SWIZZLE_128B,
+                         why))
+      return -1;
+  } else {
+    tq = tk;  // the reverse scan reads q through the k slot only
+  }
   if (g) {
     if (!gl_make_tmap_3d(&tg, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g, 128, p.H, BT, 128,
                          static_cast<int64_t>(p.H) * 128, 128, 1, 64, CU_TENSOR_MAP_SWIZZLE_NONE,
                          why))
       return -1;
   } else {
-    tg = tq;  // unused when the per-head gate is given
+    tg = tk;  // unused when the per-head gate is given
+  }
+  if (sout) {
+    // [B, NT, H, 128 keys, 128] bf16 as 2-D rows of 128, boxes of 64 x 128.
+    if (!gl_make_tmap_2d(&th, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, sout, 128, BT / 64 * p.H * 128, 128,
+                         64, 128, CU_TENSOR_MAP_SWIZZLE_128B, why))
+      return -1;
+  } else {
+    th = tk;  // unused
   }
   const int items = p.B * p.H * p.nsplit;
   if (p.nseg > 1) {
-    // State-only pass over segments 0 .. nseg-2, the fold, then the full pass.
+    // State-only pass over segments 0 .. nseg-2 (reverse: 1 .. nseg-1), the
+    // fold, then the full pass.
     gl::gla::Params p1 = p;
     p1.seg_grid = p.nseg - 1;
-    if (int rc = launch_pass<VS, true>(tq, tk, tv, tg, p1, items * p1.seg_grid, st, why)) return rc;
+    p1.seg_base = rev ? 1 : 0;
+    p1.has_hout = 0;
+    const int rc = rev ? launch_pass<VS, gl::gla::MODE_DH_STATE>(tq, tk, tv, tg, th, p1,
+                                                                 items * p1.seg_grid, st, why)
+                       : launch_pass<VS, gl::gla::MODE_FWD_STATE>(tq, tk, tv, tg, th, p1,
+                                                                  items * p1.seg_grid, st, why);
+    if (rc) return rc;
     const int64_t n4 = static_cast<int64_t>(p.B) * p.H * 128 * 32;
     gl::gla::gla_fold_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, st>>>(
-        p.h0, p.ws_h, p.ws_d, p.B * p.H, p.nseg);
+        p.h0, p.ws_h, p.ws_d, p.B * p.H, p.nseg, rev ? 1 : 0);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
       *why = cudaGetErrorString(e);
@@ -773,24 +873,27 @@ static int launch_vs(const void* q, const void* k, const void* v, const float* g
     }
   }
   p.seg_grid = p.nseg;
-  return launch_pass<VS, false>(tq, tk, tv, tg, p, items * p.nseg, st, why);
+  p.seg_base = 0;
+  p.has_hout = sout != nullptr;
+  return rev ? launch_pass<VS, gl::gla::MODE_DH>(tq, tk, tv, tg, th, p, items * p.nseg, st, why)
+             : launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, p, items * p.nseg, st, why);
 }
 
 size_t gl_chunk_gla_ws_bytes(int64_t B, int64_t T, int64_t H, int num_sms) {
   return gla_ws_bytes(B, H, gla_segments(B, T, H, num_sms));
 }
 
-int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float* g,
-                        const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
-                        int64_t H, int64_t K, int64_t V, void* o, float* ht, void* ws,
-                        size_t ws_bytes, int* err, cudaStream_t st, int num_sms, const char** why) {
-  (void)K;
-  (void)V;
+// Shared set-up of the forward and the reverse scan: scale, segments, V split.
+static int gla_dispatch(const void* q, const void* kslot, const void* vslot, const float* g,
+                        const float* g_gamma, const float* init, float scale, int64_t B,
+                        int64_t T, int64_t H, void* o, float* fin, void* sout, void* ws,
+                        size_t ws_bytes, int* err, bool rev, cudaStream_t st, int num_sms,
+                        const char** why) {
   gl::gla::Params p;
   p.g_gamma = g_gamma;
-  p.h0 = h0;
+  p.h0 = init;
   p.o = static_cast<__nv_bfloat16*>(o);
-  p.ht = ht;
+  p.ht = fin;
   p.err = err;
   p.scale = scale;
   p.scale_apart = !(scale > 0.f && std::isfinite(scale));
@@ -799,6 +902,8 @@ int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float
   p.T = static_cast<int>(T);
   p.H = static_cast<int>(H);
   p.has_g = g != nullptr;
+  p.seg_base = 0;
+  p.has_hout = 0;
   // Few (batch, head) pairs: split the sequence into segments (full V width,
   // one CTA per SM) when the workspace allows it, else split V in two.
   // GLAUCIS_GLA_VS=64|128 and GLAUCIS_GLA_SEGMENTS=n override the choice.
@@ -817,8 +922,28 @@ int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float
   if (const char* e = std::getenv("GLAUCIS_GLA_VS")) split_v = std::atoi(e) == 64;
   if (split_v) {
     p.nsplit = 2;
-    return launch_vs<64>(q, k, v, g, p, st, why);
+    return launch_vs<64>(q, kslot, vslot, g, sout, p, rev, st, why);
   }
   p.nsplit = 1;
-  return launch_vs<128>(q, k, v, g, p, st, why);
+  return launch_vs<128>(q, kslot, vslot, g, sout, p, rev, st, why);
+}
+
+int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float* g,
+                        const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
+                        int64_t H, int64_t K, int64_t V, void* o, float* ht, void* h_out, void* ws,
+                        size_t ws_bytes, int* err, cudaStream_t st, int num_sms, const char** why) {
+  (void)K;
+  (void)V;
+  return gla_dispatch(q, k, v, g, g_gamma, h0, scale, B, T, H, o, ht, h_out, ws, ws_bytes, err,
+                      false, st, num_sms, why);
+}
+
+// Reverse state-gradient scan of the backward: E_n (bf16 [B,NT,H,K,V]) for
+// every chunk and dh0 (fp32, nullable) from q, do, the gate and dht.
+int gl_launch_chunk_gla_dh(const void* q, const void* dout, const float* g, const float* g_gamma,
+                           const float* dht, float scale, int64_t B, int64_t T, int64_t H,
+                           void* e_out, float* dh0, void* ws, size_t ws_bytes, int* err,
+                           cudaStream_t st, int num_sms, const char** why) {
+  return gla_dispatch(nullptr, q, dout, g, g_gamma, dht, scale, B, T, H, nullptr, dh0, e_out, ws,
+                      ws_bytes, err, true, st, num_sms, why);
 }

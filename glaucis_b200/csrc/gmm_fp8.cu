@@ -644,13 +644,6 @@ constexpr uint32_t T_OFF_ROWOFF = T_OFF_MISC + 128;
 constexpr uint32_t T_SMEM_BYTES = T_OFF_ROWOFF + (MAX_G + 1) * 4 + 1024;
 constexpr uint32_t T_IDESC = idesc(1, 0, 0, 1, 1, 128, 256);  // A and B MN-major
 
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int32_t x,
-                                             int32_t y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(m),
-               "r"(smem_u32(src)), "r"(x), "r"(y)
-               : "memory");
-}
-
 // OR of `v` over the 128 threads of named barrier `id` (a barrier).
 __device__ __forceinline__ bool tgmm_bar_or(int id, bool v) {
   uint32_t r;

@@ -6,8 +6,9 @@ constant gate) mode as in KE/examples/kernels/chunk_gla.py, whose entry
 points it keeps: `_make_test_data`, `chunk_gla_fwd`, `chunk_gla`,
 `optimized_compute(B, T, H, K, V, chunk_size)`.
 
-optimized_compute runs the FORWARD pass and returns the scalar loss o.sum();
-the reference template also runs the backward, not built on B200 yet.
+optimized_compute runs the forward and the backward (reverse state-gradient
+scan + chunk-parallel dq/dk/dv kernel) and returns the scalar loss o.sum(),
+as the reference's value_and_grad does; mode="fwd" runs the forward only.
 """
 
 import torch
@@ -33,15 +34,20 @@ def chunk_gla_fwd(q, k, v, g_gamma, scale, chunk_size):
 
 
 def chunk_gla(q, k, v, g_gamma, scale, chunk_size):
-    """Chunked GLA forward output o (bf16)."""
-    _, _, _, o = chunk_gla_fwd(q, k, v, g_gamma, scale, chunk_size)
-    return o
+    """Chunked GLA output o (bf16), differentiable in q, k, v."""
+    return ops.chunk_gla(q, k, v, g_gamma, scale, chunk_size)
 
 
-def optimized_compute(B=2, T=4096, H=16, K=128, V=128, chunk_size=64):
-    """Forward chunked GLA; returns the loss scalar o.sum()."""
+def optimized_compute(B=2, T=4096, H=16, K=128, V=128, chunk_size=64, mode="fwd_bwd"):
+    """Forward + backward chunked GLA (gradients of q, k, v computed, as the
+    reference's value_and_grad); returns the loss scalar o.sum()."""
     q, k_arr, v, g_gamma = _make_test_data(B, T, H, K, V, chunk_size)
     scale = K ** -0.5
-    o = chunk_gla(q, k_arr, v, g_gamma, scale, chunk_size)
-    return o.float().sum().cpu()
+    if mode == "fwd":
+        return chunk_gla(q, k_arr, v, g_gamma, scale, chunk_size).float().sum().cpu()
+    for t in (q, k_arr, v):
+        t.requires_grad_(True)
+    loss = chunk_gla(q, k_arr, v, g_gamma, scale, chunk_size).float().sum()
+    loss.backward()
+    return loss.detach().cpu()
 # EVOLVE-BLOCK-END

@@ -375,11 +375,13 @@ def gmm_fp8_blockwise_host(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: to
 # ---------------------------------------------------------------------------
 class GLAForward(tuple):
     """Result of chunk_gla_fwd, unpackable as the reference's
-    (g_cumsum, A, h, o).  The fused kernel keeps g_cumsum, A and the per-chunk
-    states on chip, so those entries are None; the final state is `.ht`."""
+    (g_cumsum, A, h, o).  The fused kernel keeps g_cumsum and A on chip, so
+    those entries are None; h (the bf16 state before every chunk,
+    [B, T/64, H, K, V]) is returned when asked for with output_states=True,
+    else None; the final state is `.ht`."""
 
-    def __new__(cls, o: torch.Tensor, ht: Optional[torch.Tensor]):
-        self = tuple.__new__(cls, (None, None, None, o))
+    def __new__(cls, o: torch.Tensor, ht: Optional[torch.Tensor], h: Optional[torch.Tensor] = None):
+        self = tuple.__new__(cls, (None, None, h, o))
         self.ht = ht
         return self
 
@@ -387,19 +389,12 @@ class GLAForward(tuple):
     def o(self) -> torch.Tensor:
         return self[3]
 
+    @property
+    def h(self) -> Optional[torch.Tensor]:
+        return self[2]
 
-def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                  g_gamma: Optional[torch.Tensor], scale: float, chunk_size: int = 64, *,
-                  g: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
-                  output_final_state: bool = False,
-                  o: Optional[torch.Tensor] = None,
-                  ht: Optional[torch.Tensor] = None) -> GLAForward:
-    """Chunked GLA forward (KE/examples/kernels/chunk_gla.py:258-273), fused
-    into one kernel.  Either the per-head constant gate `g_gamma` [H] (the
-    reference template's mode) or the per-key log-gate `g` [B, T, H, K] (raw,
-    chunk-local cumsum taken in-kernel; semantics of
-    KE/upstream/fused_chunk_simple_gla/common_chunk_h.py:330-334) is used.
-    """
+
+def _gla_check(q, k, v, g_gamma, g, h0):
     _need_cuda(q, k, v, g_gamma, g, h0)
     B, T, H, K = q.shape
     V = v.shape[-1]
@@ -412,6 +407,24 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         raise ValueError("g_gamma must be fp32 [H]")
     if h0 is not None and (h0.dtype != torch.float32 or tuple(h0.shape) != (B, H, K, V)):
         raise ValueError("h0 must be fp32 [B, H, K, V]")
+    return B, T, H, K, V
+
+
+def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                  g_gamma: Optional[torch.Tensor], scale: float, chunk_size: int = 64, *,
+                  g: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
+                  output_final_state: bool = False, output_states: bool = False,
+                  o: Optional[torch.Tensor] = None,
+                  ht: Optional[torch.Tensor] = None) -> GLAForward:
+    """Chunked GLA forward (KE/examples/kernels/chunk_gla.py:258-273), fused
+    into one kernel.  Either the per-head constant gate `g_gamma` [H] (the
+    reference template's mode) or the per-key log-gate `g` [B, T, H, K] (raw,
+    chunk-local cumsum taken in-kernel; semantics of
+    KE/upstream/fused_chunk_simple_gla/common_chunk_h.py:330-334) is used.
+    output_states=True also returns the per-chunk states h (bf16), the
+    residual of the backward.
+    """
+    B, T, H, K, V = _gla_check(q, k, v, g_gamma, g, h0)
     if o is None:
         o = torch.empty((B, T, H, V), dtype=torch.bfloat16, device=q.device)
     if output_final_state and ht is None:
@@ -421,19 +434,85 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     # workspace for the per-segment states (0 bytes otherwise).
     ws_bytes = lib.gl_chunk_gla_fwd_workspace_bytes(B, T, H, K, V, chunk_size)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
-    _lib.check(lib.gl_chunk_gla_fwd_ws(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
-                                       _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
-                                       chunk_size, o.data_ptr(), _ptr(ht), _ptr(ws), ws_bytes,
-                                       None, _stream()),
-               "gl_chunk_gla_fwd")
-    return GLAForward(o, ht if output_final_state else None)
+    h = None
+    if output_states:
+        h = torch.empty((B, T // chunk_size, H, K, V), dtype=torch.bfloat16, device=q.device)
+        _lib.check(lib.gl_chunk_gla_fwd_states(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
+                                               _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
+                                               chunk_size, o.data_ptr(), _ptr(ht), h.data_ptr(),
+                                               _ptr(ws), ws_bytes, None, _stream()),
+                   "gl_chunk_gla_fwd_states")
+    else:
+        _lib.check(lib.gl_chunk_gla_fwd_ws(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
+                                           _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
+                                           chunk_size, o.data_ptr(), _ptr(ht), _ptr(ws), ws_bytes,
+                                           None, _stream()),
+                   "gl_chunk_gla_fwd")
+    return GLAForward(o, ht if output_final_state else None, h)
 
 
-def chunk_gla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g_gamma: torch.Tensor,
-              scale: float, chunk_size: int = 64) -> torch.Tensor:
-    """Forward of `chunk_gla(q, k, v, g_gamma, scale, chunk_size)`
-    (KE/examples/kernels/chunk_gla.py:434-456).  Returns o (bf16)."""
-    return chunk_gla_fwd(q, k, v, g_gamma, scale, chunk_size).o
+def chunk_gla_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, do: torch.Tensor,
+                  h: torch.Tensor, g_gamma: Optional[torch.Tensor], scale: float,
+                  chunk_size: int = 64, *, g: Optional[torch.Tensor] = None,
+                  dht: Optional[torch.Tensor] = None, output_dh0: bool = False
+                  ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, Optional[torch.Tensor]]:
+    """Backward of chunk_gla_fwd: (dq, dk, dv, dh0) for the output gradient
+    `do` (and the final-state gradient `dht`), from the forward's per-chunk
+    states `h` (chunk_gla_fwd(..., output_states=True).h).  Replaces _bwd of
+    KE/examples/kernels/chunk_gla.py:446-453 (reverse dh scan :281-305, fused
+    dq/dk/dv :313-426); the gate gets no gradient, as there."""
+    B, T, H, K, V = _gla_check(q, k, v, g_gamma, g, dht)
+    _need_cuda(do, h)
+    if do.dtype != torch.bfloat16 or tuple(do.shape) != (B, T, H, V):
+        raise ValueError("do must be bf16 [B, T, H, V]")
+    if h.dtype != torch.bfloat16 or tuple(h.shape) != (B, T // chunk_size, H, K, V):
+        raise ValueError("h must be bf16 [B, T/chunk, H, K, V]")
+    lib = _lib.load()
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    dh0 = torch.empty((B, H, K, V), dtype=torch.float32, device=q.device) if output_dh0 else None
+    ws_bytes = lib.gl_chunk_gla_bwd_workspace_bytes(B, T, H, K, V, chunk_size)
+    if ws_bytes == 0:
+        raise ValueError("gl_chunk_gla_bwd: unsupported shape")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    _lib.check(lib.gl_chunk_gla_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g), _ptr(g_gamma),
+                                    h.data_ptr(), do.data_ptr(), _ptr(dht), float(scale), B, T, H, K,
+                                    V, chunk_size, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                    _ptr(dh0), ws.data_ptr(), ws_bytes, None, _stream()),
+               "gl_chunk_gla_bwd")
+    return dq, dk, dv, dh0
+
+
+class _ChunkGLA(torch.autograd.Function):
+    """custom-VJP pair of the template (chunk_gla.py:434-456): the forward
+    keeps q, k, v, the gate and the per-chunk states; the backward returns
+    dq, dk, dv (and dh0 when h0 is given)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g_gamma, g, h0, scale, chunk_size):
+        res = chunk_gla_fwd(q, k, v, g_gamma, scale, chunk_size, g=g, h0=h0, output_states=True)
+        ctx.save_for_backward(q, k, v, g_gamma, g, res.h)
+        ctx.scale, ctx.chunk_size, ctx.has_h0 = scale, chunk_size, h0 is not None
+        return res.o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, g_gamma, g, h = ctx.saved_tensors
+        dq, dk, dv, dh0 = chunk_gla_bwd(q, k, v, do.to(torch.bfloat16).contiguous(), h, g_gamma,
+                                        ctx.scale, ctx.chunk_size, g=g, output_dh0=ctx.has_h0)
+        return dq, dk, dv, None, None, dh0, None, None
+
+
+def chunk_gla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g_gamma: Optional[torch.Tensor],
+              scale: float, chunk_size: int = 64, *, g: Optional[torch.Tensor] = None,
+              h0: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """`chunk_gla(q, k, v, g_gamma, scale, chunk_size)`
+    (KE/examples/kernels/chunk_gla.py:434-456): returns o (bf16),
+    differentiable in q, k, v (and h0) when any of them requires grad."""
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (q, k, v, h0)):
+        return _ChunkGLA.apply(q, k, v, g_gamma, g, h0, scale, chunk_size)
+    return chunk_gla_fwd(q, k, v, g_gamma, scale, chunk_size, g=g, h0=h0).o
 
 
 def device_status() -> int:

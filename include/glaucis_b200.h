@@ -144,6 +144,48 @@ int gl_chunk_gla_fwd_ws(const void* q, const void* k, const void* v, const float
                         size_t workspace_bytes, int* err_word, void* stream);
 
 /*
+ * Training forward of the chunked GLA: gl_chunk_gla_fwd_ws that also writes
+ * the state before every chunk, h_states bf16 [B, T/64, H, K, V]
+ * (h_states[:, n] = h_n, h_0 = h0), the residual the backward reads.
+ * Replaces the h output of chunk_gla_fwd (KE/examples/kernels/chunk_gla.py
+ * :258-273, kept fp32 there and cast to bf16 where the backward uses it,
+ * :356-359).
+ */
+int gl_chunk_gla_fwd_states(const void* q, const void* k, const void* v, const float* g,
+                            const float* g_gamma, const float* h0, float scale,
+                            int64_t B, int64_t T, int64_t H, int64_t K, int64_t V,
+                            int64_t chunk_size, void* o, float* ht, void* h_states,
+                            void* workspace, size_t workspace_bytes, int* err_word,
+                            void* stream);
+
+/*
+ * Backward of the chunked GLA: dq, dk, dv (bf16, shaped as q, k, v) and,
+ * when dh0 is non-NULL, the gradient of the initial state (fp32 [B,H,K,V]),
+ * for the loss sum(o * dout) (+ sum(ht * dht) when dht is non-NULL).
+ *   h_states  the forward's bf16 [B, T/64, H, K, V] (gl_chunk_gla_fwd_states)
+ *   dout      bf16 [B, T, H, V];  dht fp32 [B, H, K, V] or NULL
+ *   g / g_gamma, scale, shapes as the forward.  The gate is not
+ *   differentiated (the reference's custom_vjp returns dq, dk, dv).
+ *   workspace device memory of gl_chunk_gla_bwd_workspace_bytes(...) bytes
+ *   (required, 256-byte aligned): the reverse scan's per-chunk state
+ *   gradient E_n = e^{G_last(n)} dL/dh_{n+1} (bf16) and the records of its
+ *   sequence split.
+ * Two launches: the reverse state-gradient scan (a mode of the forward's
+ * sequential kernel, with its own sequence split) and the chunk-parallel
+ * dq/dk/dv kernel.  Replaces _bwd of chunk_gla (KE/examples/kernels/
+ * chunk_gla.py:446-453): _chunk_bwd_dh_scan :281-305 and
+ * chunk_gla_bwd_fused :313-426.
+ */
+size_t gl_chunk_gla_bwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K,
+                                        int64_t V, int64_t chunk_size);
+int gl_chunk_gla_bwd(const void* q, const void* k, const void* v, const float* g,
+                     const float* g_gamma, const void* h_states, const void* dout,
+                     const float* dht, float scale, int64_t B, int64_t T, int64_t H,
+                     int64_t K, int64_t V, int64_t chunk_size, void* dq, void* dk, void* dv,
+                     float* dh0, void* workspace, size_t workspace_bytes, int* err_word,
+                     void* stream);
+
+/*
  * Backward of the grouped matmul (KE/examples/kernels/gmm_fp8_blockwise.py:123-169).
  *
  * gl_quant_col_128x1: 128x1 column blocks of x bf16 [M, C] (M, C multiples

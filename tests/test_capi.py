@@ -66,6 +66,24 @@ def test_gla_rejects_bad_arguments_without_device():
     assert rc == _lib.GL_EINVAL and "256-byte" in _err()
     # workspace size query: 0 for unsupported shapes (no device needed)
     assert lib.gl_chunk_gla_fwd_workspace_bytes(1, 100, 1, 128, 128, 64) == 0
+    assert lib.gl_chunk_gla_bwd_workspace_bytes(1, 100, 1, 128, 128, 64) == 0
+    # training forward: the per-chunk state output is required
+    rc = lib.gl_chunk_gla_fwd_states(p, p, p, f, None, None, 0.1, 1, 64, 1, 128, 128, 64, p, None,
+                                     None, None, 0, None, None)
+    assert rc == _lib.GL_EINVAL and "h_states" in _err()
+    # backward: shape checks, then the required workspace
+    rc = lib.gl_chunk_gla_bwd(p, p, p, f, f, p, p, None, 0.1, 1, 64, 1, 128, 128, 64, p, p, p,
+                              None, None, 0, None, None)
+    assert rc == _lib.GL_EINVAL and "exactly one" in _err()
+    rc = lib.gl_chunk_gla_bwd(p, p, p, f, None, None, p, None, 0.1, 1, 64, 1, 128, 128, 64, p, p,
+                              p, None, None, 0, None, None)
+    assert rc == _lib.GL_EINVAL and "null pointer" in _err()
+    rc = lib.gl_chunk_gla_bwd(p, p, p, f, None, p, p, None, 0.1, 1, 64, 1, 128, 128, 64, p, p, p,
+                              None, None, 0, None, None)
+    assert rc == _lib.GL_EINVAL and "workspace" in _err()
+    rc = lib.gl_chunk_gla_bwd(p, p, p, f, None, p, p, None, 0.1, 1, 64, 1, 128, 128, 64, p, p, p,
+                              None, ctypes.c_void_p(272), 1 << 20, None, None)
+    assert rc == _lib.GL_EINVAL and "256-byte" in _err()
 
 
 def test_quantisers_reject_bad_arguments_without_device():

@@ -115,3 +115,28 @@ def test_gla_bwd_oracle_against_finite_differences():
             am[name][idx] -= eps
             fd = (loss(ap["q"], ap["k"], ap["v"], ap["h0"]) - loss(am["q"], am["k"], am["v"], am["h0"])) / (2 * eps)
             assert abs(fd - grads[name][idx]) < 1e-6 * max(1.0, abs(fd)), (name, idx, fd, grads[name][idx])
+
+
+@pytest.mark.parametrize("gate", ["per_key", "gamma"])
+@pytest.mark.parametrize("with_state", [False, True])
+def test_gla_chunked_bwd_oracle_against_autograd(gate, with_state):
+    # the chunked restatement of the reference backward (fp32, chunk formulas)
+    # against float64 autograd through the token recurrence
+    from oracle.gla_bwd_oracle import chunk_gla_bwd, gla_bwd_reference
+    rng = np.random.default_rng(3)
+    B, T, H, K, V, C = 1, 48, 2, 8, 6, 16
+    q = rng.standard_normal((B, T, H, K)).astype(np.float32)
+    k = rng.standard_normal((B, T, H, K)).astype(np.float32)
+    v = rng.standard_normal((B, T, H, V)).astype(np.float32)
+    do = rng.standard_normal((B, T, H, V)).astype(np.float32)
+    g = gg = None
+    if gate == "per_key":
+        g = (-np.abs(rng.standard_normal((B, T, H, K))) * 0.2).astype(np.float32)
+    else:
+        gg = (-np.abs(rng.standard_normal(H)) * 0.1).astype(np.float32)
+    h0 = (rng.standard_normal((B, H, K, V)) * 0.3).astype(np.float32) if with_state else None
+    dht = rng.standard_normal((B, H, K, V)).astype(np.float32) if with_state else None
+    got = chunk_gla_bwd(q, k, v, do, g=g, g_gamma=gg, h0=h0, scale=0.4, chunk_size=C, dht=dht)
+    ref = gla_bwd_reference(q, k, v, do, g=g, g_gamma=gg, h0=h0, scale=0.4, dht=dht)
+    for name, a, b in zip(("dq", "dk", "dv", "dh0"), got, ref):
+        np.testing.assert_allclose(a, b, rtol=2e-4, atol=2e-4 * np.abs(b).max(), err_msg=name)
