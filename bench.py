@@ -326,7 +326,6 @@ def run_reference(args):
 def run_b200(args):
     import torch
     from glaucis_b200 import configs, ops
-    from oracle import gla_oracle as GO
     rank, world, local = dist_setup(args.gpus)
     peaks, peak_kind = load_peaks()
     traffic = ncu_traffic("gmm_fp8_fwd_kernel", args.workload)
@@ -470,8 +469,8 @@ def run_b200(args):
         gla_ms = timed(gla_step, args.steps, args.warmup, world)
         if ops.device_status() != 0:
             raise SystemExit("device error word set after the GLA timed region")
-        gla_bytes = GO.gla_bytes(gcfg.B, gcfg.T, gcfg.H, has_h0=gcfg.h0_std > 0)
-        gla_flops = GO.gla_flops(gcfg.B, gcfg.T, gcfg.H)
+        gla_bytes = configs.gla_bytes(gcfg.B, gcfg.T, gcfg.H, has_h0=gcfg.h0_std > 0)
+        gla_flops = configs.gla_flops(gcfg.B, gcfg.T, gcfg.H)
         gla_gbs = gla_bytes / (gla_ms * 1e-3) / 1e9
         blk = {"workload": workload, "B": gcfg.B, "T": gcfg.T, "H": gcfg.H,
                "tokens_per_s": world * gcfg.B * gcfg.T / (gla_ms * 1e-3), "ms_per_step": gla_ms,
@@ -482,7 +481,48 @@ def run_b200(args):
                             "kernel": "chunk_gla_fwd_kernel", "peak_source": f"{peak_kind} hbm_gbs",
                             "algorithmic_bytes_per_step": gla_bytes,
                             "traffic": ncu_traffic("chunk_gla_fwd_kernel", workload)}}
-        del inp, go, ght
+        # backward: the training forward (o, ht and the per-chunk states h)
+        # and the backward (reverse state-gradient scan + chunk-parallel
+        # dq/dk/dv kernel) on a synthetic output gradient, buffers resident
+        gh = torch.empty((gcfg.B, gcfg.T // 64, gcfg.H, 128, 128), dtype=torch.bfloat16,
+                         device="cuda")
+
+        def fwd_states_step():
+            ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], 128 ** -0.5, 64,
+                              g=inp["g"], h0=inp["h0"], output_final_state=True, output_states=True,
+                              o=go, ht=ght, h=gh)
+
+        fs_ms = timed(fwd_states_step, max(5, args.steps // 2), 3, world)
+        gen = torch.Generator(device="cuda").manual_seed(args.seed + 11 + rank)
+        gdo = torch.randn(inp["v"].shape, generator=gen, device="cuda").to(torch.bfloat16)
+        dq, dk, dv = (torch.empty_like(inp[n]) for n in ("q", "k", "v"))
+        gws = torch.empty(ops.chunk_gla_bwd_workspace_bytes(gcfg.B, gcfg.T, gcfg.H),
+                          dtype=torch.uint8, device="cuda")
+
+        def bwd_step():
+            ops.chunk_gla_bwd(inp["q"], inp["k"], inp["v"], gdo, gh, inp["g_gamma"], 128 ** -0.5, 64,
+                              g=inp["g"], dq=dq, dk=dk, dv=dv, workspace=gws)
+
+        bw_ms = timed(bwd_step, max(5, args.steps // 2), 3, world)
+        if ops.device_status() != 0:
+            raise SystemExit("device error word set after the GLA backward rows")
+        pk = inp["g"] is not None
+        bw_bytes = configs.gla_bwd_bytes(gcfg.B, gcfg.T, gcfg.H, per_key_gate=pk)
+        bw_min = configs.gla_bwd_bytes(gcfg.B, gcfg.T, gcfg.H, per_key_gate=pk, fused_minimum=True)
+        bw_flops = configs.gla_bwd_flops(gcfg.B, gcfg.T, gcfg.H)
+        bw_gbs = bw_bytes / (bw_ms * 1e-3) / 1e9
+        blk["bwd"] = {
+            "ms_per_step": bw_ms, "tokens_per_s": world * gcfg.B * gcfg.T / (bw_ms * 1e-3),
+            "tflops": world * bw_flops / (bw_ms * 1e-3) / 1e12,
+            "achieved_gbs": bw_gbs, "hbm_frac": bw_gbs / peaks["hbm_gbs"],
+            "algorithmic_bytes_per_step": bw_bytes,
+            "fused_minimum_bytes": bw_min,
+            "fused_minimum_frac": bw_min / (bw_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+            "fwd_with_states_ms": fs_ms,
+            "kernels": "chunk_gla_fwd_kernel in reverse-scan mode (+ its state-only pre-pass and "
+                       "fold when the sequence is split), then chunk_gla_bwd_kernel",
+        }
+        del inp, go, ght, gh, gdo, dq, dk, dv, gws
         torch.cuda.empty_cache()
         return blk
 
@@ -557,6 +597,20 @@ def run_profile(args):
         def fn():
             ops.quant_act_1x128(x)
             ops.quant_w_128x128(w)
+    elif args.profile == "gla_bwd":
+        # the GLA backward (reverse scan + gradient kernel) on the GLA
+        # workload: inputs, the states h, E and the gradients resident
+        gcfg = configs.GLA_CONFIGS[args.gla_workload]
+        inp = configs.make_gla_inputs(gcfg, device="cuda", seed=args.seed)
+        h = ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], 128 ** -0.5, 64,
+                              g=inp["g"], h0=inp["h0"], output_states=True).h
+        gen = torch.Generator(device="cuda").manual_seed(args.seed + 11)
+        do = torch.randn(inp["v"].shape, generator=gen, device="cuda").to(torch.bfloat16)
+        dq, dk, dv = (torch.empty_like(inp[n]) for n in ("q", "k", "v"))
+        ws = torch.empty(ops.chunk_gla_bwd_workspace_bytes(gcfg.B, gcfg.T, gcfg.H),
+                         dtype=torch.uint8, device="cuda")
+        fn = lambda: ops.chunk_gla_bwd(inp["q"], inp["k"], inp["v"], do, h, inp["g_gamma"],
+                                       128 ** -0.5, 64, g=inp["g"], dq=dq, dk=dk, dv=dv, workspace=ws)
     else:
         gcfg = configs.GLA_CONFIGS[args.gla_workload]
         inp = configs.make_gla_inputs(gcfg, device="cuda", seed=args.seed)
@@ -582,7 +636,7 @@ def main(argv=None):
     ap.add_argument("--cpu-rows", type=int, default=8192,
                     help="rows of the headline workload in one CPU-baseline step")
     ap.add_argument("--cpu-gla-tokens", type=int, default=4096)
-    ap.add_argument("--profile", choices=["gmm", "gla", "quant"], default=None,
+    ap.add_argument("--profile", choices=["gmm", "gla", "gla_bwd", "quant"], default=None,
                     help="run one kernel only, small footprint (for ncu captures)")
     ap.add_argument("--gla-workload", default=GLA_WORKLOAD)
     args = ap.parse_args(argv)

@@ -156,3 +156,49 @@ def make_gla_inputs(cfg: GLAConfig, device="cuda", seed: int = 0):
         out["h0"] = torch.randn((cfg.B, cfg.H, cfg.K, cfg.V), generator=gen,
                                 device=device) * cfg.h0_std
     return out
+
+
+# ---------------------------------------------------------------------------
+# Roofline accounting of the GLA kernels
+# ---------------------------------------------------------------------------
+def gla_flops(B: int, T: int, H: int, K: int = 128, V: int = 128, C: int = 64) -> float:
+    """Algorithmic FLOPs of the forward: per token-head 2CK (QK^T) + 2CV (A.V)
+    + 2KV (q.h) + 2KV (k^T v state update)."""
+    return float(B) * T * H * (2 * C * K + 2 * C * V + 2 * K * V + 2 * K * V)
+
+
+def gla_bytes(B: int, T: int, H: int, K: int = 128, V: int = 128, per_key_gate: bool = True,
+              has_h0: bool = False, has_ht: bool = True) -> float:
+    """Algorithmic HBM bytes of the forward: q, k, v (bf16) + g (fp32, per-key
+    gate) + o (bf16) per token-head, plus the final (and initial) state per
+    sequence."""
+    per_tok = 2 * K + 2 * K + 2 * V + (4 * K if per_key_gate else 0) + 2 * V
+    state = 4 * K * V * (int(has_h0) + int(has_ht))
+    return float(B) * T * H * per_tok + float(B) * H * state
+
+
+def gla_bwd_flops(B: int, T: int, H: int, K: int = 128, V: int = 128, C: int = 64) -> float:
+    """Algorithmic FLOPs of the backward per token-head: the scan's Qs^T do
+    (2KV) and the gradient kernel's A, dA (2CK + 2CV), do h^T and v E^T
+    (2 x 2KV), dP Kg and dP^T Qs (2 x 2CK), P^T do (2CV), Kg E (2KV)."""
+    return float(B) * T * H * (2 * K * V + 2 * C * K + 2 * C * V + 4 * K * V + 4 * C * K
+                               + 2 * C * V + 2 * K * V)
+
+
+def gla_bwd_bytes(B: int, T: int, H: int, K: int = 128, V: int = 128, C: int = 64,
+                  per_key_gate: bool = True, fused_minimum: bool = False) -> float:
+    """HBM bytes of the backward per token-head.  The two-kernel design: the
+    reverse scan reads q, do (bf16) and g, and writes E (bf16 [K, V] per
+    chunk); the gradient kernel reads q, k, v, do, g, h and E and writes dq,
+    dk, dv.  fused_minimum: one pass that keeps E on chip (reads q, k, v,
+    do, g, h; writes dq, dk, dv)."""
+    g = 4 * K if per_key_gate else 0
+    state = 2 * K * V / C  # one bf16 [K, V] tile per chunk, per token
+    grads_rd = 2 * K + 2 * K + 2 * V + 2 * V + g + state
+    grads_wr = 2 * K + 2 * K + 2 * V
+    if fused_minimum:
+        per_tok = grads_rd + grads_wr
+    else:
+        per_tok = (2 * K + 2 * V + g + state) + (grads_rd + state + grads_wr)
+    return float(B) * T * H * per_tok
+

@@ -415,14 +415,15 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                   g: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
                   output_final_state: bool = False, output_states: bool = False,
                   o: Optional[torch.Tensor] = None,
-                  ht: Optional[torch.Tensor] = None) -> GLAForward:
+                  ht: Optional[torch.Tensor] = None,
+                  h: Optional[torch.Tensor] = None) -> GLAForward:
     """Chunked GLA forward (KE/examples/kernels/chunk_gla.py:258-273), fused
     into one kernel.  Either the per-head constant gate `g_gamma` [H] (the
     reference template's mode) or the per-key log-gate `g` [B, T, H, K] (raw,
     chunk-local cumsum taken in-kernel; semantics of
     KE/upstream/fused_chunk_simple_gla/common_chunk_h.py:330-334) is used.
     output_states=True also returns the per-chunk states h (bf16), the
-    residual of the backward.
+    residual of the backward.  o, ht and h may be given preallocated.
     """
     B, T, H, K, V = _gla_check(q, k, v, g_gamma, g, h0)
     if o is None:
@@ -434,9 +435,8 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     # workspace for the per-segment states (0 bytes otherwise).
     ws_bytes = lib.gl_chunk_gla_fwd_workspace_bytes(B, T, H, K, V, chunk_size)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
-    h = None
     if output_states:
-        h = torch.empty((B, T // chunk_size, H, K, V), dtype=torch.bfloat16, device=q.device)
+        h = _out(h, (B, T // chunk_size, H, K, V), torch.bfloat16, q.device, "h")
         _lib.check(lib.gl_chunk_gla_fwd_states(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
                                                _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
                                                chunk_size, o.data_ptr(), _ptr(ht), h.data_ptr(),
@@ -454,13 +454,17 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 def chunk_gla_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, do: torch.Tensor,
                   h: torch.Tensor, g_gamma: Optional[torch.Tensor], scale: float,
                   chunk_size: int = 64, *, g: Optional[torch.Tensor] = None,
-                  dht: Optional[torch.Tensor] = None, output_dh0: bool = False
+                  dht: Optional[torch.Tensor] = None, output_dh0: bool = False,
+                  dq: Optional[torch.Tensor] = None, dk: Optional[torch.Tensor] = None,
+                  dv: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None
                   ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, Optional[torch.Tensor]]:
     """Backward of chunk_gla_fwd: (dq, dk, dv, dh0) for the output gradient
     `do` (and the final-state gradient `dht`), from the forward's per-chunk
     states `h` (chunk_gla_fwd(..., output_states=True).h).  Replaces _bwd of
     KE/examples/kernels/chunk_gla.py:446-453 (reverse dh scan :281-305, fused
-    dq/dk/dv :313-426); the gate gets no gradient, as there."""
+    dq/dk/dv :313-426); the gate gets no gradient, as there.  dq, dk, dv and
+    the uint8 `workspace` (chunk_gla_bwd_workspace_bytes) may be given
+    preallocated."""
     B, T, H, K, V = _gla_check(q, k, v, g_gamma, g, dht)
     _need_cuda(do, h)
     if do.dtype != torch.bfloat16 or tuple(do.shape) != (B, T, H, V):
@@ -468,20 +472,30 @@ def chunk_gla_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, do: torch.T
     if h.dtype != torch.bfloat16 or tuple(h.shape) != (B, T // chunk_size, H, K, V):
         raise ValueError("h must be bf16 [B, T/chunk, H, K, V]")
     lib = _lib.load()
-    dq = torch.empty_like(q)
-    dk = torch.empty_like(k)
-    dv = torch.empty_like(v)
+    dq = _out(dq, q.shape, torch.bfloat16, q.device, "dq")
+    dk = _out(dk, k.shape, torch.bfloat16, q.device, "dk")
+    dv = _out(dv, v.shape, torch.bfloat16, q.device, "dv")
     dh0 = torch.empty((B, H, K, V), dtype=torch.float32, device=q.device) if output_dh0 else None
     ws_bytes = lib.gl_chunk_gla_bwd_workspace_bytes(B, T, H, K, V, chunk_size)
     if ws_bytes == 0:
         raise ValueError("gl_chunk_gla_bwd: unsupported shape")
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    if workspace is None:
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    elif workspace.dtype != torch.uint8 or workspace.numel() < ws_bytes or not workspace.is_cuda:
+        raise ValueError(f"workspace must be a CUDA uint8 tensor of at least {ws_bytes} bytes")
+    ws = workspace
     _lib.check(lib.gl_chunk_gla_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g), _ptr(g_gamma),
                                     h.data_ptr(), do.data_ptr(), _ptr(dht), float(scale), B, T, H, K,
                                     V, chunk_size, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
-                                    _ptr(dh0), ws.data_ptr(), ws_bytes, None, _stream()),
+                                    _ptr(dh0), ws.data_ptr(), ws.numel(), None, _stream()),
                "gl_chunk_gla_bwd")
     return dq, dk, dv, dh0
+
+
+def chunk_gla_bwd_workspace_bytes(B: int, T: int, H: int, K: int = 128, V: int = 128,
+                                  chunk_size: int = 64) -> int:
+    """Device workspace chunk_gla_bwd needs for this shape on the current device."""
+    return int(_lib.load().gl_chunk_gla_bwd_workspace_bytes(B, T, H, K, V, chunk_size))
 
 
 class _ChunkGLA(torch.autograd.Function):

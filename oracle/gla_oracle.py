@@ -105,18 +105,3 @@ def naive_recurrence(q, k, v, g=None, g_gamma=None, h0=None, scale=None, chunk_s
         S = S * np.exp(gt[:, t])[..., None] + k[:, t, :, :, None] * v[:, t, :, None, :]
         o[:, t] = scale * np.einsum("bhk,bhkv->bhv", q[:, t], S)
     return o, S
-
-
-def gla_flops(B: int, T: int, H: int, K: int = 128, V: int = 128, C: int = 64) -> float:
-    """Algorithmic FLOPs: per token-head 2CK (QK^T) + 2CV (A.V) + 2KV (q.h)
-    + 2KV (k^T v state update)."""
-    return float(B) * T * H * (2 * C * K + 2 * C * V + 2 * K * V + 2 * K * V)
-
-
-def gla_bytes(B: int, T: int, H: int, K: int = 128, V: int = 128, per_key_gate: bool = True,
-              has_h0: bool = False, has_ht: bool = True) -> float:
-    """Algorithmic HBM bytes: q, k, v (bf16) + g (fp32, per-key gate) + o (bf16)
-    per token-head, plus the final (and initial) state per sequence."""
-    per_tok = 2 * K + 2 * K + 2 * V + (4 * K if per_key_gate else 0) + 2 * V
-    state = 4 * K * V * (int(has_h0) + int(has_ht))
-    return float(B) * T * H * per_tok + float(B) * H * state

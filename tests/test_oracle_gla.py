@@ -68,8 +68,13 @@ def test_golden_fixture_reproduces():
 
 
 def test_flop_and_byte_model():
-    assert O.gla_flops(8, 4096, 16) == pytest.approx(51.54e9, rel=1e-3)
-    assert O.gla_bytes(8, 4096, 16) == pytest.approx(0.814e9, rel=2e-2)
+    from glaucis_b200 import configs
+    assert configs.gla_flops(8, 4096, 16) == pytest.approx(51.54e9, rel=1e-3)
+    assert configs.gla_bytes(8, 4096, 16) == pytest.approx(0.814e9, rel=2e-2)
+    # backward: 212,992 FLOP and 4,864 B (two-kernel design) per token-head
+    assert configs.gla_bwd_flops(1, 1, 1) == 212992
+    assert configs.gla_bwd_bytes(1, 1, 1) == 4864
+    assert configs.gla_bwd_bytes(1, 1, 1, fused_minimum=True) == 2816
 
 
 @pytest.mark.parametrize("gate", ["per_key", "gamma"])
