@@ -637,8 +637,12 @@ constexpr uint32_t T_OUT_BYTES = 128 * 256 * 2;  // bf16 output tile: 4 atoms of
 constexpr uint32_t T_OFF_A = 0;
 constexpr uint32_t T_OFF_B = T_OFF_A + T_STAGES * T_A_BYTES;
 constexpr uint32_t T_OFF_OUT = T_OFF_B + T_STAGES * T_B_BYTES;
-constexpr uint32_t T_OFF_DS = T_OFF_OUT + T_OUT_BYTES;  // [2 halves][2 buffers][128] floats
-constexpr uint32_t T_OFF_BAR = T_OFF_DS + 2 * 2 * 128 * 4;
+// Scale ring: per row block, ls[mb, k0 .. k0+127] (512 B) then ds[mb, n0 .. n0+255] (1 KB),
+// bulk-copied by the producer next to the operand tiles and released by the epilogue.
+constexpr int T_SC_SLOTS = 4;
+constexpr uint32_t T_SC_BYTES = 512 + 1024;
+constexpr uint32_t T_OFF_SC = T_OFF_OUT + T_OUT_BYTES;
+constexpr uint32_t T_OFF_BAR = T_OFF_SC + T_SC_SLOTS * T_SC_BYTES;
 constexpr uint32_t T_OFF_MISC = T_OFF_BAR + 256;
 constexpr uint32_t T_OFF_ROWOFF = T_OFF_MISC + 128;
 constexpr uint32_t T_SMEM_BYTES = T_OFF_ROWOFF + (MAX_G + 1) * 4 + 1024;
@@ -686,11 +690,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + NBUF;
   uint64_t* drain = tempty + NBUF;
+  uint64_t* sc_full = drain + 1;
+  uint64_t* sc_empty = sc_full + T_SC_SLOTS;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + T_OFF_MISC);
   int* abort_flag = reinterpret_cast<int*>(smem + T_OFF_MISC + 4);
   int* valid_s = reinterpret_cast<int*>(smem + T_OFF_MISC + 8);
   int* row_off = reinterpret_cast<int*>(smem + T_OFF_ROWOFF);
-  float* dsbuf = reinterpret_cast<float*>(smem + T_OFF_DS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.G, K = p.K, N = p.N;
@@ -715,6 +720,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_init(&tempty[i], 8);
       }
       mbar_init(drain, 1);
+      for (int i = 0; i < T_SC_SLOTS; ++i) {
+        mbar_init(&sc_full[i], 1);
+        mbar_init(&sc_empty[i], 8);
+      }
       *abort_flag = 0;
       fence_mbar_init();
     }
@@ -757,7 +766,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
     if (lane == 0) {
       // ------------------------------------------------------------ producer
-      int it = 0;
+      int it = 0, sc_it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         int g, k0, n0, r0, r1, mb0, nblk;
@@ -773,13 +782,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tma_load_2d(sa, &tm_a, &full[s], k0, m0);
           tma_load_2d(sb, &tm_b, &full[s], n0, m0);
           tma_load_2d(sb + 16384, &tm_b, &full[s], n0 + 128, m0);
+          // the block's scales: ls[mb, k0 ..] and ds[mb, n0 ..] (N % 128 == 0)
+          const int c = it % T_SC_SLOTS;
+          if (!mbar_wait(&sc_empty[c], ((it / T_SC_SLOTS) & 1) ^ 1, ab)) { ok = false; ++it; break; }
+          const uint32_t dsn = static_cast<uint32_t>(min(256, N - n0)) * 4u;
+          uint8_t* sc = smem + T_OFF_SC + c * T_SC_BYTES;
+          mbar_arrive_expect_tx(&sc_full[c], 512u + dsn);
+          bulk_load(sc, p.ls + static_cast<int64_t>(mb0 + b) * K + k0, 512u, &sc_full[c]);
+          bulk_load(sc + 512, p.ds + static_cast<int64_t>(mb0 + b) * N + n0, dsn, &sc_full[c]);
+          ++sc_it;
         }
       }
       if (!ok) {
+        // copies in flight finish before the CTA exits (bounded waits)
         const int first = it > STAGES ? it - STAGES : 0;
         for (int j = first; j < it; ++j) {
           const uint64_t t0 = global_ns();
           while (!mbar_try_wait(&full[j % STAGES], (j / STAGES) & 1) && global_ns() - t0 < 100000000ull) {
+          }
+        }
+        const int sfirst = sc_it > T_SC_SLOTS ? sc_it - T_SC_SLOTS : 0;
+        for (int j = sfirst; j < sc_it; ++j) {
+          const uint64_t t0 = global_ns();
+          while (!mbar_try_wait(&sc_full[j % T_SC_SLOTS], (j / T_SC_SLOTS) & 1) &&
+                 global_ns() - t0 < 100000000ull) {
           }
         }
       }
@@ -862,16 +888,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int j = 0; j < EC / 2; ++j) acc[j] = make_float2(0.f, 0.f);
       for (int b = 0; b < nblk; ++b, ++acc_it) {
-        const int mb = mb0 + b;
         const int buf = acc_it % NBUF;
-        // column scales of this block: one per thread of the half, via smem
-        float* dsb = dsbuf + (chalf * 2 + buf) * 128;
-        dsb[ht] = col_ok ? __ldg(p.ds + static_cast<int64_t>(mb) * N + ncol0 + ht) : 0.f;
-        const float lsr = __ldg(p.ls + static_cast<int64_t>(mb) * K + k0 + r);
-        // a barrier of this half that also votes: once any role gave up,
-        // every thread of the half leaves here together
-        if (tgmm_bar_or(1 + chalf, *static_cast<volatile int*>(abort_flag) != 0)) { stop = true; break; }
-        // a wait that gives up sets the abort flag: the next vote stops the half
+        const int c = acc_it % T_SC_SLOTS;
+        // the block's scales, bulk-copied by the producer (a wait that gives
+        // up sets the abort flag; the tile's vote below stops the half)
+        if (!mbar_wait(&sc_full[c], (acc_it / T_SC_SLOTS) & 1, ab)) { ok = false; continue; }
+        const float* scl = reinterpret_cast<const float*>(smem + T_OFF_SC + c * T_SC_BYTES);
+        const float lsr = scl[r];
+        const float* dsb = scl + 128 + chalf * EC;
         if (!mbar_wait(&tfull[buf], (acc_it / NBUF) & 1, ab)) { ok = false; continue; }
         tc_fence_after();
         const uint32_t ta = lane_base + buf * BN;
@@ -906,8 +930,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) mbar_arrive(&tempty[buf]);
         promote(v[0], 16 * (NCH - 2));
         promote(v[1], 16 * (NCH - 1));
-        // dsb of this buffer is rewritten two blocks later, after this
-        // half's next barrier: every thread has read it by then
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sc_empty[c]);
       }
       if (stop) break;
       if (p.out_f32) {
@@ -924,7 +948,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // thread of the half takes part (the condition is the half's vote).
         const bool leader = ht == 0;
         if (leader) bulk_wait_read<0>();  // the previous tile's stores have read the tile
-        asm volatile("bar.sync %0, 128;" ::"r"(3 + chalf) : "memory");
+        // a barrier of this half that also votes: once any role gave up,
+        // every thread of the half leaves here together
+        if (tgmm_bar_or(3 + chalf, *static_cast<volatile int*>(abort_flag) != 0)) { stop = true; break; }
         uint8_t* ot = smem + T_OFF_OUT + chalf * 2 * 16384;
 #pragma unroll
         for (int i = 0; i < EC / 8; ++i) {
