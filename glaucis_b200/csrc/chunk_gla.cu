@@ -47,10 +47,11 @@ static_assert(128 * REG_CTRL + 256 * 128 + 128 * REG_STATE <= NUM_THREADS * 128,
 template <int VS>
 struct Cfg {
   // q/k/v ring depth: a stage is released only once O of its chunk has
-  // completed, so with two stages the gating of chunk n+2 waits for the whole
-  // A -> P -> O chain of chunk n; VS = 64 leaves room for three.  The S
-  // accumulator is double-buffered in TMEM when its columns fit (VS = 64).
-  static constexpr int QS = VS == 64 ? 3 : 2;
+  // completed, so the load of chunk n+3 waits for the A -> P -> O chain of
+  // chunk n.  The raw gate has one buffer, reloaded for chunk n+1 as soon as
+  // the gating of chunk n has read it.  The S accumulator is double-buffered
+  // in TMEM when its columns fit (VS = 64).
+  static constexpr int QS = 3;
   static constexpr int NS = VS == 64 ? 2 : 1;
   static constexpr int V_BOXES = VS / 64;
   static constexpr uint32_t Q_BYTES = C * KD * 2;          // 16 KB (2 boxes of 64 features)
@@ -62,7 +63,7 @@ struct Cfg {
   static constexpr uint32_t OFF_K = OFF_Q + QS * Q_BYTES;
   static constexpr uint32_t OFF_V = OFF_K + QS * Q_BYTES;
   static constexpr uint32_t OFF_G = OFF_V + QS * V_BYTES;
-  static constexpr uint32_t OFF_P = OFF_G + 2 * G_BYTES;
+  static constexpr uint32_t OFF_P = OFF_G + G_BYTES;
   static constexpr uint32_t OFF_H = OFF_P + P_BYTES;
   static constexpr uint32_t OFF_DEC = OFF_H + H_BYTES;      // 2 x 128 floats
   static constexpr uint32_t OFF_PART = OFF_DEC + 2 * KD * 4;  // [2][8 warps][32 lanes] float4
@@ -119,8 +120,8 @@ struct Params {
 enum {
   B_QKV_FULL = 0,    // [QS] TMA -> gating
   B_QKV_EMPTY = 3,   // [QS] O_n committed -> TMA
-  B_G_FULL = 6,      // [2] TMA -> gating
-  B_G_EMPTY = 8,     // [2] gating -> TMA
+  B_G_FULL = 6,      // TMA -> gating
+  B_G_EMPTY = 7,     // gating -> TMA (8 warps read the gate)
   B_PREP = 10,       // [2] gating -> MMA
   B_DEC_FULL = 12,   // [2] gating -> state
   B_DEC_EMPTY = 14,  // [2] state -> gating
@@ -205,8 +206,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&bar[B_QKV_EMPTY + i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar[B_G_FULL + i], 1);
-      mbar_init(&bar[B_G_EMPTY + i], GATE_WARPS);
       mbar_init(&bar[B_PREP + i], GATE_WARPS);
       mbar_init(&bar[B_DEC_FULL + i], GATE_WARPS);
       mbar_init(&bar[B_GSYNC + i], GATE_WARPS);
@@ -224,6 +223,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(&bar[B_H_FULL], STATE_WARPS);
     mbar_init(&bar[B_DRAIN], 1);
     mbar_init(&bar[B_HST], 1);
+    mbar_init(&bar[B_G_FULL], 1);
+    mbar_init(&bar[B_G_EMPTY], GATE_WARPS);
     *abort_flag = 0;
     fence_mbar_init();
   } else if (warp == 2) {
@@ -387,11 +388,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ----------------------------------------------------------- TMA g
     if (lane == 0 && p.has_g) {
       for (int n = 0; n < NT; ++n) {
-        const int s = n & 1;
-        if (!mbar_wait(&bar[B_G_EMPTY + s], ((n >> 1) & 1) ^ 1, ab)) break;
-        mbar_arrive_expect_tx(&bar[B_G_FULL + s], CF::G_BYTES);
-        tma_load_3d(smem + CF::OFF_G + s * CF::G_BYTES, &tm_g, &bar[B_G_FULL + s], 0, h,
-                    tok0 + chunk_of(n) * C);
+        if (!mbar_wait(&bar[B_G_EMPTY], (n & 1) ^ 1, ab)) break;
+        mbar_arrive_expect_tx(&bar[B_G_FULL], CF::G_BYTES);
+        tma_load_3d(smem + CF::OFF_G, &tm_g, &bar[B_G_FULL], 0, h, tok0 + chunk_of(n) * C);
       }
     }
     __syncwarp();
@@ -448,7 +447,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int n = 0; n < NT && gok; ++n) {
       const int s = n & 1;
       const uint32_t ph2 = (n >> 1) & 1;
-      if (p.has_g && !mbar_wait(&bar[B_G_FULL + s], ph2, ab)) { gok = false; break; }
+      if (p.has_g && !mbar_wait(&bar[B_G_FULL], n & 1, ab)) { gok = false; break; }
       if (!mbar_wait(&bar[B_QKV_FULL + n % CF::QS], (n / CF::QS) & 1, ab)) { gok = false; break; }
       if (!mbar_wait(&bar[B_DEC_EMPTY + s], ph2 ^ 1, ab)) { gok = false; break; }
       uint8_t* qs = smem + CF::OFF_Q + (n % CF::QS) * CF::Q_BYTES + qk_atom + qk_sub;
@@ -456,7 +455,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       float4 gv[8];
       float4 G = make_float4(0.f, 0.f, 0.f, 0.f);
       if (p.has_g) {
-        const float4* g4 = reinterpret_cast<const float4*>(smem + CF::OFF_G + s * CF::G_BYTES) + lane;
+        const float4* g4 = reinterpret_cast<const float4*>(smem + CF::OFF_G) + lane;
         float4 tot = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -466,6 +465,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tot.z += gv[i].z;
           tot.w += gv[i].w;
         }
+        // the gate buffer can take the next chunk's gate
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[B_G_EMPTY]);
         float4* part = reinterpret_cast<float4*>(smem + CF::OFF_PART) + s * (GATE_WARPS * 32);
         part[gw * 32 + lane] = tot;
         __syncwarp();
@@ -536,7 +538,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        if (p.has_g) mbar_arrive(&bar[B_G_EMPTY + s]);
         mbar_arrive(&bar[B_PREP + s]);
         mbar_arrive(&bar[B_DEC_FULL + s]);
       }
