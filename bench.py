@@ -529,6 +529,11 @@ def run_b200(args):
     gla = gla_block(GLA_WORKLOAD)
     gla_long = gla_block(GLA_LONG_WORKLOAD)
 
+    # ------------------------------------------ one instance across ranks
+    sharded = None
+    if world > 1 and not args.skip_sharded:
+        sharded = run_sharded(args, rank, world, max(3, args.steps // 2), 3)
+
     # ------------------------------------------------------- CPU baseline
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -562,12 +567,120 @@ def run_b200(args):
             "gmm_bwd": gmm_bwd,
             "gla": gla,
             "gla_long": gla_long,
+            "sharded": sharded,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
     return 0
+
+
+def run_sharded(args, rank, world, steps, warmup):
+    """Strong scaling of one workload instance across the ranks (N > 1 only):
+    gmm_dense_expert split by expert group (row ranges at 128-row cuts) with
+    an all-gather of the output rows, gla_b1_t32768 split by head with an
+    all-gather of the head blocks.  Compute-only and gather-inclusive device
+    times (max over ranks); rank 0 checks the gathered result against the
+    single-GPU one (GMM: bit for bit; GLA: to rounding, its sequence split
+    differs)."""
+    import torch
+    from glaucis_b200 import configs, ops, shard
+    res = {}
+    # ------------------------------------------------ GMM by expert group
+    cfg = configs.GMM_CONFIGS["gmm_dense_expert"]
+    lhs, rhs, gs = configs.make_gmm_inputs(cfg, device="cuda", seed=args.seed)
+    sizes = gs.cpu().numpy()
+    parts = shard.gmm_partition(sizes, world)
+    me = parts[rank]
+    counts = [p.rows for p in parts]
+    a_q, a_s = ops.quant_act_1x128(lhs[me.r0:me.r1].contiguous())
+    b_q, b_s = ops.quant_w_128x128(rhs[me.g0:me.g1].contiguous())
+    gs_l = torch.from_numpy(me.sizes).to("cuda")
+    out_l = torch.empty((me.rows, cfg.N), dtype=torch.bfloat16, device="cuda")
+    out_full = torch.empty((sum(counts), cfg.N), dtype=torch.bfloat16, device="cuda")
+
+    def gmm_local():
+        if me.rows:
+            ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs_l, out=out_l)
+
+    def gmm_gathered():
+        gmm_local()
+        shard.all_gather_rows(out_l, counts, out_full)
+
+    c_ms = timed(gmm_local, steps, warmup, world)
+    g_ms = timed(gmm_gathered, steps, warmup, world)
+    flops = 2.0 * float(sizes.sum()) * cfg.K * cfg.N
+    same = None
+    if rank == 0:
+        fa, fs = ops.quant_act_1x128(lhs)
+        fb, fbs = ops.quant_w_128x128(rhs)
+        single = ops.gmm_fp8_fwd(fa, fs, fb, fbs, gs, out_dtype=torch.bfloat16)
+        same = bool(torch.equal(single[: sum(counts)], out_full))
+        del fa, fs, fb, fbs, single
+    if ops.device_status() != 0:
+        raise SystemExit("device error word set after the sharded GMM")
+    res["gmm"] = {"workload": "gmm_dense_expert", "split": "expert groups, 128-row cuts",
+                  "rows_per_rank": counts, "groups_per_rank": [p.g1 - p.g0 for p in parts],
+                  "compute_ms": c_ms, "with_gather_ms": g_ms,
+                  "tflops_compute": flops / (c_ms * 1e-3) / 1e12,
+                  "tflops_with_gather": flops / (g_ms * 1e-3) / 1e12,
+                  "gather_bytes_per_rank": 2 * cfg.N * (cfg.M - me.rows),
+                  "matches_single_gpu": same, "scaling": "strong"}
+    del lhs, rhs, a_q, a_s, b_q, b_s, out_l, out_full
+    torch.cuda.empty_cache()
+    # ------------------------------------------------------- GLA by head
+    gcfg = configs.GLA_CONFIGS["gla_b1_t32768"]
+    inp = configs.make_gla_inputs(gcfg, device="cuda", seed=args.seed)
+    hr = shard.gla_head_partition(gcfg.H, world)[rank]
+    heads = [len(r) for r in shard.gla_head_partition(gcfg.H, world)]
+    sl = lambda t: t[:, :, hr.start:hr.stop].contiguous()
+    q, k, v, g = sl(inp["q"]), sl(inp["k"]), sl(inp["v"]), sl(inp["g"])
+    h0 = inp["h0"][:, hr.start:hr.stop].contiguous()
+    o_l = torch.empty_like(v)
+    ht_l = torch.empty_like(h0)
+    blk = gcfg.B * gcfg.T * gcfg.V  # elements of one head's output
+
+    def gla_local():
+        ops.chunk_gla_fwd(q, k, v, None, 128 ** -0.5, 64, g=g, h0=h0, output_final_state=True,
+                          o=o_l, ht=ht_l)
+
+    # head-block-major staging: rank r's [B, T, H_r, V] block is row r
+    width = max(heads) * blk
+    stage = torch.empty((world, width), dtype=torch.bfloat16, device="cuda")
+
+    def gla_gathered():
+        gla_local()
+        row = o_l.reshape(1, -1)
+        if row.shape[1] < width:  # unequal head counts: pad this rank's block
+            row = torch.nn.functional.pad(row, (0, width - row.shape[1]))
+        shard.all_gather_rows(row, [1] * world, stage)
+
+    c2 = timed(gla_local, steps, warmup, world)
+    g2 = timed(gla_gathered, steps, warmup, world)
+    err = None
+    if rank == 0:
+        full = ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], None, 128 ** -0.5, 64, g=inp["g"],
+                                 h0=inp["h0"], output_final_state=True).o
+        worst = 0.0
+        for r, hrange in enumerate(shard.gla_head_partition(gcfg.H, world)):
+            got = stage[r, : gcfg.B * gcfg.T * len(hrange) * gcfg.V].view(
+                gcfg.B, gcfg.T, len(hrange), gcfg.V).float()
+            want = full[:, :, hrange.start:hrange.stop].float()
+            worst = max(worst, float((got - want).norm() / want.norm()))
+        err = worst
+        del full
+    if ops.device_status() != 0:
+        raise SystemExit("device error word set after the sharded GLA")
+    res["gla"] = {"workload": "gla_b1_t32768", "split": "heads", "heads_per_rank": heads,
+                  "compute_ms": c2, "with_gather_ms": g2,
+                  "tokens_per_s_compute": gcfg.B * gcfg.T / (c2 * 1e-3),
+                  "tokens_per_s_with_gather": gcfg.B * gcfg.T / (g2 * 1e-3),
+                  "gathered_layout": "[world, B, T, H/world, V] head blocks",
+                  "rel_err_vs_single_gpu": err, "scaling": "strong"}
+    del inp, q, k, v, g, h0, o_l, ht_l, stage
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_profile(args):
@@ -631,6 +744,8 @@ def main(argv=None):
     ap.add_argument("--workload", default=HEADLINE)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-sharded", action="store_true",
+                    help="N > 1: skip the strong-scaling rows (one workload split across ranks)")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-rows", type=int, default=8192,

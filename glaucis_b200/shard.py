@@ -1,0 +1,99 @@
+"""Multi-GPU partitioning of the two workloads, one process per GPU.
+
+Grouped matmul (by expert group): the rows of the ragged group list are cut
+into `world` contiguous ranges at 128-row boundaries, balanced by row count; a
+cut may fall inside a group, whose expert weights then live on both ranks.
+Rank r multiplies its rows by its experts' weights (a smaller ragged problem
+with its own group sizes) and the output rows are assembled on every rank by
+one all-gather of equal (padded) slabs.  Each output element is computed in
+the same K-block order as on one GPU, so the gathered output equals the
+single-GPU one bit for bit.
+
+Chunked GLA (by head): heads are cut into contiguous ranges; each rank runs
+the forward on its heads (its own [B, T, H_r, K] tensors) and the outputs are
+gathered head-major ([world, B, T, H_r, V]).
+
+No reference counterpart (the reference evaluates on one TPU slice); the
+partitioning follows the planned sharding of the grouped matmul by expert
+group with an output all-gather and of GLA by batch x head.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List
+
+import numpy as np
+import torch
+
+TILE = 128
+
+
+@dataclass
+class GmmShard:
+    r0: int             # first global row of this rank
+    r1: int             # one past its last row
+    g0: int             # first group touching [r0, r1)
+    g1: int             # one past the last group touching it
+    sizes: np.ndarray   # int32 [g1 - g0]: this rank's rows of each of those groups
+
+    @property
+    def rows(self) -> int:
+        return self.r1 - self.r0
+
+
+def gmm_partition(group_sizes, world: int, tile: int = TILE) -> List[GmmShard]:
+    """Contiguous row ranges, one per rank, cut at multiples of `tile` rows
+    nearest to equal shares of the assigned rows (sum of group_sizes)."""
+    sizes = np.asarray(group_sizes, dtype=np.int64)
+    if (sizes < 0).any():
+        raise ValueError("group sizes must be non-negative")
+    off = np.concatenate([[0], np.cumsum(sizes)])
+    total = int(off[-1])
+    cuts = [0]
+    for k in range(1, world):
+        c = int(round(total * k / world / tile)) * tile
+        cuts.append(min(max(c, cuts[-1]), total))
+    cuts.append(total)
+    shards = []
+    for r in range(world):
+        r0, r1 = cuts[r], cuts[r + 1]
+        if r1 <= r0:
+            shards.append(GmmShard(r0, r0, 0, 0, np.zeros(0, np.int32)))
+            continue
+        g0 = int(np.searchsorted(off, r0, side="right") - 1)
+        g1 = int(np.searchsorted(off, r1, side="left"))
+        loc = [max(0, min(int(off[g + 1]), r1) - max(int(off[g]), r0)) for g in range(g0, g1)]
+        shards.append(GmmShard(r0, r1, g0, g1, np.asarray(loc, np.int32)))
+    return shards
+
+
+def gla_head_partition(H: int, world: int) -> List[range]:
+    """Contiguous head ranges, sizes differing by at most one."""
+    return [range(H * r // world, H * (r + 1) // world) for r in range(world)]
+
+
+def all_gather_rows(local: torch.Tensor, counts: List[int], out: torch.Tensor) -> torch.Tensor:
+    """Assembles `out` [sum(counts), ...] from every rank's `local`
+    [counts[rank], ...] (rank order = row order).  Equal counts gather
+    straight into `out`; unequal ones through slabs padded to the largest."""
+    import torch.distributed as dist
+    world = dist.get_world_size()
+    width = max(counts)
+    nccl = dist.get_backend() == "nccl"
+    if all(c == width for c in counts) and nccl:
+        dist.all_gather_into_tensor(out, local.contiguous())
+        return out
+    pad = local.new_zeros((width,) + tuple(local.shape[1:]))
+    pad[: local.shape[0]] = local
+    if nccl:
+        slabs = local.new_empty((world * width,) + tuple(local.shape[1:]))
+        dist.all_gather_into_tensor(slabs, pad)
+        parts = list(slabs.split(width))
+    else:
+        parts = [torch.empty_like(pad) for _ in range(world)]
+        dist.all_gather(parts, pad)
+    r = 0
+    for k, c in enumerate(counts):
+        out[r:r + c] = parts[k][:c]
+        r += c
+    return out
