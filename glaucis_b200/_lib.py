@@ -38,6 +38,12 @@ SIGNATURES = {
     "gl_chunk_gla_bwd_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I64, _I64]),
     "gl_chunk_gla_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64,
                               _I64, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P]),
+    "gl_gmm_fp8_fwd_scatter": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I, _I64, _I,
+                                    _P, _P]),
+    "gl_ipc_alloc": (_I, [ctypes.c_size_t, _P, _P]),
+    "gl_ipc_open": (_I, [_P, _P]),
+    "gl_ipc_close": (_I, [_P]),
+    "gl_ipc_free": (_I, [_P]),
     "gl_gmm_fp8_act_fwd_noalloc": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _P]),
     "gl_quant_col_128x1": (_I, [_P, _I64, _I64, _P, _P, _P, _P]),
     "gl_gmm_fp8_dlhs": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _P]),

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <set>
 #include <string>
@@ -28,6 +29,10 @@ int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float
                         int64_t H, int64_t K, int64_t V, void* o, float* ht, void* h_out, void* ws,
                         size_t ws_bytes, int* err, cudaStream_t st, int num_sms, const char** why);
 size_t gl_chunk_gla_ws_bytes(int64_t B, int64_t T, int64_t H, int num_sms);
+int gl_launch_gmm_fp8_multi(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
+                            const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                            void* const* outs, int n_outs, int64_t row_off, int out_f32, int* err,
+                            cudaStream_t st, int num_sms, const char** why);
 int gl_launch_chunk_gla_dh(const void* q, const void* dout, const float* g, const float* g_gamma,
                            const float* dht, float scale, int64_t B, int64_t T, int64_t H,
                            void* e_out, float* dh0, void* ws, size_t ws_bytes, int* err,
@@ -268,6 +273,85 @@ int gl_gmm_fp8_fwd(const void* a_q, const float* a_s, const void* b_q, const flo
                                    static_cast<cudaStream_t>(stream), d->num_sms, &why);
   if (rc == -1) return fail(GL_EINVAL, std::string("gl_gmm_fp8_fwd: ") + why);
   if (rc != 0) return fail(GL_ELAUNCH, std::string("gl_gmm_fp8_fwd: ") + why);
+  return GL_OK;
+}
+
+int gl_gmm_fp8_fwd_scatter(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
+                           const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                           void* const* outs, int n_outs, int64_t row_offset, int out_dtype,
+                           int* err_word, void* stream) {
+  const char* f = "gl_gmm_fp8_fwd_scatter";
+  if (!a_q || !a_s || !b_q || !b_s || !group_sizes || !outs)
+    return fail(GL_EINVAL, std::string(f) + ": null pointer");
+  if (n_outs < 1 || n_outs > GL_MAX_SCATTER_OUTS)
+    return fail(GL_EINVAL, std::string(f) + ": need 1 <= n_outs <= GL_MAX_SCATTER_OUTS");
+  for (int i = 0; i < n_outs; ++i)
+    if (!outs[i] || !aligned16(outs[i]))
+      return fail(GL_EINVAL, std::string(f) + ": every output must be a 16-byte aligned pointer");
+  if (row_offset < 0) return fail(GL_EINVAL, std::string(f) + ": row_offset must be >= 0");
+  if (G < 1 || G > 1024) return fail(GL_EINVAL, std::string(f) + ": need 1 <= G <= 1024");
+  if (M < 0 || K <= 0 || N <= 0 || K % 128 != 0 || N % 128 != 0)
+    return fail(GL_EINVAL, std::string(f) + ": need K, N positive multiples of 128");
+  if (M > (int64_t(1) << 31) - 256 || G * K > (int64_t(1) << 31) - 256)
+    return fail(GL_EINVAL, std::string(f) + ": M and G*K must fit in 31 bits");
+  if (out_dtype != GL_OUT_BF16 && out_dtype != GL_OUT_F32)
+    return fail(GL_EINVAL, std::string(f) + ": out_dtype must be GL_OUT_BF16 or GL_OUT_F32");
+  if (!aligned16(a_q) || !aligned16(b_q))
+    return fail(GL_EINVAL, std::string(f) + ": a_q and b_q must be 16-byte aligned");
+  if (M == 0) return GL_OK;
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  const char* why = "";
+  const int rc = gl_launch_gmm_fp8_multi(a_q, a_s, b_q, b_s, group_sizes, G, M, K, N, outs, n_outs,
+                                         row_offset, out_dtype == GL_OUT_F32,
+                                         err_word ? err_word : d->err,
+                                         static_cast<cudaStream_t>(stream), d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string(f) + ": " + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string(f) + ": " + why);
+  return GL_OK;
+}
+
+// Cross-process peer buffers (CUDA IPC: unicast peer mappings, no multicast).
+int gl_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return fail(GL_EINVAL, "gl_ipc_alloc: null pointer or zero size");
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("gl_ipc_alloc: cudaMalloc: ") + cudaGetErrorString(e));
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, *ptr);
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return fail(GL_ELAUNCH, std::string("gl_ipc_alloc: cudaIpcGetMemHandle: ") + cudaGetErrorString(e));
+  }
+  static_assert(sizeof(h) == GL_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  return GL_OK;
+}
+
+int gl_ipc_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(GL_EINVAL, "gl_ipc_open: null pointer");
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("gl_ipc_open: ") + cudaGetErrorString(e));
+  return GL_OK;
+}
+
+int gl_ipc_close(void* ptr) {
+  if (!ptr) return GL_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("gl_ipc_close: ") + cudaGetErrorString(e));
+  return GL_OK;
+}
+
+int gl_ipc_free(void* ptr) {
+  if (!ptr) return GL_OK;
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return fail(GL_ELAUNCH, std::string("gl_ipc_free: ") + cudaGetErrorString(e));
   return GL_OK;
 }
 

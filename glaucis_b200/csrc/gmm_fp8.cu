@@ -66,6 +66,8 @@ struct Cfg {
   static_assert(2 * STAGES + 2 * NBUF + 1 <= 32, "barrier area");
 };
 
+constexpr int MAX_OUTS = 8;
+
 struct Params {
   const float* a_s;
   const float* b_s;
@@ -74,6 +76,13 @@ struct Params {
   int* err;
   int G, M, K, N;
   int out_f32;
+  // Output copies (single-CTA kernel): row m of this call is stored as row
+  // row_off + m of every outs[0 .. n_outs-1] (device or peer-mapped buffers
+  // of at least row_off + M rows of N); outs[0] = out, n_outs = 1,
+  // row_off = 0 for a plain call.
+  void* outs[MAX_OUTS];
+  int n_outs;
+  int64_t row_off;
 };
 
 struct Tile {
@@ -345,19 +354,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (!ok) break;
       if (row_ok && col_ok) {
-        if (p.out_f32) {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + grow * N + ncol0);
+        const int64_t orow = p.row_off + grow;
+        for (int o = 0; o < p.n_outs; ++o) {
+          if (p.out_f32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.outs[o]) + orow * N + ncol0);
 #pragma unroll
-          for (int i = 0; i < EC / 4; ++i)
-            dst[i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
-        } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + grow * N + ncol0);
+            for (int i = 0; i < EC / 4; ++i)
+              dst[i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
+          } else {
+            uint4* dst =
+                reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.outs[o]) + orow * N + ncol0);
 #pragma unroll
-          for (int i = 0; i < EC / 8; ++i)
-            dst[i] = make_uint4(pack_bf16x2(acc[4 * i].x, acc[4 * i].y),
-                                pack_bf16x2(acc[4 * i + 1].x, acc[4 * i + 1].y),
-                                pack_bf16x2(acc[4 * i + 2].x, acc[4 * i + 2].y),
-                                pack_bf16x2(acc[4 * i + 3].x, acc[4 * i + 3].y));
+            for (int i = 0; i < EC / 8; ++i)
+              dst[i] = make_uint4(pack_bf16x2(acc[4 * i].x, acc[4 * i].y),
+                                  pack_bf16x2(acc[4 * i + 1].x, acc[4 * i + 1].y),
+                                  pack_bf16x2(acc[4 * i + 2].x, acc[4 * i + 2].y),
+                                  pack_bf16x2(acc[4 * i + 3].x, acc[4 * i + 3].y));
+          }
         }
       }
     }
@@ -1049,10 +1062,10 @@ static int launch_pair(const CUtensorMap& tm_a, const CUtensorMap& tm_b,
   return 0;
 }
 
-int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
-                      const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
-                      void* out, int out_f32, int* err, cudaStream_t st, int num_sms,
-                      const char** why) {
+int gl_launch_gmm_fp8_multi(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
+                            const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                            void* const* outs, int n_outs, int64_t row_off, int out_f32, int* err,
+                            cudaStream_t st, int num_sms, const char** why) {
   using namespace gl::gmm;
   CUtensorMap tm_a, tm_b;
   if (!gl_make_tmap_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, a_q, K, M, K, 128, 128,
@@ -1065,13 +1078,19 @@ int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const 
   p.a_s = a_s;
   p.b_s = b_s;
   p.group_sizes = group_sizes;
-  p.out = out;
+  p.out = outs[0];
   p.err = err;
   p.G = static_cast<int>(G);
   p.M = static_cast<int>(M);
   p.K = static_cast<int>(K);
   p.N = static_cast<int>(N);
   p.out_f32 = out_f32;
+  for (int o = 0; o < MAX_OUTS; ++o) p.outs[o] = o < n_outs ? outs[o] : nullptr;
+  p.n_outs = n_outs;
+  p.row_off = row_off;
+  // several outputs or a row offset: the single-CTA kernel
+  if (n_outs > 1 || row_off != 0)
+    return launch_bn<256, false>(tm_a, tm_b, p, G, M, N, st, num_sms, why);
   // Variant: GLAUCIS_GMM_VARIANT=pair|256|128 overrides the default.
   int variant = 256;
   if (const char* e = std::getenv("GLAUCIS_GMM_VARIANT")) {
@@ -1081,6 +1100,15 @@ int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const 
   if (variant == 2) return launch_pair(tm_a, tm_b, p, G, M, N, st, num_sms, why);
   return variant == 256 ? launch_bn<256, false>(tm_a, tm_b, p, G, M, N, st, num_sms, why)
                         : launch_bn<128, false>(tm_a, tm_b, p, G, M, N, st, num_sms, why);
+}
+
+int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
+                      const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                      void* out, int out_f32, int* err, cudaStream_t st, int num_sms,
+                      const char** why) {
+  void* outs[1] = {out};
+  return gl_launch_gmm_fp8_multi(a_q, a_s, b_q, b_s, group_sizes, G, M, K, N, outs, 1, 0, out_f32,
+                                 err, st, num_sms, why);
 }
 
 // Backward dlhs = dout x rhs^T per group (tokamax gmm with transpose_rhs=True):
@@ -1112,6 +1140,9 @@ int gl_launch_gmm_fp8_dlhs(const void* a_q, const float* a_s, const void* b_q, c
   p.K = static_cast<int>(K);
   p.N = static_cast<int>(N);
   p.out_f32 = out_f32;
+  for (int o = 0; o < MAX_OUTS; ++o) p.outs[o] = o == 0 ? out : nullptr;
+  p.n_outs = 1;
+  p.row_off = 0;
   return launch_bn<256, true>(tm_a, tm_b, p, G, M, N, st, num_sms, why);
 }
 

@@ -152,6 +152,35 @@ def gmm_fp8_blockwise(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.T
 # ---------------------------------------------------------------------------
 # Grouped matmul backward (KE/examples/kernels/gmm_fp8_blockwise.py:123-169)
 # ---------------------------------------------------------------------------
+def gmm_fp8_fwd_scatter(a_q: torch.Tensor, a_s: torch.Tensor, b_q: torch.Tensor, b_s: torch.Tensor,
+                        group_sizes: torch.Tensor, outs, row_offset: int,
+                        out_dtype: torch.dtype = torch.bfloat16) -> None:
+    """gmm_fp8_fwd whose output rows go to row `row_offset` + m of every
+    buffer in `outs` (tensors on this device, or integer device addresses of
+    peer-mapped buffers such as symmetric-memory peers), each holding at
+    least row_offset + M rows of N elements of `out_dtype`.  Used to assemble
+    an expert-sharded output on every rank inside the matmul's epilogue; the
+    caller synchronises the ranks after it."""
+    _need_cuda(a_q, a_s, b_q, b_s, group_sizes)
+    M, K = a_q.shape
+    G, K2, N = b_q.shape
+    if K2 != K:
+        raise ValueError(f"K mismatch: a {K} vs b {K2}")
+    ptrs = [o.data_ptr() if isinstance(o, torch.Tensor) else int(o) for o in outs]
+    for o in outs:
+        if isinstance(o, torch.Tensor) and (o.dtype != out_dtype or o.dim() != 2 or o.shape[1] != N
+                                            or o.shape[0] < row_offset + M or not o.is_contiguous()):
+            raise ValueError(f"each output must be a contiguous {out_dtype} [>= row_offset + M, N] tensor")
+    import ctypes
+    arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    code = _lib.GL_OUT_F32 if out_dtype == torch.float32 else _lib.GL_OUT_BF16
+    _lib.check(_lib.load().gl_gmm_fp8_fwd_scatter(a_q.data_ptr(), a_s.data_ptr(), b_q.data_ptr(),
+                                                  b_s.data_ptr(), group_sizes.data_ptr(), G, M, K, N,
+                                                  ctypes.cast(arr, ctypes.c_void_p), len(ptrs),
+                                                  int(row_offset), code, None, _stream()),
+               "gl_gmm_fp8_fwd_scatter")
+
+
 def quant_col_128x1(x: torch.Tensor, q: Optional[torch.Tensor] = None,
                     s: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """bf16 [M, C] (M, C multiples of 128) -> (e4m3 [M, C], fp32 scales

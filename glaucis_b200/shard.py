@@ -4,10 +4,14 @@ Grouped matmul (by expert group): the rows of the ragged group list are cut
 into `world` contiguous ranges at 128-row boundaries, balanced by row count; a
 cut may fall inside a group, whose expert weights then live on both ranks.
 Rank r multiplies its rows by its experts' weights (a smaller ragged problem
-with its own group sizes) and the output rows are assembled on every rank by
-one all-gather of equal (padded) slabs.  Each output element is computed in
-the same K-block order as on one GPU, so the gathered output equals the
-single-GPU one bit for bit.
+with its own group sizes) and the output rows are assembled on every rank
+either by one NCCL all-gather of equal (padded) slabs after the matmul
+(`all_gather_rows`), or overlapped with it: the rows are computed in chunks
+straight into IPC-shared output buffers (`PeerBuffers`) and every finished
+chunk, a contiguous block of rows, is copied into each peer's buffer by the
+copy engines over NVLink while the next chunk is computed.  Each output
+element is computed in the same K-block order as on one GPU, so the gathered
+output equals the single-GPU one bit for bit.
 
 Chunked GLA (by head): heads are cut into contiguous ranges; each rank runs
 the forward on its heads (its own [B, T, H_r, K] tensors) and the outputs are
@@ -97,3 +101,63 @@ def all_gather_rows(local: torch.Tensor, counts: List[int], out: torch.Tensor) -
         out[r:r + c] = parts[k][:c]
         r += c
     return out
+
+
+class _CudaArray:
+    """A raw device allocation seen through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3, "strides": None}
+
+
+def tensor_at(ptr: int, shape) -> torch.Tensor:
+    """A bf16 tensor over device memory at `ptr` (own or peer-mapped), shape `shape`."""
+    return torch.as_tensor(_CudaArray(ptr, shape, "<i2"), device="cuda").view(torch.bfloat16)
+
+
+class PeerBuffers:
+    """One [rows, N] bf16 buffer per rank, every rank's buffer mapped into
+    every process (CUDA IPC over NVLink, unicast; no multicast object), for
+    peer copies or gl_gmm_fp8_fwd_scatter.  `ptrs[r]` is rank r's buffer as seen from this
+    process; `local` is this rank's buffer as a tensor.  Collective: every
+    rank constructs and closes it together."""
+
+    def __init__(self, rows: int, cols: int):
+        import ctypes
+        import torch.distributed as dist
+        from . import _lib
+        self._lib = _lib.load()
+        rank, world = dist.get_rank(), dist.get_world_size()
+        nbytes = rows * cols * 2
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        _lib.check(self._lib.gl_ipc_alloc(nbytes, ctypes.byref(ptr), handle), "gl_ipc_alloc")
+        self._own = ptr.value
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle))
+        self.ptrs, self._opened = [], []
+        for r, hb in enumerate(handles):
+            if r == rank:
+                self.ptrs.append(self._own)
+                continue
+            peer = ctypes.c_void_p()
+            _lib.check(self._lib.gl_ipc_open((ctypes.c_ubyte * 64).from_buffer_copy(hb),
+                                             ctypes.byref(peer)), "gl_ipc_open")
+            self.ptrs.append(peer.value)
+            self._opened.append(peer.value)
+        self.local = tensor_at(self._own, (rows, cols))
+
+    def close(self) -> None:
+        """Unmaps the peers and frees this rank's buffer (after a barrier, so
+        no rank still writes into it)."""
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank writes any more
+        for p in self._opened:
+            self._lib.gl_ipc_close(p)
+        self._opened = []
+        self.local = None
+        dist.barrier()  # every rank has unmapped this rank's buffer
+        self._lib.gl_ipc_free(self._own)
+        self._own = None

@@ -95,6 +95,40 @@ int gl_gmm_fp8_fwd(const void* a_q, const float* a_s, const void* b_q,
                    int64_t M, int64_t K, int64_t N, void* out, int out_dtype,
                    int* err_word, void* stream);
 
+/* Largest n_outs of gl_gmm_fp8_fwd_scatter. */
+#define GL_MAX_SCATTER_OUTS 8
+
+/*
+ * gl_gmm_fp8_fwd with its output rows stored into several buffers: row m of
+ * this call is written as row row_offset + m of each of outs[0 .. n_outs-1]
+ * (each at least row_offset + M rows of N elements of out_dtype, 16-byte
+ * aligned).  The buffers may be other GPUs' memory mapped into this process
+ * (CUDA IPC / VMM peer mappings, e.g. symmetric memory over NVLink): the
+ * kernel only stores to them, so a grouped matmul sharded by expert group
+ * across ranks assembles the full output on every rank inside its epilogue,
+ * overlapped with the MMAs, instead of an all-gather after it.  The caller
+ * orders the readers after the kernels of all ranks (a barrier).  Rows past
+ * sum(group_sizes) are not written.  No counterpart in the reference (its
+ * sharded output would be all-gathered by a collective).
+ */
+int gl_gmm_fp8_fwd_scatter(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
+                           const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
+                           void* const* outs, int n_outs, int64_t row_offset, int out_dtype,
+                           int* err_word, void* stream);
+
+/*
+ * Peer buffers for gl_gmm_fp8_fwd_scatter across processes (one per GPU):
+ * gl_ipc_alloc allocates device memory on the current device and returns its
+ * CUDA IPC handle (GL_IPC_HANDLE_BYTES bytes); another process opens it with
+ * gl_ipc_open (a unicast peer mapping over NVLink; no multicast object) and
+ * releases the mapping with gl_ipc_close; the owner frees with gl_ipc_free.
+ */
+#define GL_IPC_HANDLE_BYTES 64
+int gl_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int gl_ipc_open(const void* handle, void** ptr);
+int gl_ipc_close(void* ptr);
+int gl_ipc_free(void* ptr);
+
 /*
  * Chunked Gated Linear Attention forward (fixed-length sequences).
  *   q, k  bf16 [B, T, H, K];  v bf16 [B, T, H, V];  K == 128, V == 128

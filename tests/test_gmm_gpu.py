@@ -208,3 +208,21 @@ def test_gmm_full_size_sampled_rows(cuda, name):
         sel = np.nonzero(gid == g)[0]
         ref = O.gmm_group_rows(aq_rows[sel], as_rows[sel], _np_bytes(b_q[int(g)]), b_s_n[g])
         assert_close(got[sel], ref, RTOL, ATOL_FRAC, what=f"{name} group {g}")
+
+
+def test_gmm_scatter_writes_every_output_at_the_row_offset(cuda):
+    # the epilogue that assembles an expert-sharded output on every rank:
+    # here two local buffers stand in for the ranks' buffers
+    cfg = configs.GMMConfig("t", G=5, M=640, K=512, N=384, routing="uniform_one_empty")
+    lhs, rhs, gs = configs.make_gmm_inputs(cfg, device=cuda, seed=11)
+    a_q, a_s = ops.quant_act_1x128(lhs)
+    b_q, b_s = ops.quant_w_128x128(rhs)
+    want = ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs, out_dtype=torch.bfloat16)
+    off = 256
+    outs = [torch.full((off + cfg.M + 128, cfg.N), 7.0, dtype=torch.bfloat16, device=cuda) for _ in range(2)]
+    ops.gmm_fp8_fwd_scatter(a_q, a_s, b_q, b_s, gs, [outs[0], outs[1].data_ptr()], off)
+    assert ops.device_status() == 0
+    rows = int(gs.sum().item())
+    for o in outs:
+        assert torch.equal(o[off:off + rows], want[:rows])
+        assert bool((o[:off] == 7.0).all()) and bool((o[off + rows:] == 7.0).all())
