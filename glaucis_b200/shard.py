@@ -129,23 +129,36 @@ class PeerBuffers:
         from . import _lib
         self._lib = _lib.load()
         rank, world = dist.get_rank(), dist.get_world_size()
-        nbytes = rows * cols * 2
         ptr = ctypes.c_void_p()
         handle = (ctypes.c_ubyte * 64)()
-        _lib.check(self._lib.gl_ipc_alloc(nbytes, ctypes.byref(ptr), handle), "gl_ipc_alloc")
-        self._own = ptr.value
+        rc = self._lib.gl_ipc_alloc(rows * cols * 2, ctypes.byref(ptr), handle)
+        self._own = ptr.value if rc == 0 else None
+        # every rank learns every rank's outcome, so that all of them raise
+        # together (no rank is left waiting in a collective)
         handles = [None] * world
-        dist.all_gather_object(handles, bytes(handle))
+        dist.all_gather_object(handles, bytes(handle) if rc == 0 else None)
+        if any(h is None for h in handles):
+            if self._own:
+                self._lib.gl_ipc_free(self._own)
+            raise RuntimeError("peer buffer allocation failed on a rank")
         self.ptrs, self._opened = [], []
+        opened_all = True
         for r, hb in enumerate(handles):
             if r == rank:
                 self.ptrs.append(self._own)
                 continue
             peer = ctypes.c_void_p()
-            _lib.check(self._lib.gl_ipc_open((ctypes.c_ubyte * 64).from_buffer_copy(hb),
-                                             ctypes.byref(peer)), "gl_ipc_open")
+            if self._lib.gl_ipc_open((ctypes.c_ubyte * 64).from_buffer_copy(hb), ctypes.byref(peer)) != 0:
+                opened_all = False
+                break
             self.ptrs.append(peer.value)
             self._opened.append(peer.value)
+        flag = torch.tensor([1 if opened_all else 0], dtype=torch.int32, device="cuda")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if int(flag.item()) == 0:
+            self.local = None
+            self.close()
+            raise RuntimeError("peer buffer mapping failed on a rank")
         self.local = tensor_at(self._own, (rows, cols))
 
     def close(self) -> None:
