@@ -138,3 +138,28 @@ def test_autograd_function_and_template(cuda):
     loss = tmpl.optimized_compute(B=1, T=256, H=2, K=128, V=128, chunk_size=64)
     assert np.isfinite(float(loss))
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("name", ["gla_b8_t4096", "gla_b1_t32768"])
+def test_backward_full_size_sampled_heads(cuda, name):
+    # Full benchmark shapes on the GPU (both the plain and the sequence-split
+    # scan); the oracle recomputes three (b, h) sequences end to end.
+    cfg = configs.GLA_CONFIGS[name]
+    inp = configs.make_gla_inputs(cfg, device=cuda, seed=0)
+    gen = torch.Generator(device=cuda).manual_seed(12)
+    do = torch.randn(inp["v"].shape, generator=gen, device=cuda).to(torch.bfloat16)
+    scale = cfg.K ** -0.5
+    h = ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], scale, cfg.C, g=inp["g"],
+                          h0=inp["h0"], output_states=True).h
+    dq, dk, dv, dh0 = ops.chunk_gla_bwd(inp["q"], inp["k"], inp["v"], do, h, inp["g_gamma"], scale,
+                                        cfg.C, g=inp["g"], output_dh0=True)
+    assert ops.device_status() == 0
+    for (b, hh) in [(0, 0), (cfg.B - 1, cfg.H - 1), (cfg.B // 2, cfg.H // 3)]:
+        sl = lambda t: t[b:b + 1, :, hh:hh + 1].float().cpu().numpy()
+        h0 = None if inp["h0"] is None else inp["h0"][b:b + 1, hh:hh + 1].cpu().numpy()
+        gg = None if inp["g_gamma"] is None else inp["g_gamma"][hh:hh + 1].cpu().numpy()
+        ref = oracle_bwd(sl(inp["q"]), sl(inp["k"]), sl(inp["v"]), sl(do),
+                         g=None if inp["g"] is None else sl(inp["g"]), g_gamma=gg, h0=h0,
+                         scale=scale, chunk_size=cfg.C)
+        got = (sl(dq), sl(dk), sl(dv), dh0[b:b + 1, hh:hh + 1].cpu().numpy())
+        _check(got, ref, f"{name} (b={b}, h={hh})")

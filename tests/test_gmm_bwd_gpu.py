@@ -103,3 +103,42 @@ def test_autograd_matches_oracle_and_reference_bound(cuda):
     assert_close(dr, dr_ref, RTOL + 4e-3, ATOL_FRAC, what="drhs (autograd, bf16)")
     ul, ur = B.gmm_bwd_unquantised(f(lhs), f(rhs), sizes, f(grad))
     assert rel_fro(dl, ul) < 0.5 and rel_fro(dr, ur) < 0.5
+
+
+def test_backward_full_size_sampled(cuda):
+    # gmm_moe_up at full size on the GPU (dlhs and drhs); the oracle
+    # recomputes sampled rows of dlhs (first / last rows of several groups)
+    # and whole drhs slabs of sampled experts, each from just the rows it
+    # needs.
+    from glaucis_b200 import configs
+    cfg = configs.GMM_CONFIGS["gmm_moe_up"]
+    lhs, rhs, gs = configs.make_gmm_inputs(cfg, device=cuda, seed=0)
+    gen = torch.Generator(device=cuda).manual_seed(13)
+    grad = torch.randn((cfg.M, cfg.N), generator=gen, device=cuda).to(torch.bfloat16)
+    b_q, b_s = ops.quant_w_128x128(rhs)
+    del rhs
+    dq1, ds1 = ops.quant_act_1x128(grad)
+    dlhs = ops.gmm_fp8_dlhs(dq1, ds1, b_q, b_s, gs, out_dtype=torch.float32)
+    lq, ls = ops.quant_col_128x1(lhs)
+    dq2, ds2 = ops.quant_col_128x1(grad)
+    drhs = ops.tgmm_fp8(lq, ls, dq2, ds2, gs, out_dtype=torch.float32)
+    assert ops.device_status() == 0
+    sizes = gs.cpu().numpy()
+    off = np.concatenate([[0], np.cumsum(sizes)])
+    nonempty = [g for g in range(cfg.G) if sizes[g] > 0]
+    picks = [nonempty[0], nonempty[len(nonempty) // 2], nonempty[-1], int(np.argmax(sizes))]
+    for g in picks:
+        r0, r1 = int(off[g]), int(off[g + 1])
+        rows = sorted({r0, r0 + 1, (r0 + r1) // 2, r1 - 2, r1 - 1} & set(range(r0, r1)))
+        ref = B.gmm_dlhs(dq1.view(torch.uint8)[rows].cpu().numpy(), ds1[rows].cpu().numpy(),
+                         _bytes(b_q[g:g + 1]),
+                         b_s[g:g + 1].cpu().numpy(), [len(rows)])
+        assert_close(dlhs[rows].cpu().numpy(), ref, RTOL, ATOL_FRAC, what=f"dlhs rows of group {g}")
+        # drhs of group g from the 128-row blocks its rows touch
+        base = (r0 // 128) * 128
+        end = ((r1 + 127) // 128) * 128
+        sub = slice(base, end)
+        mb = slice(base // 128, end // 128)
+        ref_g = B.tgmm(_bytes(lq[sub]), ls[mb].cpu().numpy(), _bytes(dq2[sub]), ds2[mb].cpu().numpy(),
+                       [r0 - base, r1 - r0], groups=[1])[1]
+        assert_close(drhs[g].cpu().numpy(), ref_g, RTOL, ATOL_FRAC, what=f"drhs of group {g}")
