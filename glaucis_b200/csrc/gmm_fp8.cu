@@ -42,23 +42,34 @@ static_assert(128 * REG_CTRL + 256 * REG_EPI <= NUM_THREADS * 168, "register spl
 constexpr int MAX_G = 1024;
 constexpr int TMEM_COLS = 512;
 
-template <int BN>
+template <int BN, bool kStg = false>
 struct Cfg {
   static constexpr int B_BYTES = BK * BN;                      // 16 / 32 KB
-  static constexpr int STAGES = (6 * 32768) / (A_BYTES + B_BYTES) < 6
-                                    ? (6 * 32768) / (A_BYTES + B_BYTES) : 6;  // 4 / 6
+  // kStg (BN = 256): the bf16 output is staged through shared memory (one
+  // 8 KB slot per promotion warp: 32 rows x 128 columns as two 128B-swizzled
+  // 32x64 boxes) and TMA-stored, so the epilogue does not hold up the next
+  // tile's MMAs; the slots take the room of one operand stage.  Pays off
+  // for short reductions (few K blocks per tile, e.g. dlhs of an
+  // up-projection); long ones keep the fourth stage.
+  static constexpr bool STG = kStg && BN == 256;
+  static constexpr int STG_BYTES = STG ? 8 * 8192 : 0;
+  static constexpr int STAGES = STG ? 3
+                                    : ((6 * 32768) / (A_BYTES + B_BYTES) < 6
+                                           ? (6 * 32768) / (A_BYTES + B_BYTES) : 6);  // 3 / 6
   static constexpr int NBUF = TMEM_COLS / BN;                  // TMEM accumulators: 2 / 4
   static constexpr int EC = BN / 2;                            // columns per promotion thread
   static constexpr int NCH = EC / 32;                          // 32-column TMEM loads per K block
   static_assert(NCH % 2 == 0, "TMEM loads go in pairs");
   static constexpr uint32_t OFF_A = 0;
   static constexpr uint32_t OFF_B = OFF_A + STAGES * A_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_B + STAGES * B_BYTES;
+  static constexpr uint32_t OFF_STG = OFF_B + STAGES * B_BYTES;  // 1 KB aligned
+  static constexpr uint32_t OFF_BAR = OFF_STG + STG_BYTES;
   static constexpr uint32_t OFF_MISC = OFF_BAR + 256;
   static constexpr uint32_t OFF_ROWOFF = OFF_MISC + 128;
   static constexpr uint32_t OFF_TILEOFF = OFF_ROWOFF + (MAX_G + 1) * 4;
   static constexpr uint32_t SMEM_USED = OFF_TILEOFF + (MAX_G + 1) * 4;
   static constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;     // slack for 1 KB alignment
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
   // e4m3 x e4m3 -> f32, A K-major, B MN-major, M=128, N=BN.
   static constexpr uint32_t IDESC = idesc(1, 0, 0, 0, 1, BM, BN);
   // transposed weight (backward dlhs): B K-major (rows = output columns)
@@ -83,6 +94,10 @@ struct Params {
   void* outs[MAX_OUTS];
   int n_outs;
   int64_t row_off;
+  // 1: outs[0] is bf16, n_outs = 1, row_off = 0 and tm_o maps it (box 32
+  // rows x 64 columns, 128B swizzle): whole 32-row slices of a tile leave
+  // through shared memory and TMA stores (BN = 256 only).
+  int tma_out;
 };
 
 struct Tile {
@@ -152,11 +167,12 @@ __device__ __forceinline__ void build_group_table(const int32_t* group_sizes, in
   }
 }
 
-template <int BN, bool kTransB>
+template <int BN, bool kTransB, bool kStg>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gmm_fp8_fwd_kernel(const __grid_constant__ CUtensorMap tm_a,
-                       const __grid_constant__ CUtensorMap tm_b, const Params p) {
-  using CF = Cfg<BN>;
+                       const __grid_constant__ CUtensorMap tm_b,
+                       const __grid_constant__ CUtensorMap tm_o, const Params p) {
+  using CF = Cfg<BN, kStg>;
   constexpr int STAGES = CF::STAGES, NBUF = CF::NBUF, EC = CF::EC, NCH = CF::NCH;
   extern __shared__ uint8_t smem_raw[];
   // 1 KB-aligned base derived by pointer arithmetic on the shared array so
@@ -353,7 +369,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         promote(v[1], 16 * (NCH - 1));
       }
       if (!ok) break;
-      if (row_ok && col_ok) {
+      bool staged = false;
+      if constexpr (CF::STG) {
+        // The tile is decoded again (from shared memory) rather than kept
+        // live across the K loop, which leaves the promotion its registers.
+        const Tile te = decode_tile(t, tile_off, row_off, G, BN);
+        const int ecol0 = te.n0 + chalf * EC;
+        if (p.tma_out && ecol0 < N && te.rows - quad * 32 >= 32) {
+          // this warp's 32 rows x 128 columns -> its slot as two swizzled
+          // 32x64 boxes -> two TMA stores
+          uint8_t* slot = smem + CF::OFF_STG + ew * 8192;
+          const uint32_t srow = smem_u32(slot) + lane * 128;
+          if (lane == 0) bulk_wait_read<0>();  // the previous tile's stores have read the slot
+          __syncwarp();
+#pragma unroll
+          for (int b = 0; b < 2; ++b)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const int j = b * 32 + c * 4;  // acc[j] = columns 2j, 2j+1 of this thread's range
+              st_shared_v4(srow + b * 4096 + ((c ^ (lane & 7)) << 4),
+                           pack_bf16x2(acc[j].x, acc[j].y), pack_bf16x2(acc[j + 1].x, acc[j + 1].y),
+                           pack_bf16x2(acc[j + 2].x, acc[j + 2].y), pack_bf16x2(acc[j + 3].x, acc[j + 3].y));
+            }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tm_o, slot, ecol0, te.m0 + quad * 32);
+            tma_store_2d(&tm_o, slot + 4096, ecol0 + 64, te.m0 + quad * 32);
+            bulk_commit();
+          }
+          staged = true;
+        }
+      }
+      if (!staged && row_ok && col_ok) {
         const int64_t orow = p.row_off + grow;
         for (int o = 0; o < p.n_outs; ++o) {
           if (p.out_f32) {
@@ -373,6 +421,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
+    }
+    if constexpr (CF::STG) {
+      if (lane == 0) bulk_wait<0>();  // the TMA stores are done before the CTA exits
+      __syncwarp();
     }
   }
 
@@ -1005,25 +1057,56 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 #include "tmap.h"
 
-template <int BN, bool kTransB = false>
-static int launch_bn(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const gl::gmm::Params& p,
-                     int64_t G, int64_t M, int64_t N, cudaStream_t st, int num_sms,
+// Sets p.tma_out and tm_o when the output can leave through TMA stores (one
+// bf16 output, no row offset).
+static bool out_tmap(gl::gmm::Params& p, int64_t M, int64_t N, CUtensorMap* tm_o,
                      const char** why) {
+  p.tma_out = 0;
+  if (p.out_f32 || p.n_outs != 1 || p.row_off != 0) return true;
+  if (!gl_make_tmap_2d(tm_o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.outs[0], N, M, N, 64, 32,
+                       CU_TENSOR_MAP_SWIZZLE_128B, why))
+    return false;
+  p.tma_out = 1;
+  return true;
+}
+
+// Staged output (TMA stores) for at most this many K blocks per tile.
+constexpr int STG_MAX_KB = 24;
+
+template <int BN, bool kTransB, bool kStg>
+static int launch_cfg(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const CUtensorMap& tm_o,
+                      const gl::gmm::Params& p, int64_t G, int64_t M, int64_t N, cudaStream_t st,
+                      int num_sms, const char** why) {
   using namespace gl::gmm;
-  using CF = Cfg<BN>;
-  if (!gl_set_smem_attr(reinterpret_cast<const void*>(gmm_fp8_fwd_kernel<BN, kTransB>), 0,
-                        static_cast<int>(CF::SMEM_BYTES), why))
-    return -2;
+  using CF = Cfg<BN, kStg>;
+  const void* fn = reinterpret_cast<const void*>(gmm_fp8_fwd_kernel<BN, kTransB, kStg>);
+  if (!gl_set_smem_attr(fn, 0, static_cast<int>(CF::SMEM_BYTES), why)) return -2;
   const int64_t ntn = (N + BN - 1) / BN;
   const int64_t max_tiles = ((M + BM - 1) / BM + G) * ntn;
   const int grid = static_cast<int>(max_tiles < num_sms ? (max_tiles > 0 ? max_tiles : 1) : num_sms);
-  gmm_fp8_fwd_kernel<BN, kTransB><<<grid, NUM_THREADS, CF::SMEM_BYTES, st>>>(tm_a, tm_b, p);
+  gmm_fp8_fwd_kernel<BN, kTransB, kStg><<<grid, NUM_THREADS, CF::SMEM_BYTES, st>>>(tm_a, tm_b, tm_o, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     *why = cudaGetErrorString(e);
     return -2;
   }
   return 0;
+}
+
+template <int BN, bool kTransB = false>
+static int launch_bn(const CUtensorMap& tm_a, const CUtensorMap& tm_b, gl::gmm::Params p,
+                     int64_t G, int64_t M, int64_t N, cudaStream_t st, int num_sms,
+                     const char** why) {
+  CUtensorMap tm_o = tm_a;  // unused unless p.tma_out
+  p.tma_out = 0;
+  if constexpr (BN == 256) {
+    if (p.K / gl::gmm::BK <= STG_MAX_KB) {
+      if (!out_tmap(p, M, N, &tm_o, why)) return -1;
+      if (p.tma_out)
+        return launch_cfg<BN, kTransB, true>(tm_a, tm_b, tm_o, p, G, M, N, st, num_sms, why);
+    }
+  }
+  return launch_cfg<BN, kTransB, false>(tm_a, tm_b, tm_o, p, G, M, N, st, num_sms, why);
 }
 
 static int launch_pair(const CUtensorMap& tm_a, const CUtensorMap& tm_b,
