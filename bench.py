@@ -444,9 +444,30 @@ def run_b200(args):
 
         e_steps = max(1, min(args.steps, args.e2e_steps))
         e_ms = timed(e2e_step, e_steps, min(args.warmup, 2), world)
+        # the host link at the time of the run: plain pinned copies of the
+        # same activations and output (best of three, CUDA events), so the
+        # e2e figure can be read against the PCIe bound of this box
+        def copy_ms(dst, src):
+            best = float("inf")
+            for _ in range(3):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                dst.copy_(src, non_blocking=True)
+                e1.record()
+                e1.synchronize()
+                best = min(best, e0.elapsed_time(e1))
+            return best
+        h2d_ms = copy_ms(lhs, lhs_h)
+        out_d = torch.empty((cfg.M, cfg.N), dtype=torch.bfloat16, device="cuda")
+        d2h_ms = copy_ms(out_h, out_d)
+        del out_d
         e2e = {"value": world * flops / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": lhs_h.numel() * 2 + n_chunks * cfg.G * 4,
                "d2h_bytes_per_step": out_h.numel() * 2, "ms_per_step": e_ms,
+               "link": {"h2d_gbs": lhs_h.numel() * 2 / (h2d_ms * 1e-3) / 1e9,
+                        "d2h_gbs": out_h.numel() * 2 / (d2h_ms * 1e-3) / 1e9,
+                        "h2d_ms": h2d_ms, "d2h_ms": d2h_ms,
+                        "note": "one plain pinned copy each way of the step's activations / output"},
                "path": "gmm_fp8_blockwise_host(lhs, rhs, group_sizes): H2D lhs in 16 row chunks "
                        "overlapping quantise lhs (per chunk) + rhs and the grouped matmul, D2H bf16 out "
                        "per chunk"}
