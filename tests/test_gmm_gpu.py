@@ -226,3 +226,29 @@ def test_gmm_scatter_writes_every_output_at_the_row_offset(cuda):
     for o in outs:
         assert torch.equal(o[off:off + rows], want[:rows])
         assert bool((o[:off] == 7.0).all()) and bool((o[off + rows:] == 7.0).all())
+
+
+@pytest.mark.parametrize("K,N", [(384, 384), (3072, 256), (3200, 640)])
+def test_gmm_bf16_output_is_the_rounded_fp32_output(cuda, K, N):
+    # The bf16 output of a call is the fp32 accumulator rounded once, however
+    # it leaves the kernel: with short reductions (up to 24 K blocks) whole
+    # 32-row warp slices go through shared memory and TMA stores, partial
+    # slices (the last rows of a group) and fp32 outputs are stored directly.
+    # Both dtypes of the forward and of dlhs must agree bit for bit.
+    sizes = [0, 1, 31, 32, 33, 300, 0, 129, 127, 64, 96, 2]
+    G, M = len(sizes), 1100
+    g = torch.Generator().manual_seed(21)
+    lhs = torch.randn((M, K), generator=g).to(torch.bfloat16).to(cuda)
+    rhs = (torch.randn((G, K, N), generator=g) * 0.02).to(torch.bfloat16).to(cuda)
+    dout = torch.randn((M, N), generator=g).to(torch.bfloat16).to(cuda)
+    gs = torch.tensor(sizes, dtype=torch.int32, device=cuda)
+    a_q, a_s = ops.quant_act_1x128(lhs)
+    b_q, b_s = ops.quant_w_128x128(rhs)
+    d_q, d_s = ops.quant_act_1x128(dout)
+    total = sum(sizes)
+    for name, fn in (("forward", lambda dt: ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs, out_dtype=dt)),
+                     ("dlhs", lambda dt: ops.gmm_fp8_dlhs(d_q, d_s, b_q, b_s, gs, out_dtype=dt))):
+        o16 = fn(torch.bfloat16)
+        o32 = fn(torch.float32)
+        assert ops.device_status() == 0
+        assert torch.equal(o16[:total], o32[:total].to(torch.bfloat16)), name
