@@ -163,3 +163,18 @@ def test_backward_full_size_sampled_heads(cuda, name):
                          scale=scale, chunk_size=cfg.C)
         got = (sl(dq), sl(dk), sl(dv), dh0[b:b + 1, hh:hh + 1].cpu().numpy())
         _check(got, ref, f"{name} (b={b}, h={hh})")
+
+
+@pytest.mark.parametrize("seed", range(3))
+def test_backward_random_shapes(cuda, monkeypatch, seed):
+    # Seeded random problems for the backward: B x H from 1 to 12 sequences,
+    # 1 to 24 chunks, either gate, with or without h0 and dht, and a random
+    # sequence split of the reverse scan.
+    rng = np.random.default_rng(300 + seed)
+    cfg = configs.GLAConfig("rand", B=int(rng.integers(1, 3)), T=64 * int(rng.integers(1, 25)),
+                            H=int(rng.integers(1, 7)), h0_std=float(rng.choice([0.0, 0.1])),
+                            gate=str(rng.choice(["per_key", "gamma"])))
+    if rng.random() < 0.5:
+        monkeypatch.setenv("GLAUCIS_GLA_SEGMENTS", str(int(rng.integers(2, 5))))
+    got, ref = _run_bwd(cuda, cfg, seed=seed, with_dht=bool(rng.random() < 0.5))
+    _check(got, ref, f"random {cfg}")

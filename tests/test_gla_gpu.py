@@ -2,11 +2,17 @@
 through the C ABI.  The launcher reads GLAUCIS_GLA_VS at every call, so
 each test runs on both kernel instances.
 
-Tolerance (o and the final state): |gpu - ref| <= 2e-2 * |ref| + 2e-2 * rms(ref)
+Tolerance (o and the final state): |gpu - ref| <= 2e-2 * |ref| + 3e-2 * rms(ref)
 element-wise, plus a relative Frobenius error below 1e-2.  The kernel feeds
 the tensor cores bf16 operands (q e^G, k e^-G, tril(A), the state copy h_n)
 with fp32 accumulation and an fp32 recurrent state; the oracle is fp32
-throughout, as the reference's Precision.HIGHEST path.
+throughout.  The reference itself casts q e^G and the state h to bf16 before
+its output dot (KE/examples/kernels/chunk_gla.py:204-205); with slowly
+decaying per-head gates that alone moves single outputs up to ~3 % of
+rms(o) from the fp32 oracle beyond the relative term
+(tests/test_oracle_gla.py::test_reference_bf16_casts_stay_within_the_kernel_tolerance),
+so the absolute term is 3e-2 * rms.  The kernel's further bf16 rounding of
+tril(A) adds well under 1e-2 * rms.
 """
 import os
 
@@ -21,7 +27,7 @@ from tests.helpers import assert_close, rel_fro
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
-RTOL, ATOL_FRAC, FRO = 2e-2, 2e-2, 1e-2
+RTOL, ATOL_FRAC, FRO = 2e-2, 3e-2, 1e-2
 
 
 @pytest.fixture(autouse=True, params=["64", "128"])
@@ -133,3 +139,17 @@ def test_gla_full_size_sampled_heads(cuda, name):
                                         h0=h0, scale=cfg.K ** -0.5)
         _check(sl(res.o), res.ht[b:b + 1, h:h + 1].cpu().numpy(), ref_o, ref_ht,
                what=f"{name} (b={b}, h={h})")
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_gla_random_shapes(cuda, monkeypatch, seed):
+    # Seeded random problems: B x H from 1 to 24 sequences, 1 to 40 chunks,
+    # either gate, with or without h0, and a random sequence split (which
+    # the launcher also takes by itself when there are few heads).
+    rng = np.random.default_rng(200 + seed)
+    cfg = configs.GLAConfig("rand", B=int(rng.integers(1, 4)), T=64 * int(rng.integers(1, 41)),
+                            H=int(rng.integers(1, 9)), h0_std=float(rng.choice([0.0, 0.1])),
+                            gate=str(rng.choice(["per_key", "gamma"])))
+    if rng.random() < 0.5:
+        monkeypatch.setenv("GLAUCIS_GLA_SEGMENTS", str(int(rng.integers(2, 6))))
+    _check(*_run(cuda, cfg, seed=seed), f"random {cfg}")

@@ -252,3 +252,18 @@ def test_gmm_bf16_output_is_the_rounded_fp32_output(cuda, K, N):
         o32 = fn(torch.float32)
         assert ops.device_status() == 0
         assert torch.equal(o16[:total], o32[:total].to(torch.bfloat16)), name
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_gmm_random_ragged_shapes(cuda, seed):
+    # Seeded random problems: group counts from 1 to 40 with empty groups and
+    # groups of 1-300 rows, unassigned tail rows, K and N from 128 to 640,
+    # bf16 or fp32 output.
+    rng = np.random.default_rng(100 + seed)
+    G = int(rng.integers(1, 41))
+    sizes = [int(x) if rng.random() > 0.25 else 0 for x in rng.integers(1, 301, size=G)]
+    M = max(1, sum(sizes) + int(rng.integers(0, 200)))
+    K = 128 * int(rng.integers(1, 6))
+    N = 128 * int(rng.integers(1, 6))
+    out_dtype = torch.float32 if seed % 2 else torch.bfloat16
+    _gmm_case(cuda, G, M, K, N, sizes, seed=seed, out_dtype=out_dtype)
