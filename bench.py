@@ -787,6 +787,26 @@ def run_profile(args):
         def fn():
             ops.quant_act_1x128(x)
             ops.quant_w_128x128(w)
+    elif args.profile == "gmm_bwd":
+        # dlhs and tgmm on a 16-expert slice of the headline workload (the
+        # same routing, K and N; M = 4096 rows): about 0.9 GB resident
+        cfg = configs.GMMConfig("gmm_moe_up_g16", G=16, M=4096, K=7168, N=2048, routing="zipf_topk")
+        lhs, rhs, gs = configs.make_gmm_inputs(cfg, device="cuda", seed=args.seed)
+        b_q, b_s = ops.quant_w_128x128(rhs)
+        lq, ls = ops.quant_col_128x1(lhs)
+        del lhs, rhs
+        gen = torch.Generator(device="cuda").manual_seed(args.seed + 7)
+        grad = torch.randn((cfg.M, cfg.N), device="cuda", generator=gen).to(torch.bfloat16)
+        dq1, ds1 = ops.quant_act_1x128(grad)
+        dq2, ds2 = ops.quant_col_128x1(grad)
+        del grad
+        torch.cuda.empty_cache()
+        dlhs = torch.zeros((cfg.M, cfg.K), dtype=torch.bfloat16, device="cuda")
+        drhs = torch.empty((cfg.G, cfg.K, cfg.N), dtype=torch.bfloat16, device="cuda")
+
+        def fn():
+            ops.gmm_fp8_dlhs(dq1, ds1, b_q, b_s, gs, out=dlhs)
+            ops.tgmm_fp8(lq, ls, dq2, ds2, gs, out=drhs)
     elif args.profile == "gla_bwd":
         # the GLA backward (reverse scan + gradient kernel) on the GLA
         # workload: inputs, the states h, E and the gradients resident
@@ -828,7 +848,7 @@ def main(argv=None):
     ap.add_argument("--cpu-rows", type=int, default=8192,
                     help="rows of the headline workload in one CPU-baseline step")
     ap.add_argument("--cpu-gla-tokens", type=int, default=4096)
-    ap.add_argument("--profile", choices=["gmm", "gla", "gla_bwd", "quant"], default=None,
+    ap.add_argument("--profile", choices=["gmm", "gmm_bwd", "gla", "gla_bwd", "quant"], default=None,
                     help="run one kernel only, small footprint (for ncu captures)")
     ap.add_argument("--gla-workload", default=GLA_WORKLOAD)
     args = ap.parse_args(argv)
