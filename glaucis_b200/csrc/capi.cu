@@ -289,6 +289,8 @@ int gl_gmm_fp8_fwd_scatter(const void* a_q, const float* a_s, const void* b_q, c
     if (!outs[i] || !aligned16(outs[i]))
       return fail(GL_EINVAL, std::string(f) + ": every output must be a 16-byte aligned pointer");
   if (row_offset < 0) return fail(GL_EINVAL, std::string(f) + ": row_offset must be >= 0");
+  if (row_offset + M > (int64_t(1) << 31) - 256)
+    return fail(GL_EINVAL, std::string(f) + ": row_offset + M must fit in 31 bits");
   if (G < 1 || G > 1024) return fail(GL_EINVAL, std::string(f) + ": need 1 <= G <= 1024");
   if (M < 0 || K <= 0 || N <= 0 || K % 128 != 0 || N % 128 != 0)
     return fail(GL_EINVAL, std::string(f) + ": need K, N positive multiples of 128");

@@ -94,10 +94,16 @@ struct Params {
   void* outs[MAX_OUTS];
   int n_outs;
   int64_t row_off;
-  // 1: outs[0] is bf16, n_outs = 1, row_off = 0 and tm_o maps it (box 32
-  // rows x 64 columns, 128B swizzle): whole 32-row slices of a tile leave
-  // through shared memory and TMA stores (BN = 256 only).
+  // 1: the outputs are bf16 and tm_o.m[o] maps outs[o] (rows row_off + M,
+  // box 32 rows x 64 columns, 128B swizzle): whole 32-row slices of a tile
+  // leave through shared memory and TMA stores, one pair per output (own or
+  // peer-mapped memory; BN = 256 with the staged configuration only).
   int tma_out;
+};
+
+// Tensor maps of the outputs (kernel parameter).
+struct OutMaps {
+  CUtensorMap m[MAX_OUTS];
 };
 
 struct Tile {
@@ -171,7 +177,7 @@ template <int BN, bool kTransB, bool kStg>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gmm_fp8_fwd_kernel(const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_b,
-                       const __grid_constant__ CUtensorMap tm_o, const Params p) {
+                       const __grid_constant__ OutMaps tm_o, const Params p) {
   using CF = Cfg<BN, kStg>;
   constexpr int STAGES = CF::STAGES, NBUF = CF::NBUF, EC = CF::EC, NCH = CF::NCH;
   extern __shared__ uint8_t smem_raw[];
@@ -394,8 +400,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tm_o, slot, ecol0, te.m0 + quad * 32);
-            tma_store_2d(&tm_o, slot + 4096, ecol0 + 64, te.m0 + quad * 32);
+            const int y = static_cast<int>(p.row_off) + te.m0 + quad * 32;
+            for (int o = 0; o < p.n_outs; ++o) {
+              tma_store_2d(&tm_o.m[o], slot, ecol0, y);
+              tma_store_2d(&tm_o.m[o], slot + 4096, ecol0 + 64, y);
+            }
             bulk_commit();
           }
           staged = true;
@@ -1057,24 +1066,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 #include "tmap.h"
 
-// Sets p.tma_out and tm_o when the output can leave through TMA stores (one
-// bf16 output, no row offset).
-static bool out_tmap(gl::gmm::Params& p, int64_t M, int64_t N, CUtensorMap* tm_o,
-                     const char** why) {
+// Sets p.tma_out and the output maps when the outputs can leave through TMA
+// stores (bf16): one map per output, rows row_off + M.
+static bool out_tmaps(gl::gmm::Params& p, int64_t M, int64_t N, gl::gmm::OutMaps* om,
+                      const char** why) {
   p.tma_out = 0;
-  if (p.out_f32 || p.n_outs != 1 || p.row_off != 0) return true;
-  if (!gl_make_tmap_2d(tm_o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.outs[0], N, M, N, 64, 32,
-                       CU_TENSOR_MAP_SWIZZLE_128B, why))
-    return false;
+  if (p.out_f32) return true;
+  for (int o = 0; o < p.n_outs; ++o)
+    if (!gl_make_tmap_2d(&om->m[o], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.outs[o], N, p.row_off + M, N,
+                         64, 32, CU_TENSOR_MAP_SWIZZLE_128B, why))
+      return false;
   p.tma_out = 1;
   return true;
 }
 
-// Staged output (TMA stores) for at most this many K blocks per tile.
+// Staged output (TMA stores) for at most this many K blocks per tile, and
+// always for several outputs or a row offset (the rows go to every output,
+// own or peer-mapped, by TMA while the next tile is computed).
 constexpr int STG_MAX_KB = 24;
 
 template <int BN, bool kTransB, bool kStg>
-static int launch_cfg(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const CUtensorMap& tm_o,
+static int launch_cfg(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const gl::gmm::OutMaps& tm_o,
                       const gl::gmm::Params& p, int64_t G, int64_t M, int64_t N, cudaStream_t st,
                       int num_sms, const char** why) {
   using namespace gl::gmm;
@@ -1097,11 +1109,12 @@ template <int BN, bool kTransB = false>
 static int launch_bn(const CUtensorMap& tm_a, const CUtensorMap& tm_b, gl::gmm::Params p,
                      int64_t G, int64_t M, int64_t N, cudaStream_t st, int num_sms,
                      const char** why) {
-  CUtensorMap tm_o = tm_a;  // unused unless p.tma_out
+  gl::gmm::OutMaps tm_o;  // unused unless p.tma_out
+  for (int o = 0; o < gl::gmm::MAX_OUTS; ++o) tm_o.m[o] = tm_a;
   p.tma_out = 0;
   if constexpr (BN == 256) {
-    if (p.K / gl::gmm::BK <= STG_MAX_KB) {
-      if (!out_tmap(p, M, N, &tm_o, why)) return -1;
+    if (p.K / gl::gmm::BK <= STG_MAX_KB || p.n_outs > 1 || p.row_off != 0) {
+      if (!out_tmaps(p, M, N, &tm_o, why)) return -1;
       if (p.tma_out)
         return launch_cfg<BN, kTransB, true>(tm_a, tm_b, tm_o, p, G, M, N, st, num_sms, why);
     }

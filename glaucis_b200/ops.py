@@ -157,7 +157,7 @@ def gmm_fp8_fwd_scatter(a_q: torch.Tensor, a_s: torch.Tensor, b_q: torch.Tensor,
                         out_dtype: torch.dtype = torch.bfloat16) -> None:
     """gmm_fp8_fwd whose output rows go to row `row_offset` + m of every
     buffer in `outs` (tensors on this device, or integer device addresses of
-    peer-mapped buffers such as symmetric-memory peers), each holding at
+    peer-mapped buffers such as shard.PeerBuffers.ptrs), each holding at
     least row_offset + M rows of N elements of `out_dtype`.  Used to assemble
     an expert-sharded output on every rank inside the matmul's epilogue; the
     caller synchronises the ranks after it."""
