@@ -103,10 +103,12 @@ int gl_gmm_fp8_fwd(const void* a_q, const float* a_s, const void* b_q,
  * this call is written as row row_offset + m of each of outs[0 .. n_outs-1]
  * (each at least row_offset + M rows of N elements of out_dtype, 16-byte
  * aligned).  The buffers may be other GPUs' memory mapped into this process
- * (CUDA IPC / VMM peer mappings, e.g. symmetric memory over NVLink): the
- * kernel only stores to them, so a grouped matmul sharded by expert group
- * across ranks assembles the full output on every rank inside its epilogue,
- * overlapped with the MMAs, instead of an all-gather after it.  The caller
+ * (CUDA IPC peer mappings over NVLink, e.g. gl_ipc_open): the kernel only
+ * stores to them (bf16: TMA stores of each finished 32-row slice from shared
+ * memory; fp32 and a group's last rows: direct stores), so a grouped matmul
+ * sharded by expert group across ranks assembles the full output on every
+ * rank inside its epilogue, overlapped with the MMAs, instead of an
+ * all-gather after it.  The caller
  * orders the readers after the kernels of all ranks (a barrier).  Rows past
  * sum(group_sizes) are not written.  No counterpart in the reference (its
  * sharded output would be all-gathered by a collective).
