@@ -697,17 +697,16 @@ def run_sharded(args, rank, world, steps, warmup):
         dist.barrier()
 
         def gmm_scatter():
-            if me.rows:
-                ops.gmm_fp8_fwd_scatter(a_q, a_s, b_q, b_s, gs_l, peers.ptrs, me.r0)
-            dist.all_reduce(flag)
+            shard.gmm_fp8_fwd_gathered(a_q, a_s, b_q, b_s, me, peers, group_sizes=gs_l)
 
         x_ms = timed(gmm_scatter, steps, warmup, world)
         xsame = bool(torch.equal(single_cmp, peers.local)) if rank == 0 else None
         fused["epilogue_scatter"] = {
             "with_gather_ms": x_ms, "tflops_with_gather": flops / (x_ms * 1e-3) / 1e12,
             "matches_single_gpu": xsame,
-            "how": "gl_gmm_fp8_fwd_scatter: one kernel; each 32x128 output slice is staged in "
-                   "shared memory and TMA-stored to every rank's IPC-shared buffer"}
+            "how": "shard.gmm_fp8_fwd_gathered (gl_gmm_fp8_fwd_scatter): one kernel; each 32x128 "
+                   "output slice is staged in shared memory and TMA-stored to every rank's "
+                   "IPC-shared buffer"}
         del peer_views
         peers.close()
     except Exception as e:  # peer mappings unavailable: report, keep the NCCL rows

@@ -9,7 +9,9 @@ either by one NCCL all-gather of equal (padded) slabs after the matmul
 (`all_gather_rows`), or overlapped with it: the rows are computed in chunks
 straight into IPC-shared output buffers (`PeerBuffers`) and every finished
 chunk, a contiguous block of rows, is copied into each peer's buffer by the
-copy engines over NVLink while the next chunk is computed.  Each output
+copy engines over NVLink while the next chunk is computed, or inside the
+matmul itself (`gmm_fp8_fwd_gathered`): its epilogue TMA-stores every
+finished slice of rows into every rank's buffer.  Each output
 element is computed in the same K-block order as on one GPU, so the gathered
 output equals the single-GPU one bit for bit.
 
@@ -174,3 +176,33 @@ class PeerBuffers:
         dist.barrier()  # every rank has unmapped this rank's buffer
         self._lib.gl_ipc_free(self._own)
         self._own = None
+
+
+def gmm_fp8_fwd_gathered(a_q: torch.Tensor, a_s: torch.Tensor, b_q: torch.Tensor, b_s: torch.Tensor,
+                         me: GmmShard, peers: PeerBuffers,
+                         group_sizes: torch.Tensor = None) -> torch.Tensor:
+    """This rank's part of an expert-sharded grouped matmul, with the output
+    assembled on every rank by the matmul itself: the rows of `me` (a_q / a_s
+    are this rank's rows me.r0:me.r1, quantised 1x128; b_q / b_s the weights
+    of groups me.g0:me.g1) are multiplied and each finished 32-row slice is
+    TMA-stored from the epilogue into every rank's `peers` buffer at row
+    me.r0 + m, over NVLink, while the next tile is computed
+    (gl_gmm_fp8_fwd_scatter).  A stream-ordered all-reduce of one int then
+    orders the readers, so when the current stream reaches it every rank's
+    rows are in `peers.local`, which is returned ([sum of rows, N] bf16).
+    Collective: every rank calls it, in the same order.  Each output element
+    is computed in the single-GPU K-block order, so the assembled output
+    equals a one-GPU gl_gmm_fp8_fwd bit for bit.  `group_sizes` (int32, on
+    the device) may hold me.sizes already, saving a host-to-device copy."""
+    import torch.distributed as dist
+    from . import ops
+    if me.rows:
+        if a_q.shape[0] != me.rows or b_q.shape[0] != me.g1 - me.g0:
+            raise ValueError("a_q must hold this rank's rows and b_q its groups' weights")
+        gs = group_sizes
+        if gs is None:
+            gs = torch.from_numpy(np.ascontiguousarray(me.sizes, np.int32)).to(a_q.device)
+        ops.gmm_fp8_fwd_scatter(a_q, a_s, b_q, b_s, gs, peers.ptrs, me.r0)
+    flag = torch.zeros(1, dtype=torch.int32, device=peers.local.device)
+    dist.all_reduce(flag)
+    return peers.local
