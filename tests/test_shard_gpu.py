@@ -4,8 +4,6 @@ one-rank NCCL group on one GPU: the rank's rows go through the TMA-store
 scatter epilogue into its IPC-allocated buffer at the shard's row offset and
 must equal the plain one-GPU matmul bit for bit.  (With several GPUs the
 same call also stores into the peers' buffers; bench.py measures that.)"""
-import os
-
 import pytest
 import torch
 
@@ -19,9 +17,12 @@ def one_rank_group(cuda):
     import torch.distributed as dist
     if dist.is_initialized():
         pytest.skip("a process group already exists")
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    os.environ.setdefault("MASTER_PORT", "29561")
-    dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device(cuda))
+    import socket
+    with socket.socket() as sk:  # a free local port for the one-rank rendezvous
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                            device_id=torch.device(cuda))
     yield
     dist.destroy_process_group()
 
