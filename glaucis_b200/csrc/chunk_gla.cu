@@ -99,8 +99,8 @@ struct Params {
   int scale_apart;   // 1: scale <= 0 or not finite, applied as a separate multiply
   // Sequence split: chunks [seg*NT/nseg, (seg+1)*NT/nseg) form segment seg.
   // The state-only pass runs segments 0..nseg-2 from a zero state and writes
-  // each one's final state ws_h [B*H][nseg-1][K][V] and total decay
-  // ws_d [B*H][nseg-1][K]; the fold kernel turns record j into the initial
+  // each one's final state ws_h [nseg-1][B*H][K][V] and total decay
+  // ws_d [nseg-1][B*H][K]; the fold kernel turns record j into the initial
   // state of segment j+1 (h0 folded with segments 0..j), which the full pass
   // loads like h0.  nseg == 1: no split.
   // The reverse scan (DH) uses the same records for segments 1..nseg-1 (its
@@ -109,6 +109,14 @@ struct Params {
   // the gradient at the end of segment j.  A state-only grid covers segments
   // seg_base .. seg_base + seg_grid - 1.
   int nseg, seg_grid, seg_base;  // segments in total / per (b, h, V slice) in this grid / first
+  // Forward split with a short first segment (c_first > 0 chunks): segment 0
+  // runs the full pass from h0 while the state-only pass covers segments
+  // 1..nseg-2; segment 0's full pass writes its final state, as its ht, into
+  // record 0 (ht = ws_h, ht_seg = 0), which the fold passes through (zero
+  // start, decay 0); segments 1.. share the remaining chunks.  c_first = 0:
+  // equal segments as above.  Record of segment seg: seg - rec_base.
+  // ht_seg: the segment whose final state is written to ht.
+  int c_first, rec_base, ht_seg;
   int has_hout;  // FWD: write h_n (bf16, [B,NT,H,K,V]) through tm_h; DH: E_n (always)
   float* ws_h;
   float* ws_d;
@@ -186,8 +194,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int bh = rest / p.nsplit, vsl = rest % p.nsplit;
   const int b = bh / H, h = bh % H;
   const int v0 = vsl * VS;
-  const int c0 = static_cast<int>(static_cast<int64_t>(seg) * (T / C) / p.nseg);
-  const int c1 = static_cast<int>(static_cast<int64_t>(seg + 1) * (T / C) / p.nseg);
+  auto seg_chunk = [&](int j) -> int {  // first chunk of segment j (j = nseg: the end)
+    const int64_t nt = T / C;
+    if (p.c_first <= 0) return static_cast<int>(j * nt / p.nseg);
+    if (j == 0) return 0;
+    return p.c_first + static_cast<int>((j - 1) * (nt - p.c_first) / (p.nseg - 1));
+  };
+  const int c0 = seg_chunk(seg);
+  const int c1 = seg_chunk(seg + 1);
   const int NT = c1 - c0;  // chunks of this CTA
   const int tok0 = b * T + c0 * C;
   // Sequence position of the n-th chunk this CTA processes.
@@ -560,10 +574,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float* init = nullptr;
     if (kMode == MODE_FWD)
       init = seg == 0 ? (p.h0 ? p.h0 + bhi * KD * 128 : nullptr)
-                      : p.ws_h + (bhi * (p.nseg - 1) + seg - 1) * KD * 128;
+                      : p.ws_h + (static_cast<int64_t>(seg - 1) * p.B * H + bhi) * KD * 128;
     else if (kMode == MODE_DH)
       init = seg == p.nseg - 1 ? (p.h0 ? p.h0 + bhi * KD * 128 : nullptr)
-                               : p.ws_h + (bhi * (p.nseg - 1) + seg) * KD * 128;
+                               : p.ws_h + (static_cast<int64_t>(seg) * p.B * H + bhi) * KD * 128;
     if (init) {
       const float4* src = reinterpret_cast<const float4*>(init + static_cast<int64_t>(key) * 128 + v0);
 #pragma unroll
@@ -714,13 +728,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     if (st_issuer && p.has_hout) bulk_wait<0>();
     if (ok && (kMode == MODE_FWD_STATE || kMode == MODE_DH_STATE)) {
-      const int64_t rec = bhi * (p.nseg - 1) + seg - p.seg_base;
+      const int64_t rec = static_cast<int64_t>(seg - p.rec_base) * p.B * H + bhi;
       float4* dst = reinterpret_cast<float4*>(p.ws_h + (rec * KD + key) * 128 + v0);
 #pragma unroll
       for (int j = 0; j < VS / 4; ++j)
         dst[j] = make_float4(hreg[4 * j], hreg[4 * j + 1], hreg[4 * j + 2], hreg[4 * j + 3]);
       if (vsl == 0) p.ws_d[rec * KD + key] = dacc;
-    } else if (ok && p.ht && seg == (kMode == MODE_DH ? 0 : p.nseg - 1)) {
+    } else if (ok && p.ht && seg == p.ht_seg) {
       float4* dst = reinterpret_cast<float4*>(p.ht + (bhi * KD + key) * 128 + v0);
 #pragma unroll
       for (int j = 0; j < VS / 4; ++j)
@@ -754,7 +768,7 @@ __global__ void __launch_bounds__(256) gla_fold_kernel(const float* __restrict__
   float4 h = h0 ? reinterpret_cast<const float4*>(h0)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
   for (int i = 0; i < nseg - 1; ++i) {
     const int j = reverse ? nseg - 2 - i : i;
-    const int64_t rec = static_cast<int64_t>(bh) * (nseg - 1) + j;
+    const int64_t rec = static_cast<int64_t>(j) * BH + bh;
     const float d = ws_d[rec * KD + key];
     float4* slot = reinterpret_cast<float4*>(ws_h + (rec * KD + key) * 128) + c4;
     const float4 x = *slot;
@@ -768,6 +782,7 @@ __global__ void __launch_bounds__(256) gla_fold_kernel(const float* __restrict__
 
 #include <cmath>
 #include <cstdlib>
+#include <mutex>
 
 #include "tmap.h"
 
@@ -784,6 +799,62 @@ static int gla_segments(int64_t B, int64_t T, int64_t H, int num_sms) {
   int64_t n = num_sms / items;
   if (n > NT / 8) n = NT / 8;
   return static_cast<int>(n < 2 ? 1 : n);
+}
+
+// Forward sequence split (short first segment, see Params): the first phase
+// runs segment 0's full pass beside the state-only pass of segments
+// 1..nseg-2, the second the full pass of segments 1..nseg-1, each with
+// B*H*(nseg-1) CTAs, so nseg - 1 = #SMs / (B*H) puts one CTA on each SM in
+// both; every segment after the first keeps at least 8 chunks.
+static int gla_segments_fwd(int64_t B, int64_t T, int64_t H, int num_sms) {
+  const int64_t items = B * H, NT = T / 64;
+  if (const char* e = std::getenv("GLAUCIS_GLA_SEGMENTS")) {
+    const int64_t n = std::atoi(e);
+    return static_cast<int>(n < 1 ? 1 : (n > NT ? NT : n));
+  }
+  if (items * 2 > num_sms) return 1;
+  int64_t n = num_sms / items + 1;
+  if (n > NT / 8 + 1) n = NT / 8 + 1;
+  return static_cast<int>(n < 2 ? 1 : n);
+}
+
+// Chunks of segment 0 in the forward split: its full pass should take as
+// long as the state-only pass over one of the later segments, which costs
+// about 0.52 of a full pass per chunk (measured on gla_b1_t32768).
+static int gla_first_segment(int64_t NT, int nseg) {
+  const double r = 0.52;
+  int64_t c = static_cast<int64_t>(r * static_cast<double>(NT) / (nseg - 1 + r) + 0.5);
+  if (c < 1) c = 1;
+  if (c > NT - (nseg - 1)) c = NT - (nseg - 1);
+  return static_cast<int>(c);
+}
+
+// A second stream per device for the first phase of the forward split, and
+// the two events that fork it from and join it to the caller's stream.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+static std::mutex g_side_mu;
+static SideStream g_side[64];
+
+static int side_stream(SideStream** out, const char** why) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *why = "cudaGetDevice failed";
+    return -2;
+  }
+  SideStream& d = g_side[dev];
+  if (d.s == nullptr) {
+    if (cudaStreamCreateWithFlags(&d.s, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&d.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&d.join, cudaEventDisableTiming) != cudaSuccess) {
+      *why = "creating the side stream of the sequence split failed";
+      return -2;
+    }
+  }
+  *out = &d;
+  return 0;
 }
 
 // Workspace of a split launch: final state [B*H][nseg-1][128][128] and total
@@ -852,12 +923,69 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
     th = tk;  // unused
   }
   const int items = p.B * p.H * p.nsplit;
+  if (p.nseg > 1 && !rev && p.c_first > 0) {
+    // Phase 1: segment 0's full pass (from h0; its final state becomes
+    // record 0) on the caller's stream, beside the state-only pass of
+    // segments 1..nseg-2 on the side stream.  Then the fold and the full
+    // pass of segments 1..nseg-1.
+    gl::gla::Params pa = p;
+    pa.seg_base = 0;
+    pa.seg_grid = 1;
+    pa.ht = p.ws_h;  // record 0 = [B*H][K][V], the layout of ht
+    pa.ht_seg = 0;
+    pa.has_hout = sout != nullptr;
+    {
+      std::lock_guard<std::mutex> lk(g_side_mu);
+      SideStream* ss = nullptr;
+      if (p.nseg > 2) {
+        if (int rc = side_stream(&ss, why)) return rc;
+        if (cudaEventRecord(ss->fork, st) != cudaSuccess || cudaStreamWaitEvent(ss->s, ss->fork, 0) != cudaSuccess) {
+          *why = "forking the side stream failed";
+          return -2;
+        }
+        gl::gla::Params ps = p;
+        ps.seg_base = 1;
+        ps.seg_grid = p.nseg - 2;
+        ps.rec_base = 0;
+        ps.has_hout = 0;
+        if (int rc = launch_pass<VS, gl::gla::MODE_FWD_STATE>(tq, tk, tv, tg, th, ps, items * ps.seg_grid,
+                                                              ss->s, why))
+          return rc;
+      }
+      if (int rc = launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, pa, items, st, why)) return rc;
+      if (ss != nullptr &&
+          (cudaEventRecord(ss->join, ss->s) != cudaSuccess || cudaStreamWaitEvent(st, ss->join, 0) != cudaSuccess)) {
+        *why = "joining the side stream failed";
+        return -2;
+      }
+    }
+    // Record 0 already holds the true state after segment 0: fold from a
+    // zero start with its decay cleared, so it passes through unchanged.
+    if (cudaMemsetAsync(p.ws_d, 0, static_cast<size_t>(p.B) * p.H * 128 * sizeof(float), st) != cudaSuccess) {
+      *why = "clearing the first segment's decay record failed";
+      return -2;
+    }
+    const int64_t n4 = static_cast<int64_t>(p.B) * p.H * 128 * 32;
+    gl::gla::gla_fold_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, st>>>(
+        nullptr, p.ws_h, p.ws_d, p.B * p.H, p.nseg, 0);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      *why = cudaGetErrorString(e);
+      return -2;
+    }
+    p.seg_base = 1;
+    p.seg_grid = p.nseg - 1;
+    p.ht_seg = p.nseg - 1;
+    p.has_hout = sout != nullptr;
+    return launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, p, items * p.seg_grid, st, why);
+  }
   if (p.nseg > 1) {
     // State-only pass over segments 0 .. nseg-2 (reverse: 1 .. nseg-1), the
     // fold, then the full pass.
     gl::gla::Params p1 = p;
     p1.seg_grid = p.nseg - 1;
     p1.seg_base = rev ? 1 : 0;
+    p1.rec_base = p1.seg_base;
     p1.has_hout = 0;
     const int rc = rev ? launch_pass<VS, gl::gla::MODE_DH_STATE>(tq, tk, tv, tg, th, p1,
                                                                  items * p1.seg_grid, st, why)
@@ -875,13 +1003,16 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
   }
   p.seg_grid = p.nseg;
   p.seg_base = 0;
+  p.ht_seg = rev ? 0 : p.nseg - 1;
   p.has_hout = sout != nullptr;
   return rev ? launch_pass<VS, gl::gla::MODE_DH>(tq, tk, tv, tg, th, p, items * p.nseg, st, why)
              : launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, p, items * p.nseg, st, why);
 }
 
 size_t gl_chunk_gla_ws_bytes(int64_t B, int64_t T, int64_t H, int num_sms) {
-  return gla_ws_bytes(B, H, gla_segments(B, T, H, num_sms));
+  const size_t f = gla_ws_bytes(B, H, gla_segments_fwd(B, T, H, num_sms));
+  const size_t r = gla_ws_bytes(B, H, gla_segments(B, T, H, num_sms));
+  return f > r ? f : r;
 }
 
 // Shared set-up of the forward and the reverse scan: scale, segments, V split.
@@ -904,13 +1035,16 @@ static int gla_dispatch(const void* q, const void* kslot, const void* vslot, con
   p.H = static_cast<int>(H);
   p.has_g = g != nullptr;
   p.seg_base = 0;
+  p.rec_base = 0;
+  p.ht_seg = 0;
   p.has_hout = 0;
   // Few (batch, head) pairs: split the sequence into segments (full V width,
   // one CTA per SM) when the workspace allows it, else split V in two.
   // GLAUCIS_GLA_VS=64|128 and GLAUCIS_GLA_SEGMENTS=n override the choice.
-  int nseg = gla_segments(B, T, H, num_sms);
+  int nseg = rev ? gla_segments(B, T, H, num_sms) : gla_segments_fwd(B, T, H, num_sms);
   while (nseg > 1 && (ws == nullptr || gla_ws_bytes(B, H, nseg) > ws_bytes)) --nseg;
   p.nseg = nseg;
+  p.c_first = (!rev && nseg > 1) ? gla_first_segment(T / 64, nseg) : 0;
   p.seg_grid = nseg;
   if (nseg > 1) {
     const size_t rec = static_cast<size_t>(B * H) * static_cast<size_t>(nseg - 1);
