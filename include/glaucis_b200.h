@@ -160,10 +160,13 @@ int gl_chunk_gla_fwd(const void* q, const void* k, const void* v, const float* g
 /*
  * gl_chunk_gla_fwd with a caller-owned device workspace.  When B*H is small
  * against the SM count (few heads, long sequences) the sequence is split into
- * segments: a state-only pass computes each segment's final state from a
- * zero state and its total decay into the workspace, and the full pass starts
- * every segment from h0 folded with the preceding segments' records, so the
- * recurrence runs on one CTA per SM instead of one per (batch, head).
+ * segments.  The first, short segment runs its full pass from h0 beside a
+ * state-only pass that computes each middle segment's final state from a
+ * zero state, and its total decay, into the workspace; the full pass of the
+ * remaining segments then starts each of them from h0 folded with the
+ * preceding segments' records, so the recurrence runs on one CTA per SM
+ * instead of one per (batch, head).  The first phase forks a library-owned
+ * stream from `stream` and joins it back with events.
  * gl_chunk_gla_fwd_workspace_bytes gives the size the split wants on the
  * current device (0: no split for this shape); a smaller workspace gives
  * fewer segments, NULL / 0 none.  The workspace must be 256-byte aligned and
