@@ -952,12 +952,15 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
                                                               ss->s, why))
           return rc;
       }
-      if (int rc = launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, pa, items, st, why)) return rc;
+      const int rc_a = launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, pa, items, st, why);
+      // join even when that launch failed, so that nothing of this call runs
+      // on the side stream after the caller's stream has moved on
       if (ss != nullptr &&
           (cudaEventRecord(ss->join, ss->s) != cudaSuccess || cudaStreamWaitEvent(st, ss->join, 0) != cudaSuccess)) {
         *why = "joining the side stream failed";
         return -2;
       }
+      if (rc_a) return rc_a;
     }
     // Record 0 already holds the true state after segment 0: fold from a
     // zero start with its decay cleared, so it passes through unchanged.
