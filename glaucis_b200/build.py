@@ -19,7 +19,8 @@ INCLUDE = PKG.parent / "include"
 BUILD = PKG / "_build"
 LIB = PKG / "libglaucis_b200.so"
 
-SOURCES = ["capi.cu", "quant.cu", "gmm_fp8.cu", "chunk_gla.cu", "chunk_gla_bwd.cu", "noalloc.cu"]
+SOURCES = ["capi.cu", "quant.cu", "gmm_fp8.cu", "chunk_gla.cu", "chunk_gla_bwd.cu",
+           "gla_intermediates.cu", "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
               "--expt-relaxed-constexpr", "-Xptxas", "-v"]

@@ -41,6 +41,9 @@ int gl_launch_chunk_gla_grads(const void* q, const void* k, const void* v, const
                               const float* g, const float* g_gamma, const void* h, const void* e,
                               float scale, int64_t B, int64_t T, int64_t H, void* dq, void* dk,
                               void* dv, int* err, cudaStream_t st, int num_sms, const char** why);
+int gl_launch_gla_intermediates(const void* q, const void* k, const float* g, const float* g_gamma,
+                                float scale, int64_t B, int64_t T, int64_t H, float* g_cumsum,
+                                float* A, cudaStream_t st, const char** why);
 int gl_launch_quant_col(const void* x, int64_t M, int64_t C, void* q, float* s, int* err,
                         cudaStream_t st, int num_sms, const char** why);
 int gl_launch_gmm_fp8_dlhs(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
@@ -438,6 +441,33 @@ int gl_chunk_gla_fwd_states(const void* q, const void* k, const void* v, const f
                                      h_states, workspace, workspace ? workspace_bytes : 0,
                                      err_word ? err_word : d->err,
                                      static_cast<cudaStream_t>(stream), d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string(f) + ": " + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string(f) + ": " + why);
+  return GL_OK;
+}
+
+int gl_chunk_gla_fwd_intermediates(const void* q, const void* k, const float* g,
+                                   const float* g_gamma, float scale, int64_t B, int64_t T,
+                                   int64_t H, int64_t K, int64_t chunk_size, float* g_cumsum,
+                                   float* A, int* err_word, void* stream) {
+  const char* f = "gl_chunk_gla_fwd_intermediates";
+  (void)err_word;  // no device-side waits: nothing is ever written there
+  if (!q || !k) return fail(GL_EINVAL, std::string(f) + ": null pointer");
+  if (!g_cumsum && !A) return fail(GL_EINVAL, std::string(f) + ": neither g_cumsum nor A requested");
+  if ((g == nullptr) == (g_gamma == nullptr))
+    return fail(GL_EINVAL, std::string(f) + ": exactly one of g / g_gamma must be given");
+  if (K != 128) return fail(GL_EINVAL, std::string(f) + ": K must be 128");
+  if (chunk_size != 64) return fail(GL_EINVAL, std::string(f) + ": chunk_size must be 64");
+  if (B <= 0 || H <= 0 || T <= 0 || T % 64 != 0)
+    return fail(GL_EINVAL, std::string(f) + ": need B, H > 0 and T a positive multiple of 64");
+  if (B * T * H > (int64_t(1) << 31) - 1) return fail(GL_EINVAL, std::string(f) + ": B*T*H must fit in 31 bits");
+  if ((A && !aligned16(A)) || (g_cumsum && !aligned16(g_cumsum)))
+    return fail(GL_EINVAL, std::string(f) + ": outputs must be 16-byte aligned");
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  const char* why = "";
+  const int rc = gl_launch_gla_intermediates(q, k, g, g_gamma, scale, B, T, H, g_cumsum, A,
+                                             static_cast<cudaStream_t>(stream), &why);
   if (rc == -1) return fail(GL_EINVAL, std::string(f) + ": " + why);
   if (rc != 0) return fail(GL_ELAUNCH, std::string(f) + ": " + why);
   return GL_OK;

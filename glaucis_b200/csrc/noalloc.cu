@@ -17,6 +17,11 @@
 //     call's contents.  Calls whose GPU work overlaps (different streams,
 //     host threads or processes sharing a context) race on it; serialise
 //     them on one stream.
+//   * Device-side errors (invalid group_sizes, a wait that gave up) are
+//     reported only through a caller-owned err_word: with NULL they land in
+//     the scratch array's own word, which nothing reads back (the library
+//     word that gl_device_status(NULL) reads is allocated memory, so this
+//     entry point does not use it).
 //   * The first call on each device looks up the array's device address
 //     (cudaGetSymbolAddress, with that device current); make that first call
 //     before any stream capture.
@@ -97,11 +102,12 @@ extern "C" int gl_gmm_fp8_act_fwd_noalloc(const void* lhs, const void* b_q, cons
   if (M < 0 || K <= 0 || N <= 0 || K % 128 != 0 || N % 128 != 0)
     return gl_set_error_message(GL_EINVAL,
                                 "gl_gmm_fp8_act_fwd_noalloc: need K, N positive multiples of 128");
-  if (M * K > static_cast<int64_t>(GL_NOALLOC_MAX_ACT_ELEMS))
+  // division form: M * K itself may overflow for huge M
+  if (M > static_cast<int64_t>(GL_NOALLOC_MAX_ACT_ELEMS) / K)
     return gl_set_error_message(
         GL_EINVAL,
-        ("gl_gmm_fp8_act_fwd_noalloc: M*K = " + std::to_string(M * K) +
-         " exceeds the static scratch limit of " + std::to_string(GL_NOALLOC_MAX_ACT_ELEMS) +
+        ("gl_gmm_fp8_act_fwd_noalloc: M = " + std::to_string(M) + ", K = " + std::to_string(K) +
+         ": M*K exceeds the static scratch limit of " + std::to_string(GL_NOALLOC_MAX_ACT_ELEMS) +
          " activation elements; use gl_quant_act_1x128 + gl_gmm_fp8_fwd with caller buffers")
             .c_str());
   if (G * K > (int64_t(1) << 31) - 256)

@@ -405,14 +405,25 @@ def gmm_fp8_blockwise_host(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: to
 class GLAForward(tuple):
     """Result of chunk_gla_fwd, unpackable as the reference's
     (g_cumsum, A, h, o).  The fused kernel keeps g_cumsum and A on chip, so
-    those entries are None; h (the bf16 state before every chunk,
-    [B, T/64, H, K, V]) is returned when asked for with output_states=True,
-    else None; the final state is `.ht`."""
+    those entries are None unless asked for with output_intermediates=True
+    (then fp32 [B, T, H, K] and fp32 [B, T, H, 64], from a separate kernel);
+    h (the bf16 state before every chunk, [B, T/64, H, K, V]) is returned
+    when asked for with output_states=True, else None; the final state is
+    `.ht`."""
 
-    def __new__(cls, o: torch.Tensor, ht: Optional[torch.Tensor], h: Optional[torch.Tensor] = None):
-        self = tuple.__new__(cls, (None, None, h, o))
+    def __new__(cls, o: torch.Tensor, ht: Optional[torch.Tensor], h: Optional[torch.Tensor] = None,
+                g_cumsum: Optional[torch.Tensor] = None, A: Optional[torch.Tensor] = None):
+        self = tuple.__new__(cls, (g_cumsum, A, h, o))
         self.ht = ht
         return self
+
+    @property
+    def g_cumsum(self) -> Optional[torch.Tensor]:
+        return self[0]
+
+    @property
+    def A(self) -> Optional[torch.Tensor]:
+        return self[1]
 
     @property
     def o(self) -> torch.Tensor:
@@ -443,6 +454,7 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                   g_gamma: Optional[torch.Tensor], scale: float, chunk_size: int = 64, *,
                   g: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
                   output_final_state: bool = False, output_states: bool = False,
+                  output_intermediates: bool = False,
                   o: Optional[torch.Tensor] = None,
                   ht: Optional[torch.Tensor] = None,
                   h: Optional[torch.Tensor] = None) -> GLAForward:
@@ -452,7 +464,11 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     chunk-local cumsum taken in-kernel; semantics of
     KE/upstream/fused_chunk_simple_gla/common_chunk_h.py:330-334) is used.
     output_states=True also returns the per-chunk states h (bf16), the
-    residual of the backward.  o, ht and h may be given preallocated.
+    residual of the backward.  output_intermediates=True also returns
+    g_cumsum (fp32 [B, T, H, K]) and the unmasked intra-chunk A (fp32
+    [B, T, H, 64]) as the reference's first two outputs, computed by a
+    separate fp32 kernel (one more pass over q, k and g).  o, ht and h may
+    be given preallocated.
     """
     B, T, H, K, V = _gla_check(q, k, v, g_gamma, g, h0)
     if o is None:
@@ -477,7 +493,16 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                                            chunk_size, o.data_ptr(), _ptr(ht), _ptr(ws), ws_bytes,
                                            None, _stream()),
                    "gl_chunk_gla_fwd")
-    return GLAForward(o, ht if output_final_state else None, h)
+    g_cumsum = A = None
+    if output_intermediates:
+        g_cumsum = torch.empty((B, T, H, K), dtype=torch.float32, device=q.device)
+        A = torch.empty((B, T, H, chunk_size), dtype=torch.float32, device=q.device)
+        _lib.check(lib.gl_chunk_gla_fwd_intermediates(q.data_ptr(), k.data_ptr(), _ptr(g),
+                                                      _ptr(g_gamma), float(scale), B, T, H, K,
+                                                      chunk_size, g_cumsum.data_ptr(), A.data_ptr(),
+                                                      None, _stream()),
+                   "gl_chunk_gla_fwd_intermediates")
+    return GLAForward(o, ht if output_final_state else None, h, g_cumsum, A)
 
 
 def chunk_gla_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, do: torch.Tensor,

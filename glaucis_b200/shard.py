@@ -190,12 +190,22 @@ def gmm_fp8_fwd_gathered(a_q: torch.Tensor, a_s: torch.Tensor, b_q: torch.Tensor
     (gl_gmm_fp8_fwd_scatter).  A stream-ordered all-reduce of one int then
     orders the readers, so when the current stream reaches it every rank's
     rows are in `peers.local`, which is returned ([sum of rows, N] bf16).
-    Collective: every rank calls it, in the same order.  Each output element
-    is computed in the single-GPU K-block order, so the assembled output
-    equals a one-GPU gl_gmm_fp8_fwd bit for bit.  `group_sizes` (int32, on
-    the device) may hold me.sizes already, saving a host-to-device copy."""
+    The result IS the shared buffer: it stays valid until the next call,
+    which overwrites it on every rank.  That call's kernels start only after
+    a second stream-ordered all-reduce of one int that every rank enqueues
+    before its kernel, so no rank stores into a peer's buffer while that
+    peer's stream still has earlier work on it (reads of the previous result
+    enqueued before the call).  Collective: every rank calls it, in the same
+    order.  Each output element is computed in the single-GPU K-block order,
+    so the assembled output equals a one-GPU gl_gmm_fp8_fwd bit for bit.
+    `group_sizes` (int32, on the device) may hold me.sizes already, saving a
+    host-to-device copy."""
     import torch.distributed as dist
     from . import ops
+    # write-after-read order across calls: every rank's earlier stream work
+    # on its buffer precedes this all-reduce, which precedes every store
+    flag = torch.zeros(1, dtype=torch.int32, device=peers.local.device)
+    dist.all_reduce(flag)
     if me.rows:
         if a_q.shape[0] != me.rows or b_q.shape[0] != me.g1 - me.g0:
             raise ValueError("a_q must hold this rank's rows and b_q its groups' weights")
@@ -203,6 +213,5 @@ def gmm_fp8_fwd_gathered(a_q: torch.Tensor, a_s: torch.Tensor, b_q: torch.Tensor
         if gs is None:
             gs = torch.from_numpy(np.ascontiguousarray(me.sizes, np.int32)).to(a_q.device)
         ops.gmm_fp8_fwd_scatter(a_q, a_s, b_q, b_s, gs, peers.ptrs, me.r0)
-    flag = torch.zeros(1, dtype=torch.int32, device=peers.local.device)
     dist.all_reduce(flag)
     return peers.local

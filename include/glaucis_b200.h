@@ -158,6 +158,26 @@ int gl_chunk_gla_fwd(const void* q, const void* k, const void* v, const float* g
                      void* stream);
 
 /*
+ * The intermediates of the chunked GLA forward that gl_chunk_gla_fwd keeps on
+ * chip, for callers that read them:
+ *   g_cumsum fp32 [B, T, H, K]  chunk-local cumsum of g (or g_gamma[h]*(1..64))
+ *   A        fp32 [B, T, H, 64] A[i, j] = scale * sum_k q[i,k] e^{G[i,k]}
+ *                               k[j,k] e^{-G[j,k]} per chunk, full 64x64
+ *                               square (not causally masked)
+ * Either output may be NULL (not written); q, k, g / g_gamma, scale and the
+ * shapes as gl_chunk_gla_fwd.  fp32 arithmetic (not the tensor cores), one
+ * extra pass over q, k and g.  err_word is accepted for symmetry and never
+ * written (the kernel has no device-side waits).
+ * Replaces the g_cumsum and A outputs of chunk_gla_fwd
+ * (KE/examples/kernels/chunk_gla.py:258-273; A from chunk_gla_fwd_intra_gk
+ * :146-188, g_cumsum :265-267).
+ */
+int gl_chunk_gla_fwd_intermediates(const void* q, const void* k, const float* g,
+                                   const float* g_gamma, float scale, int64_t B, int64_t T,
+                                   int64_t H, int64_t K, int64_t chunk_size, float* g_cumsum,
+                                   float* A, int* err_word, void* stream);
+
+/*
  * gl_chunk_gla_fwd with a caller-owned device workspace.  When B*H is small
  * against the SM count (few heads, long sequences) the sequence is split into
  * segments.  The first, short segment runs its full pass from h0 beside a
@@ -265,9 +285,12 @@ int gl_tgmm_fp8(const void* lq, const float* ls, const void* dq, const float* ds
  * gl_gmm_fp8_fwd on it.
  *   lhs bf16 [M, K] with M * K <= GL_NOALLOC_MAX_ACT_ELEMS (else GL_EINVAL);
  *   b_q, b_s, group_sizes, out, out_dtype as gl_gmm_fp8_fwd.
- *   err_word: optional caller-owned device int for device-side error codes;
- *   with NULL they go to the scratch array's own word, which every call
- *   clears first and which is not reported back.
+ *   err_word: caller-owned device int for device-side error codes (invalid
+ *   group_sizes, a wait that gave up).  Callers that need those errors must
+ *   pass one: with NULL they go to the scratch array's own word, which every
+ *   call clears first and which nothing reads back (gl_device_status(NULL)
+ *   reads the library word, which this entry point never touches because
+ *   that word is allocated memory).
  * All calls on a device share the scratch array and it keeps the last
  * call's contents; calls whose GPU work overlaps race on it.  The first call
  * on each device looks up the array's device address; make it before any

@@ -85,6 +85,26 @@ def chunk_gla_fwd(q, k, v, g=None, g_gamma=None, h0=None, scale=None, chunk_size
     return o, ht
 
 
+def chunk_gla_fwd_intermediates(q, k, g=None, g_gamma=None, scale=None, chunk_size=64):
+    """The first two outputs of the reference's chunk_gla_fwd: g_cumsum fp32
+    [B,T,H,K] and the intra-chunk A = (q e^G)(k e^-G)^T * scale fp32 [B,T,H,C]
+    over the full C x C square (the causal mask is applied only when o is
+    formed), chunk_gla_ref.py:58-77, :102-117."""
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    B, T, H, K = q.shape
+    C = chunk_size
+    NT = T // C
+    if scale is None:
+        scale = K ** -0.5
+    gcs = g_cumsum_from(g, g_gamma, B, T, H, K, C)
+    gc = gcs.reshape(B, NT, C, H, K)
+    qg = q.reshape(B, NT, C, H, K) * np.exp(gc)
+    kg = k.reshape(B, NT, C, H, K) * np.exp(-gc)
+    A = np.einsum("bnihk,bnjhk->bnihj", qg, kg) * np.float32(scale)
+    return gcs, A.reshape(B, T, H, C).astype(np.float32)
+
+
 def naive_recurrence(q, k, v, g=None, g_gamma=None, h0=None, scale=None, chunk_size=64):
     """Token-level recurrence in float64 (small sizes only).  The per-head
     gate contributes g_gamma per token; the per-key gate g[t] per token."""

@@ -45,3 +45,27 @@ def test_gathered_matmul_equals_one_gpu(cuda, one_rank_group):
         assert torch.equal(got[:rows], want[:rows])
     finally:
         peers.close()
+
+
+def test_gathered_matmul_two_calls_with_different_inputs(cuda, one_rank_group):
+    # The result is the shared buffer itself: the second call overwrites it, so
+    # the first result is cloned before that call; both must equal one GPU.
+    cfg = configs.GMMConfig("t2", G=4, M=1024, K=512, N=256, routing="uniform_one_empty")
+    (me,) = shard.gmm_partition(configs.group_sizes(cfg.routing, cfg.G, cfg.M, seed=41), 1)
+    peers = shard.PeerBuffers(cfg.M, cfg.N)
+    try:
+        outs, wants = [], []
+        for seed in (41, 42):
+            lhs, rhs, _ = configs.make_gmm_inputs(cfg, device=cuda, seed=seed)
+            gs = torch.from_numpy(me.sizes).to(cuda)
+            a_q, a_s = ops.quant_act_1x128(lhs)
+            b_q, b_s = ops.quant_w_128x128(rhs[me.g0:me.g1].contiguous())
+            wants.append(ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs, out_dtype=torch.bfloat16))
+            outs.append(shard.gmm_fp8_fwd_gathered(a_q, a_s, b_q, b_s, me, peers, gs).clone())
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        assert not torch.equal(wants[0], wants[1])
+        for got, want in zip(outs, wants):
+            assert torch.equal(got, want)
+    finally:
+        peers.close()
