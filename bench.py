@@ -3,25 +3,36 @@ chunked-GLA forward, one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Headline workload: gmm_moe_up — G=128 experts, M=32768 routed rows (4096
-tokens x top-8, Zipf(1.2) routing, some experts empty), K=7168, N=2048, e4m3
-operands with 1x128 / 128x128 fp32 block scales, bf16 output.  One step = one
-grouped-matmul launch over the resident, pre-quantised operands (inputs are
-larger than L2: 2.1 GB of e4m3 operands, so no flush is needed).
-`value` = whole-job TFLOP/s (algorithmic 2*M*K*N per step, summed over ranks,
-divided by the slowest rank's time).
+Headline workload: gmm_dense_expert — G=8 experts, M=65536 rows (seeded
+uniform-random group sizes, one expert empty), K=4096, N=14336, e4m3 operands
+with 1x128 / 128x128 fp32 block scales, bf16 output (7.70 TFLOP per step, the
+tensor-bound configuration).  Strong scaling: one instance of the workload is
+split across the N ranks by expert group (contiguous 128-row cuts balanced by
+rows; a cut may fall inside an expert) and one step = each rank's
+grouped-matmul launch whose epilogue stores every finished output slice into
+every rank's output buffer over NVLink (the output all-gather inside the
+kernel), bracketed by two stream-ordered all-reduces of one int.  At N=1 the
+step is the plain launch.  `value` = the instance's 2*M*K*N / the slowest
+rank's step time.  Operands (0.74 GB e4m3) and the 1.9 GB output exceed L2,
+so no flush.  The same instance with an NCCL all-gather after the matmul,
+and plain copy-engine peer copies of each rank's output slab (the measured
+link peak the gather is compared with), are timed beside it.
 
-Multi-GPU (torchrun, one process per GPU): weak scaling — every rank runs
-its own instance of the workload (its own seeded routing), no data-path
-collective; timing is the max over ranks.
+Secondary rows, one instance per rank (weak scaling): gmm_moe_up (G=128,
+M=32768, K=7168, N=2048; HBM-bound) with its quantisers and the backward
+kernels, gmm_small (G=8, M=2048, K=N=1024), and the GLA forward / backward
+on gla_b8_t4096 and gla_b1_t32768; for N > 1 also gla_b1_t32768 split by
+head (strong).
 
-`e2e` times the public op gmm_fp8_blockwise(lhs, rhs, group_sizes) from
-pinned host activations: H2D of lhs + group_sizes, activation and weight
-quantisation, the grouped matmul, D2H of the bf16 output.  The bf16 weights
-stay resident on the device (model parameters).
+`e2e` times the public host-input op gmm_fp8_blockwise_host(lhs, rhs,
+group_sizes) on the headline workload (each rank its shard of rows and
+experts): H2D of the pinned activations, activation and weight quantisation,
+the grouped matmul, D2H of the bf16 output rows, copies overlapping the
+kernels.  The bf16 weights stay resident on the device (model parameters).
 
 `--impl reference` times the CPU restatement of the same path (the reference
-itself is JAX + tokamax on TPU and cannot run here) on the host cores.
+itself is JAX + tokamax on TPU, and JAX is not installed on this box) on the
+host cores.
 """
 from __future__ import annotations
 
@@ -39,10 +50,16 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "FP8 GMM TFLOP/s & chunk_gla fwd tokens/s at 1/2/4/8 B200, % of roofline"
-HEADLINE = "gmm_moe_up"
+HEADLINE = "gmm_dense_expert"
+MOE_WORKLOAD = "gmm_moe_up"
+SMALL_WORKLOAD = "gmm_small"
 GLA_WORKLOAD = "gla_b8_t4096"
 GLA_LONG_WORKLOAD = "gla_b1_t32768"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# Back-to-back tcgen05.mma.kind::f8f6f4 128x256x32 from shared memory, one CTA
+# per SM, no loads and no promotion (a microbenchmark, 69.4 ns per MMA at the
+# burst clock): the rate the tensor pipe sustains for this instruction shape.
+MMA_STREAM_TFLOPS = 4470.0
 
 
 def load_peaks():
@@ -212,23 +229,23 @@ class _Null:
 # ---------------------------------------------------------------------------
 # CPU baselines (the oracle restatement, timed on the host cores)
 # ---------------------------------------------------------------------------
-def cpu_gmm_step(sample_rows: int, seed: int = 0):
-    """Builds a bounded sample of the headline workload (its first non-empty
-    experts, about `sample_rows` rows, full K and N) for the BLAS-backed CPU
-    restatement.  Returns (step_fn, flops_per_step, description)."""
+def cpu_gmm_step(sample_rows: int, seed: int = 0, workload: str = HEADLINE):
+    """Builds a bounded sample of a grouped-matmul workload (its first
+    `sample_rows` rows in group order, with the experts they belong to, full
+    K and N) for the BLAS-backed CPU restatement.  Returns (step_fn,
+    flops_per_step, description)."""
     import torch
     from glaucis_b200 import configs
     from oracle import cpu_fast
-    cfg = configs.GMM_CONFIGS[HEADLINE]
+    cfg = configs.GMM_CONFIGS[workload]
     sizes = configs.group_sizes(cfg.routing, cfg.G, cfg.M, seed=seed, topk=cfg.topk, zipf=cfg.zipf)
     sel = []
     rows = 0
     for g in range(cfg.G):
-        if sizes[g] > 0:
-            sel.append(int(sizes[g]))
-            rows += int(sizes[g])
-            if rows >= sample_rows:
-                break
+        if sizes[g] > 0 and rows < sample_rows:
+            take = min(int(sizes[g]), sample_rows - rows)
+            sel.append(take)
+            rows += take
     gen = torch.Generator().manual_seed(seed)
     lhs = torch.randn((rows, cfg.K), generator=gen).to(torch.bfloat16)
     rhs = (torch.randn((len(sel), cfg.K, cfg.N), generator=gen) * cfg.rhs_std).to(torch.bfloat16)
@@ -237,8 +254,9 @@ def cpu_gmm_step(sample_rows: int, seed: int = 0):
         cpu_fast.gmm_fp8_blockwise(lhs, rhs, sel)
 
     flops = 2.0 * rows * cfg.K * cfg.N
-    desc = (f"{len(sel)} of {cfg.G} experts of {HEADLINE} ({rows} of {cfg.M} rows, K={cfg.K}, "
-            f"N={cfg.N}): quantise lhs+rhs, dequantised fp32 GEMM per expert (torch CPU, BLAS)")
+    desc = (f"first {rows} of {cfg.M} rows of {workload} ({len(sel)} of {cfg.G} experts, "
+            f"K={cfg.K}, N={cfg.N}): quantise lhs+rhs, dequantised fp32 GEMM per expert "
+            f"(torch CPU, BLAS)")
     return step, flops, desc
 
 
@@ -288,8 +306,10 @@ def run_reference(args):
         torch.set_num_threads(cores)
     except Exception:
         pass
+    from glaucis_b200 import configs
+    cfg = configs.GMM_CONFIGS[HEADLINE]
     # keep the whole arm to a couple of minutes whatever --steps/--warmup are
-    rows = max(256, int(args.cpu_rows * min(1.0, 13.0 / (args.steps + args.warmup))))
+    rows = max(128, int(args.cpu_rows * min(1.0, 13.0 / (args.steps + args.warmup))))
     step, flops, desc = cpu_gmm_step(sample_rows=rows)
     for _ in range(args.warmup):
         step()
@@ -303,18 +323,19 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "e4m3 x e4m3 -> fp32 (dequantised fp32 GEMM on the host)",
         "data": "synthetic",
-        "config": {"workload": HEADLINE, "G": 128, "M": 32768, "K": 7168, "N": 2048,
-                   "routing": "zipf(1.2) top-8", "sample": desc},
+        "config": {"workload": HEADLINE, "G": cfg.G, "M": cfg.M, "K": cfg.K, "N": cfg.N,
+                   "routing": configs.routing_desc(cfg), "sample": desc},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "gla": {"workload": GLA_WORKLOAD, "tokens_per_s": gtok / gdt, "sample": gdesc},
         "note": ("the reference path (JAX + qwix + tokamax Pallas on TPU) cannot run on this "
-                 "box; this arm times the CPU restatement of the same forward in oracle/"),
+                 "box (JAX is not installed here or on the B200 box); this arm times the CPU "
+                 "restatement of the same forward in oracle/"),
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -323,16 +344,190 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
-def run_b200(args):
+def gmm_bytes(cfg, g_nz: int, rows: int = None) -> float:
+    """Algorithmic HBM bytes of one grouped-matmul launch on pre-quantised
+    operands: e4m3 activations + their 1x128 scales, the e4m3 weights and
+    128x128 scales of the non-empty experts, the group sizes, the bf16 output."""
+    m = cfg.M if rows is None else rows
+    return (m * cfg.K + 4 * m * cfg.K / 128 + g_nz * cfg.K * cfg.N
+            + 4 * g_nz * (cfg.K / 128) * (cfg.N / 128) + 4 * cfg.G + 2 * m * cfg.N)
+
+
+def headline_gmm(args, rank, world, local, peaks, peak_kind):
+    """gmm_dense_expert split across the ranks by expert group, the output
+    gathered on every rank by the matmul's own epilogue (strong scaling)."""
+    import torch
+    from glaucis_b200 import configs, ops, shard
+    cfg = configs.GMM_CONFIGS[HEADLINE]
+    fp8_peak = 2.0 * peaks["bf16_tflops"]
+    lhs, rhs, gs = configs.make_gmm_inputs(cfg, device="cuda", seed=args.seed)  # same on every rank
+    sizes = gs.cpu().numpy()
+    parts = shard.gmm_partition(sizes, world)
+    me = parts[rank]
+    counts = [p.rows for p in parts]
+    rows_total = sum(counts)
+    flops_total = 2.0 * rows_total * cfg.K * cfg.N
+    flops_me = 2.0 * me.rows * cfg.K * cfg.N
+    g_nz_me = int((me.sizes > 0).sum())
+    a_q, a_s = ops.quant_act_1x128(lhs[me.r0:me.r1].contiguous())
+    b_q, b_s = ops.quant_w_128x128(rhs[me.g0:me.g1].contiguous())
+    gs_l = torch.from_numpy(np.ascontiguousarray(me.sizes, np.int32)).to("cuda")
+    sampler = ClockSampler(local) if rank == 0 else None
+    res = {"rows_per_rank": counts, "groups_per_rank": [p.g1 - p.g0 for p in parts]}
+    peers = None
+    if world == 1:
+        out = torch.empty((cfg.M, cfg.N), dtype=torch.bfloat16, device="cuda")
+
+        def step():
+            ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs_l, out=out)
+
+        ms = timed(step, args.steps, args.warmup, world, sampler)
+        compute_ms = ms
+    else:
+        out_l = torch.empty((me.rows, cfg.N), dtype=torch.bfloat16, device="cuda")
+        compute_ms = timed(lambda: ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs_l, out=out_l),
+                           max(5, args.steps // 2), args.warmup, world)
+        peers = shard.PeerBuffers(rows_total, cfg.N)
+
+        def step():
+            shard.gmm_fp8_fwd_gathered(a_q, a_s, b_q, b_s, me, peers, group_sizes=gs_l)
+
+        ms = timed(step, args.steps, args.warmup, world, sampler)
+    if ops.device_status() != 0:
+        raise SystemExit("device error word set after the headline timed region")
+    res.update(ms=ms, compute_ms=compute_ms, flops_total=flops_total, flops_per_rank=flops_me,
+               sampler=sampler)
+    achieved = flops_me / (ms * 1e-3) / 1e12
+    res["roofline"] = {
+        "bound": "tensor", "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
+        "frac": achieved / fp8_peak, "traffic": ncu_traffic("gmm_fp8_fwd_kernel", HEADLINE),
+        "peak_source": f"2 x {peak_kind} bf16_tflops (dense e4m3 rate)",
+        "kernel": "gmm_fp8_fwd_kernel" if world == 1 else "gmm_fp8_fwd_kernel (scatter epilogue)",
+        "per": "one GPU: its rows' 2*m*K*N over the step time" if world > 1 else "the launch",
+        "mma_stream_frac": achieved / MMA_STREAM_TFLOPS,
+        "mma_stream_tflops": MMA_STREAM_TFLOPS,
+        "compute_only_frac": flops_me / (compute_ms * 1e-3) / 1e12 / fp8_peak,
+        "algorithmic_flops_per_launch": flops_me,
+        "algorithmic_bytes_per_launch": gmm_bytes(cfg, g_nz_me, me.rows),
+    }
+    if world > 1:
+        # -------------------------------------------------- the gather's links
+        row_bytes = 2 * cfg.N
+        slab = me.rows * row_bytes
+        pushed = slab * (world - 1)
+        received = (rows_total - me.rows) * row_bytes
+        same = None
+        if rank == 0:
+            fa, fs = ops.quant_act_1x128(lhs)
+            fb, fbs = ops.quant_w_128x128(rhs)
+            single = ops.gmm_fp8_fwd(fa, fs, fb, fbs, gs, out_dtype=torch.bfloat16)
+            same = bool(torch.equal(single[:rows_total], peers.local))
+            del fa, fs, fb, fbs, single
+        views = [shard.tensor_at(ptr, (rows_total, cfg.N)) for ptr in peers.ptrs]
+        own = peers.local[me.r0:me.r1]
+        nxt = (rank + 1) % world
+        others = [(rank + i) % world for i in range(1, world)]
+        streams = {r: torch.cuda.Stream() for r in others}
+
+        def copy_one():
+            views[nxt][me.r0:me.r1].copy_(own, non_blocking=True)
+
+        def copy_all():
+            cur = torch.cuda.current_stream()
+            for r in others:
+                streams[r].wait_stream(cur)
+                with torch.cuda.stream(streams[r]):
+                    views[r][me.r0:me.r1].copy_(own, non_blocking=True)
+            for r in others:
+                cur.wait_stream(streams[r])
+
+        one_ms = timed(copy_one, 5, 2, world)
+        all_ms = timed(copy_all, 5, 2, world)
+        out_full = torch.empty((rows_total, cfg.N), dtype=torch.bfloat16, device="cuda")
+
+        def nccl_step():
+            ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs_l, out=out_l)
+            shard.all_gather_rows(out_l, counts, out_full)
+
+        nccl_ms = timed(nccl_step, max(5, args.steps // 2), 3, world)
+        if ops.device_status() != 0:
+            raise SystemExit("device error word set after the gather rows")
+        peer_all_gbs = pushed / (all_ms * 1e-3) / 1e9
+        res["gather"] = {
+            "in_kernel": "each rank's matmul epilogue TMA-stores every finished 32x128 output "
+                         "slice into every rank's IPC-shared buffer (own + peers over NVLink)",
+            "matches_single_gpu": same,
+            "bytes_pushed_per_rank": pushed, "bytes_received_per_rank": received,
+            "nvlink_gbs_per_rank": pushed / (ms * 1e-3) / 1e9,
+            "peer_copy_one_gbs": slab / (one_ms * 1e-3) / 1e9,
+            "peer_copy_all_gbs": peer_all_gbs,
+            "frac_of_peer_copy_all": (pushed / (ms * 1e-3) / 1e9) / peer_all_gbs,
+            "link_bound_ms": max(compute_ms, all_ms),
+            "peer_copy": "copy engines, cudaMemcpyAsync of this rank's output slab into the next "
+                         "rank's buffer (one) and into every peer's buffer at once, one stream "
+                         "per peer (all); max over ranks",
+            "nccl_allgather_after_matmul_ms": nccl_ms,
+            "nccl_tflops": flops_total / (nccl_ms * 1e-3) / 1e12,
+        }
+        del views, own, out_full, out_l
+        peers.close()
+    # ------------------------------------------------------------------ e2e
+    if not args.skip_e2e:
+        lhs_h = lhs[me.r0:me.r1].cpu().pin_memory()
+        rhs_l = rhs[me.g0:me.g1].contiguous()
+        gs_h = torch.from_numpy(np.ascontiguousarray(me.sizes, np.int32)).pin_memory()
+        out_h = torch.empty((me.rows, cfg.N), dtype=torch.bfloat16).pin_memory()
+        n_chunks = len(ops._plan_chunks(me.sizes, 16)[0])
+
+        def e2e_step():
+            # public host-input op: pinned activations and group sizes in,
+            # pinned bf16 output back; copies overlap the kernels
+            ops.gmm_fp8_blockwise_host(lhs_h, rhs_l, gs_h, out=out_h, out_dtype=torch.bfloat16)
+
+        e_steps = max(1, min(args.steps, args.e2e_steps))
+        e_ms = timed(e2e_step, e_steps, min(args.warmup, 2), world)
+
+        def copy_ms(dst, src):
+            best = float("inf")
+            for _ in range(3):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                dst.copy_(src, non_blocking=True)
+                e1.record()
+                e1.synchronize()
+                best = min(best, e0.elapsed_time(e1))
+            return best
+
+        lhs_d = torch.empty(lhs_h.shape, dtype=lhs_h.dtype, device="cuda")
+        h2d_ms = copy_ms(lhs_d, lhs_h)
+        out_d = torch.empty(out_h.shape, dtype=torch.bfloat16, device="cuda")
+        d2h_ms = copy_ms(out_h, out_d)
+        res["e2e"] = {
+            "value": flops_total / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": lhs_h.numel() * 2 + n_chunks * (me.g1 - me.g0) * 4,
+            "d2h_bytes_per_step": out_h.numel() * 2, "ms_per_step": e_ms,
+            "link": {"h2d_gbs": lhs_h.numel() * 2 / (h2d_ms * 1e-3) / 1e9,
+                     "d2h_gbs": out_h.numel() * 2 / (d2h_ms * 1e-3) / 1e9,
+                     "h2d_ms": h2d_ms, "d2h_ms": d2h_ms,
+                     "note": "one plain pinned copy each way of this rank's activations / output"},
+            "path": "gmm_fp8_blockwise_host(lhs, rhs, group_sizes) on each rank's shard: H2D lhs "
+                    "rows in up to 16 chunks overlapping quantise lhs (per chunk) + rhs and the "
+                    "grouped matmul, D2H of the bf16 output rows per chunk; the ranks' outputs "
+                    "together are the whole [M, N] in host memory",
+            "bytes_note": "per rank (each rank copies its own shard)"}
+        del lhs_h, rhs_l, out_h, lhs_d, out_d
+    del lhs, rhs, a_q, a_s, b_q, b_s
+    torch.cuda.empty_cache()
+    return res
+
+
+def secondary_gmm(args, workload, rank, world, peaks, peak_kind, with_extras: bool):
+    """One instance of a grouped-matmul workload per rank (weak scaling), with
+    its HBM / tensor roofline; with_extras adds the quantiser and backward rows."""
     import torch
     from glaucis_b200 import configs, ops
-    rank, world, local = dist_setup(args.gpus)
-    peaks, peak_kind = load_peaks()
-    traffic = ncu_traffic("gmm_fp8_fwd_kernel", args.workload)
     fp8_peak = 2.0 * peaks["bf16_tflops"]
-
-    # ---------------------------------------------------------------- GMM
-    cfg = configs.GMM_CONFIGS[args.workload]
+    cfg = configs.GMM_CONFIGS[workload]
     lhs, rhs, gs = configs.make_gmm_inputs(cfg, device="cuda", seed=args.seed + rank)
     a_q, a_s = ops.quant_act_1x128(lhs)
     b_q, b_s = ops.quant_w_128x128(rhs)
@@ -340,61 +535,48 @@ def run_b200(args):
     sizes = gs.cpu().numpy()
     g_nz = int((sizes > 0).sum())
     flops = 2.0 * float(sizes.sum()) * cfg.K * cfg.N
-    alg_bytes = (cfg.M * cfg.K + 4 * cfg.M * cfg.K / 128 + g_nz * cfg.K * cfg.N
-                 + 4 * g_nz * (cfg.K / 128) * (cfg.N / 128) + 4 * cfg.G + 2 * cfg.M * cfg.N)
-
-    def gmm_step():
-        ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs, out=out)
-
-    sampler = ClockSampler(local) if rank == 0 else None
-    ms = timed(gmm_step, args.steps, args.warmup, world, sampler)
-    status = ops.device_status()
-    if status != 0:
-        raise SystemExit(f"device error word {status} after the timed region")
-    value = whole_job_rate(flops, world, ms) / 1e12
+    alg_bytes = gmm_bytes(cfg, g_nz)
+    ms = timed(lambda: ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs, out=out), args.steps, args.warmup,
+               world)
+    if ops.device_status() != 0:
+        raise SystemExit(f"device error word set after the {workload} timed region")
     ai = flops / alg_bytes
     ridge = fp8_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
-    bound = "hbm" if ai < ridge else "tensor"
-    if bound == "hbm":
-        achieved = alg_bytes / (ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
-                "peak_source": f"{peak_kind} hbm_gbs"}
-    else:
-        achieved = flops / (ms * 1e-3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
-                "frac": achieved / fp8_peak, "traffic": traffic,
-                "peak_source": f"2 x {peak_kind} bf16_tflops (dense e4m3 rate)"}
-    roof["kernel"] = "gmm_fp8_fwd_kernel"
-    roof["fp8_tensor_frac"] = flops / (ms * 1e-3) / 1e12 / fp8_peak
-    roof["algorithmic_bytes_per_launch"] = alg_bytes
-    roof["algorithmic_flops_per_launch"] = flops
-
-    # quantiser rows (separately timed kernels of the same forward)
-    # outputs preallocated: the timed region holds the quantiser kernels only
+    gbs = alg_bytes / (ms * 1e-3) / 1e9
+    tfl = flops / (ms * 1e-3) / 1e12
+    blk = {"workload": workload, "G": cfg.G, "M": cfg.M, "K": cfg.K, "N": cfg.N,
+           "routing": configs.routing_desc(cfg), "empty_groups": cfg.G - g_nz,
+           "ms_per_step": ms, "tflops": world * tfl,
+           "roofline": {"bound": "hbm" if ai < ridge else "tensor",
+                        "achieved": gbs if ai < ridge else tfl,
+                        "unit": "GB/s" if ai < ridge else "TFLOP/s",
+                        "peak": peaks["hbm_gbs"] if ai < ridge else fp8_peak,
+                        "frac": gbs / peaks["hbm_gbs"] if ai < ridge else tfl / fp8_peak,
+                        "fp8_tensor_frac": tfl / fp8_peak, "mma_stream_frac": tfl / MMA_STREAM_TFLOPS,
+                        "traffic": ncu_traffic("gmm_fp8_fwd_kernel", workload),
+                        "algorithmic_bytes_per_launch": alg_bytes,
+                        "algorithmic_flops_per_launch": flops, "kernel": "gmm_fp8_fwd_kernel",
+                        "peak_source": f"{peak_kind} hbm_gbs / 2 x {peak_kind} bf16_tflops"}}
+    if not with_extras:
+        del lhs, rhs, a_q, a_s, b_q, b_s, out
+        torch.cuda.empty_cache()
+        return blk
+    # quantiser rows (separately timed kernels of the same forward); outputs
+    # preallocated: the timed region holds the quantiser kernels only
     qa_o, sa_o = torch.empty_like(a_q), torch.empty_like(a_s)
     qw_o, sw_o = torch.empty_like(b_q), torch.empty_like(b_s)
-    qs_act = ClockSampler(local) if rank == 0 else None
-    q_act_ms = timed(lambda: ops.quant_act_1x128(lhs, qa_o, sa_o), max(5, args.steps // 2), 3, world,
-                     qs_act)
-    qs_w = ClockSampler(local) if rank == 0 else None
-    q_w_ms = timed(lambda: ops.quant_w_128x128(rhs, qw_o, sw_o), max(5, args.steps // 10), 3, world,
-                   qs_w)
+    q_act_ms = timed(lambda: ops.quant_act_1x128(lhs, qa_o, sa_o), max(5, args.steps // 2), 3, world)
+    q_w_ms = timed(lambda: ops.quant_w_128x128(rhs, qw_o, sw_o), max(5, args.steps // 10), 3, world)
     del qa_o, sa_o, qw_o, sw_o
-    # algorithmic bytes: bf16 in, e4m3 out, fp32 scales out
     q_act_bytes = lhs.numel() * 3 + lhs.numel() // 128 * 4
     q_w_bytes = rhs.numel() * 3 + rhs.numel() // (128 * 128) * 4
-    quantisers = {
+    blk["quantisers"] = {
         name: {"ms": ms_, "achieved_gbs": by / (ms_ * 1e-3) / 1e9,
-               "frac": by / (ms_ * 1e-3) / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": by,
-               "sm_mhz": cs.summary()["sm_mhz"] if cs else None}
-        for name, ms_, by, cs in (("quant_act_1x128", q_act_ms, q_act_bytes, qs_act),
-                                  ("quant_w_128x128", q_w_ms, q_w_bytes, qs_w))}
-
-    # ---------------------------------------------------------------- e2e
-    # ------------------------------------------------- GMM backward rows
-    # dlhs (grouped kernel, weight transposed) and drhs (tgmm) on the same
-    # workload with a synthetic output gradient, quantised inputs resident.
+               "frac": by / (ms_ * 1e-3) / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": by}
+        for name, ms_, by in (("quant_act_1x128", q_act_ms, q_act_bytes),
+                              ("quant_w_128x128", q_w_ms, q_w_bytes))}
+    # backward: dlhs (grouped kernel, weight transposed) and drhs (tgmm) with a
+    # synthetic output gradient, quantised inputs resident
     gen = torch.Generator(device="cuda").manual_seed(args.seed + 7 + rank)
     grad = torch.randn((cfg.M, cfg.N), device="cuda", generator=gen).to(torch.bfloat16)
     dq1, ds1 = ops.quant_act_1x128(grad)
@@ -414,143 +596,108 @@ def run_b200(args):
     qc_bytes = grad.numel() * 3 + grad.numel() // 128 * 4
 
     def row(ms_, by, fl):
-        gbs = by / (ms_ * 1e-3) / 1e9
-        r = {"ms": ms_, "achieved_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"],
-             "algorithmic_bytes": by}
+        g = by / (ms_ * 1e-3) / 1e9
+        r = {"ms": ms_, "achieved_gbs": g, "hbm_frac": g / peaks["hbm_gbs"], "algorithmic_bytes": by}
         if fl:
             r["tflops"] = world * fl / (ms_ * 1e-3) / 1e12
             r["fp8_tensor_frac"] = fl / (ms_ * 1e-3) / 1e12 / fp8_peak
         return r
 
-    gmm_bwd = {"workload": args.workload,
-               "dlhs": row(dl_ms, dl_bytes, flops), "tgmm": row(tg_ms, tg_bytes, flops),
-               "quant_col_128x1": row(qc_ms, qc_bytes, 0.0),
-               "note": "dlhs = gl_gmm_fp8_dlhs (grouped kernel, K-major weight); tgmm writes "
-                       "drhs [G, K, N] bf16 for every group (empty ones as zeros)"}
-    del grad, dq1, ds1, dq2, ds2, lq, ls, dlhs, drhs
+    blk["bwd"] = {"dlhs": row(dl_ms, dl_bytes, flops), "tgmm": row(tg_ms, tg_bytes, flops),
+                  "quant_col_128x1": row(qc_ms, qc_bytes, 0.0),
+                  "note": "dlhs = gl_gmm_fp8_dlhs (grouped kernel, K-major weight); tgmm writes "
+                          "drhs [G, K, N] bf16 for every group (empty ones as zeros)"}
+    del grad, dq1, ds1, dq2, ds2, lq, ls, dlhs, drhs, lhs, rhs, a_q, a_s, b_q, b_s, out
     torch.cuda.empty_cache()
+    return blk
 
-    e2e = None
-    if not args.skip_e2e:
-        lhs_h = lhs.cpu().pin_memory()
-        gs_h = gs.cpu().pin_memory()
-        out_h = torch.empty((cfg.M, cfg.N), dtype=torch.bfloat16).pin_memory()
-        n_chunks = len(ops._plan_chunks(gs_h.numpy(), 16)[0])
 
-        def e2e_step():
-            # public host-input op: pinned activations and group sizes in,
-            # pinned bf16 output back; copies overlap the kernels
-            ops.gmm_fp8_blockwise_host(lhs_h, rhs, gs_h, out=out_h, out_dtype=torch.bfloat16)
+def gla_block(args, workload, rank, world, peaks, peak_kind):
+    import torch
+    from glaucis_b200 import configs, ops
+    gcfg = configs.GLA_CONFIGS[workload]
+    inp = configs.make_gla_inputs(gcfg, device="cuda", seed=args.seed + rank)
+    go = torch.empty_like(inp["v"])
+    ght = torch.empty((gcfg.B, gcfg.H, 128, 128), device="cuda")
 
-        e_steps = max(1, min(args.steps, args.e2e_steps))
-        e_ms = timed(e2e_step, e_steps, min(args.warmup, 2), world)
-        # the host link at the time of the run: plain pinned copies of the
-        # same activations and output (best of three, CUDA events), so the
-        # e2e figure can be read against the PCIe bound of this box
-        def copy_ms(dst, src):
-            best = float("inf")
-            for _ in range(3):
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                dst.copy_(src, non_blocking=True)
-                e1.record()
-                e1.synchronize()
-                best = min(best, e0.elapsed_time(e1))
-            return best
-        h2d_ms = copy_ms(lhs, lhs_h)
-        out_d = torch.empty((cfg.M, cfg.N), dtype=torch.bfloat16, device="cuda")
-        d2h_ms = copy_ms(out_h, out_d)
-        del out_d
-        e2e = {"value": world * flops / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": lhs_h.numel() * 2 + n_chunks * cfg.G * 4,
-               "d2h_bytes_per_step": out_h.numel() * 2, "ms_per_step": e_ms,
-               "link": {"h2d_gbs": lhs_h.numel() * 2 / (h2d_ms * 1e-3) / 1e9,
-                        "d2h_gbs": out_h.numel() * 2 / (d2h_ms * 1e-3) / 1e9,
-                        "h2d_ms": h2d_ms, "d2h_ms": d2h_ms,
-                        "note": "one plain pinned copy each way of the step's activations / output"},
-               "path": "gmm_fp8_blockwise_host(lhs, rhs, group_sizes): H2D lhs in 16 row chunks "
-                       "overlapping quantise lhs (per chunk) + rhs and the grouped matmul, D2H bf16 out "
-                       "per chunk"}
-        del lhs_h, out_h
+    def gla_step():
+        ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], 128 ** -0.5, 64,
+                          g=inp["g"], h0=inp["h0"], output_final_state=True, o=go, ht=ght)
 
-    del lhs, rhs, a_q, b_q, out
+    gla_ms = timed(gla_step, args.steps, args.warmup, world)
+    if ops.device_status() != 0:
+        raise SystemExit("device error word set after the GLA timed region")
+    gla_bytes = configs.gla_bytes(gcfg.B, gcfg.T, gcfg.H, has_h0=gcfg.h0_std > 0)
+    gla_flops = configs.gla_flops(gcfg.B, gcfg.T, gcfg.H)
+    gla_gbs = gla_bytes / (gla_ms * 1e-3) / 1e9
+    blk = {"workload": workload, "B": gcfg.B, "T": gcfg.T, "H": gcfg.H,
+           "tokens_per_s": world * gcfg.B * gcfg.T / (gla_ms * 1e-3), "ms_per_step": gla_ms,
+           "tflops": world * gla_flops / (gla_ms * 1e-3) / 1e12,
+           "roofline": {"bound": "hbm", "achieved": gla_gbs, "peak": peaks["hbm_gbs"],
+                        "unit": "GB/s", "frac": gla_gbs / peaks["hbm_gbs"],
+                        "bf16_tensor_frac": gla_flops / (gla_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+                        "kernel": "chunk_gla_fwd_kernel", "peak_source": f"{peak_kind} hbm_gbs",
+                        "algorithmic_bytes_per_step": gla_bytes,
+                        "traffic": ncu_traffic("chunk_gla_fwd_kernel", workload)}}
+    # backward: the training forward (o, ht and the per-chunk states h) and the
+    # backward (reverse state-gradient scan + chunk-parallel dq/dk/dv kernel)
+    # on a synthetic output gradient, buffers resident
+    gh = torch.empty((gcfg.B, gcfg.T // 64, gcfg.H, 128, 128), dtype=torch.bfloat16, device="cuda")
+
+    def fwd_states_step():
+        ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], 128 ** -0.5, 64,
+                          g=inp["g"], h0=inp["h0"], output_final_state=True, output_states=True,
+                          o=go, ht=ght, h=gh)
+
+    fs_ms = timed(fwd_states_step, max(5, args.steps // 2), 3, world)
+    gen = torch.Generator(device="cuda").manual_seed(args.seed + 11 + rank)
+    gdo = torch.randn(inp["v"].shape, generator=gen, device="cuda").to(torch.bfloat16)
+    dq, dk, dv = (torch.empty_like(inp[n]) for n in ("q", "k", "v"))
+    gws = torch.empty(ops.chunk_gla_bwd_workspace_bytes(gcfg.B, gcfg.T, gcfg.H),
+                      dtype=torch.uint8, device="cuda")
+
+    def bwd_step():
+        ops.chunk_gla_bwd(inp["q"], inp["k"], inp["v"], gdo, gh, inp["g_gamma"], 128 ** -0.5, 64,
+                          g=inp["g"], dq=dq, dk=dk, dv=dv, workspace=gws)
+
+    bw_ms = timed(bwd_step, max(5, args.steps // 2), 3, world)
+    if ops.device_status() != 0:
+        raise SystemExit("device error word set after the GLA backward rows")
+    pk = inp["g"] is not None
+    bw_bytes = configs.gla_bwd_bytes(gcfg.B, gcfg.T, gcfg.H, per_key_gate=pk)
+    bw_min = configs.gla_bwd_bytes(gcfg.B, gcfg.T, gcfg.H, per_key_gate=pk, fused_minimum=True)
+    bw_flops = configs.gla_bwd_flops(gcfg.B, gcfg.T, gcfg.H)
+    bw_gbs = bw_bytes / (bw_ms * 1e-3) / 1e9
+    blk["bwd"] = {
+        "ms_per_step": bw_ms, "tokens_per_s": world * gcfg.B * gcfg.T / (bw_ms * 1e-3),
+        "tflops": world * bw_flops / (bw_ms * 1e-3) / 1e12,
+        "achieved_gbs": bw_gbs, "hbm_frac": bw_gbs / peaks["hbm_gbs"],
+        "algorithmic_bytes_per_step": bw_bytes, "fused_minimum_bytes": bw_min,
+        "fused_minimum_frac": bw_min / (bw_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+        "fwd_with_states_ms": fs_ms,
+        "kernels": "chunk_gla_fwd_kernel in reverse-scan mode (+ its state-only pre-pass and "
+                   "fold when the sequence is split), then chunk_gla_bwd_kernel",
+    }
+    del inp, go, ght, gh, gdo, dq, dk, dv, gws
     torch.cuda.empty_cache()
+    return blk
 
-    # ---------------------------------------------------------------- GLA
-    def gla_block(workload):
-        gcfg = configs.GLA_CONFIGS[workload]
-        inp = configs.make_gla_inputs(gcfg, device="cuda", seed=args.seed + rank)
-        go = torch.empty_like(inp["v"])
-        ght = torch.empty((gcfg.B, gcfg.H, 128, 128), device="cuda")
 
-        def gla_step():
-            ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], 128 ** -0.5, 64,
-                              g=inp["g"], h0=inp["h0"], output_final_state=True, o=go, ht=ght)
+def run_b200(args):
+    import torch
+    from glaucis_b200 import configs
+    rank, world, local = dist_setup(args.gpus)
+    peaks, peak_kind = load_peaks()
+    cfg = configs.GMM_CONFIGS[HEADLINE]
 
-        gla_ms = timed(gla_step, args.steps, args.warmup, world)
-        if ops.device_status() != 0:
-            raise SystemExit("device error word set after the GLA timed region")
-        gla_bytes = configs.gla_bytes(gcfg.B, gcfg.T, gcfg.H, has_h0=gcfg.h0_std > 0)
-        gla_flops = configs.gla_flops(gcfg.B, gcfg.T, gcfg.H)
-        gla_gbs = gla_bytes / (gla_ms * 1e-3) / 1e9
-        blk = {"workload": workload, "B": gcfg.B, "T": gcfg.T, "H": gcfg.H,
-               "tokens_per_s": world * gcfg.B * gcfg.T / (gla_ms * 1e-3), "ms_per_step": gla_ms,
-               "tflops": world * gla_flops / (gla_ms * 1e-3) / 1e12,
-               "roofline": {"bound": "hbm", "achieved": gla_gbs, "peak": peaks["hbm_gbs"],
-                            "unit": "GB/s", "frac": gla_gbs / peaks["hbm_gbs"],
-                            "bf16_tensor_frac": gla_flops / (gla_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
-                            "kernel": "chunk_gla_fwd_kernel", "peak_source": f"{peak_kind} hbm_gbs",
-                            "algorithmic_bytes_per_step": gla_bytes,
-                            "traffic": ncu_traffic("chunk_gla_fwd_kernel", workload)}}
-        # backward: the training forward (o, ht and the per-chunk states h)
-        # and the backward (reverse state-gradient scan + chunk-parallel
-        # dq/dk/dv kernel) on a synthetic output gradient, buffers resident
-        gh = torch.empty((gcfg.B, gcfg.T // 64, gcfg.H, 128, 128), dtype=torch.bfloat16,
-                         device="cuda")
+    head = headline_gmm(args, rank, world, local, peaks, peak_kind)
+    ms = head["ms"]
+    value = head["flops_total"] / (ms * 1e-3) / 1e12
+    moe = secondary_gmm(args, MOE_WORKLOAD, rank, world, peaks, peak_kind, with_extras=True)
+    small = secondary_gmm(args, SMALL_WORKLOAD, rank, world, peaks, peak_kind, with_extras=False)
+    gla = gla_block(args, GLA_WORKLOAD, rank, world, peaks, peak_kind)
+    gla_long = gla_block(args, GLA_LONG_WORKLOAD, rank, world, peaks, peak_kind)
 
-        def fwd_states_step():
-            ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], 128 ** -0.5, 64,
-                              g=inp["g"], h0=inp["h0"], output_final_state=True, output_states=True,
-                              o=go, ht=ght, h=gh)
-
-        fs_ms = timed(fwd_states_step, max(5, args.steps // 2), 3, world)
-        gen = torch.Generator(device="cuda").manual_seed(args.seed + 11 + rank)
-        gdo = torch.randn(inp["v"].shape, generator=gen, device="cuda").to(torch.bfloat16)
-        dq, dk, dv = (torch.empty_like(inp[n]) for n in ("q", "k", "v"))
-        gws = torch.empty(ops.chunk_gla_bwd_workspace_bytes(gcfg.B, gcfg.T, gcfg.H),
-                          dtype=torch.uint8, device="cuda")
-
-        def bwd_step():
-            ops.chunk_gla_bwd(inp["q"], inp["k"], inp["v"], gdo, gh, inp["g_gamma"], 128 ** -0.5, 64,
-                              g=inp["g"], dq=dq, dk=dk, dv=dv, workspace=gws)
-
-        bw_ms = timed(bwd_step, max(5, args.steps // 2), 3, world)
-        if ops.device_status() != 0:
-            raise SystemExit("device error word set after the GLA backward rows")
-        pk = inp["g"] is not None
-        bw_bytes = configs.gla_bwd_bytes(gcfg.B, gcfg.T, gcfg.H, per_key_gate=pk)
-        bw_min = configs.gla_bwd_bytes(gcfg.B, gcfg.T, gcfg.H, per_key_gate=pk, fused_minimum=True)
-        bw_flops = configs.gla_bwd_flops(gcfg.B, gcfg.T, gcfg.H)
-        bw_gbs = bw_bytes / (bw_ms * 1e-3) / 1e9
-        blk["bwd"] = {
-            "ms_per_step": bw_ms, "tokens_per_s": world * gcfg.B * gcfg.T / (bw_ms * 1e-3),
-            "tflops": world * bw_flops / (bw_ms * 1e-3) / 1e12,
-            "achieved_gbs": bw_gbs, "hbm_frac": bw_gbs / peaks["hbm_gbs"],
-            "algorithmic_bytes_per_step": bw_bytes,
-            "fused_minimum_bytes": bw_min,
-            "fused_minimum_frac": bw_min / (bw_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
-            "fwd_with_states_ms": fs_ms,
-            "kernels": "chunk_gla_fwd_kernel in reverse-scan mode (+ its state-only pre-pass and "
-                       "fold when the sequence is split), then chunk_gla_bwd_kernel",
-        }
-        del inp, go, ght, gh, gdo, dq, dk, dv, gws
-        torch.cuda.empty_cache()
-        return blk
-
-    gla = gla_block(GLA_WORKLOAD)
-    gla_long = gla_block(GLA_LONG_WORKLOAD)
-
-    # ------------------------------------------ one instance across ranks
     sharded = None
     if world > 1 and not args.skip_sharded:
         sharded = run_sharded(args, rank, world, max(3, args.steps // 2), 3)
@@ -570,22 +717,28 @@ def run_b200(args):
                                "kind": "port", "sample": gdesc}
 
     if rank == 0:
+        sampler = head.pop("sampler")
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "e4m3 x e4m3 -> fp32 acc, bf16 out", "data": "synthetic",
-            "config": {"workload": args.workload, "G": cfg.G, "M": cfg.M, "K": cfg.K,
-                       "N": cfg.N, "routing": cfg.routing, "empty_groups": cfg.G - g_nz,
-                       "parallelism": f"weak: one workload instance per GPU x{world}",
-                       "l2": "operands (2.1 GB e4m3) exceed L2; no flush"},
-            "roofline": roof,
+            "config": {"workload": HEADLINE, "G": cfg.G, "M": cfg.M, "K": cfg.K, "N": cfg.N,
+                       "routing": configs.routing_desc(cfg),
+                       "parallelism": ("one GPU" if world == 1 else
+                                       f"expert-group shards x{world}, output all-gathered on "
+                                       "every rank inside the matmul epilogue"),
+                       "rows_per_rank": head["rows_per_rank"],
+                       "l2": "operands (0.74 GB e4m3) and output (1.9 GB) exceed L2; no flush"},
+            "roofline": head["roofline"],
+            "compute_only_ms": head["compute_ms"],
+            "gather": head.get("gather"),
             "cpu_baseline": cpu,
-            "e2e": e2e,
+            "e2e": head.get("e2e"),
             "gpu_launches": args.steps,
             "clocks": sampler.summary() if sampler else None,
-            "quantisers": quantisers,
-            "gmm_bwd": gmm_bwd,
+            "moe_up": moe,
+            "small": small,
             "gla": gla,
             "gla_long": gla_long,
             "sharded": sharded,
@@ -598,132 +751,15 @@ def run_b200(args):
 
 
 def run_sharded(args, rank, world, steps, warmup):
-    """Strong scaling of one workload instance across the ranks (N > 1 only):
-    gmm_dense_expert split by expert group (row ranges at 128-row cuts) with
-    an all-gather of the output rows, gla_b1_t32768 split by head with an
-    all-gather of the head blocks.  Compute-only and gather-inclusive device
-    times (max over ranks); rank 0 checks the gathered result against the
-    single-GPU one (GMM: bit for bit; GLA: to rounding, its sequence split
-    differs)."""
+    """Strong scaling of gla_b1_t32768 across the ranks (N > 1 only), split by
+    head with an all-gather of the head blocks.  Compute-only and
+    gather-inclusive device times (max over ranks); rank 0 checks the
+    gathered result against the single-GPU one (to rounding: the sequence
+    split differs with the head count).  The grouped matmul's strong scaling
+    is the headline itself."""
     import torch
     from glaucis_b200 import configs, ops, shard
     res = {}
-    # ------------------------------------------------ GMM by expert group
-    cfg = configs.GMM_CONFIGS["gmm_dense_expert"]
-    lhs, rhs, gs = configs.make_gmm_inputs(cfg, device="cuda", seed=args.seed)
-    sizes = gs.cpu().numpy()
-    parts = shard.gmm_partition(sizes, world)
-    me = parts[rank]
-    counts = [p.rows for p in parts]
-    a_q, a_s = ops.quant_act_1x128(lhs[me.r0:me.r1].contiguous())
-    b_q, b_s = ops.quant_w_128x128(rhs[me.g0:me.g1].contiguous())
-    gs_l = torch.from_numpy(me.sizes).to("cuda")
-    out_l = torch.empty((me.rows, cfg.N), dtype=torch.bfloat16, device="cuda")
-    out_full = torch.empty((sum(counts), cfg.N), dtype=torch.bfloat16, device="cuda")
-
-    def gmm_local():
-        if me.rows:
-            ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs_l, out=out_l)
-
-    def gmm_gathered():
-        gmm_local()
-        shard.all_gather_rows(out_l, counts, out_full)
-
-    c_ms = timed(gmm_local, steps, warmup, world)
-    g_ms = timed(gmm_gathered, steps, warmup, world)
-    flops = 2.0 * float(sizes.sum()) * cfg.K * cfg.N
-    same = None
-    if rank == 0:
-        fa, fs = ops.quant_act_1x128(lhs)
-        fb, fbs = ops.quant_w_128x128(rhs)
-        single = ops.gmm_fp8_fwd(fa, fs, fb, fbs, gs, out_dtype=torch.bfloat16)
-        same = bool(torch.equal(single[: sum(counts)], out_full))
-        single_cmp = single[: sum(counts)].clone()
-        del fa, fs, fb, fbs, single
-    if ops.device_status() != 0:
-        raise SystemExit("device error word set after the sharded GMM")
-    # Overlapped gather without a collective: the rank's rows are multiplied
-    # in row chunks straight into its own IPC-shared output buffer, and each
-    # finished chunk (a contiguous block of rows) goes to every peer's buffer
-    # with one copy-engine transfer per peer over NVLink while the next chunk
-    # is computed; a stream-ordered all-reduce of one int orders the readers.
-    fused = None
-    try:
-        import torch.distributed as dist
-        peers = shard.PeerBuffers(sum(counts), cfg.N)
-        peer_views = [shard.tensor_at(ptr, (sum(counts), cfg.N)) for ptr in peers.ptrs]
-        flag = torch.zeros(1, dtype=torch.int32, device="cuda")
-        plan, _ = ops._plan_chunks(me.sizes, 4, 1024)
-        chunks = [(r0, r1, torch.tensor(sub, dtype=torch.int32, device="cuda"), g_a, len(sub))
-                  for r0, r1, g_a, sub in plan]
-        # one copy stream per peer, so the transfers to different peers run
-        # on different copy engines at the same time
-        s_mm = torch.cuda.Stream()
-        others = [(rank + i) % world for i in range(1, world)]
-        s_cp = {r: torch.cuda.Stream() for r in others}
-
-        def gmm_overlapped():
-            cur = torch.cuda.current_stream()
-            s_mm.wait_stream(cur)
-            for s in s_cp.values():
-                s.wait_stream(cur)
-            for r0, r1, gsub, g_a, ng in chunks:
-                rows = slice(me.r0 + r0, me.r0 + r1)
-                with torch.cuda.stream(s_mm):
-                    ops.gmm_fp8_fwd(a_q[r0:r1], a_s[r0:r1], b_q[g_a:g_a + ng], b_s[g_a:g_a + ng], gsub,
-                                    out=peers.local[rows])
-                    done = s_mm.record_event()
-                for r in others:
-                    with torch.cuda.stream(s_cp[r]):
-                        s_cp[r].wait_event(done)
-                        peer_views[r][rows].copy_(peers.local[rows], non_blocking=True)
-            cur.wait_stream(s_mm)
-            for s in s_cp.values():
-                cur.wait_stream(s)
-            dist.all_reduce(flag)
-
-        f_ms = timed(gmm_overlapped, steps, warmup, world)
-        fsame = bool(torch.equal(single_cmp, peers.local)) if rank == 0 else None
-        fused = {"with_gather_ms": f_ms, "tflops_with_gather": flops / (f_ms * 1e-3) / 1e12,
-                 "matches_single_gpu": fsame, "chunks": len(chunks),
-                 "how": "row-chunked matmul into IPC-shared outputs, one copy-engine transfer per "
-                        "peer per chunk (one stream per peer) overlapping the next chunk, all-reduce "
-                        "barrier"}
-        # One kernel: the matmul's epilogue stages every finished 32-row
-        # slice in shared memory and TMA-stores it into every rank's buffer
-        # (its own and the peers', over NVLink) while the next tile runs.
-        peers.local.zero_()
-        torch.cuda.synchronize()
-        dist.barrier()
-
-        def gmm_scatter():
-            shard.gmm_fp8_fwd_gathered(a_q, a_s, b_q, b_s, me, peers, group_sizes=gs_l)
-
-        x_ms = timed(gmm_scatter, steps, warmup, world)
-        xsame = bool(torch.equal(single_cmp, peers.local)) if rank == 0 else None
-        fused["epilogue_scatter"] = {
-            "with_gather_ms": x_ms, "tflops_with_gather": flops / (x_ms * 1e-3) / 1e12,
-            "matches_single_gpu": xsame,
-            "how": "shard.gmm_fp8_fwd_gathered (gl_gmm_fp8_fwd_scatter): one kernel; each 32x128 "
-                   "output slice is staged in shared memory and TMA-stored to every rank's "
-                   "IPC-shared buffer"}
-        del peer_views
-        peers.close()
-    except Exception as e:  # peer mappings unavailable: report, keep the NCCL rows
-        fused = {"unavailable": f"{type(e).__name__}: {str(e)[:160]}"}
-    if ops.device_status() != 0:
-        raise SystemExit("device error word set after the fused sharded GMM")
-    res["gmm"] = {"workload": "gmm_dense_expert", "split": "expert groups, 128-row cuts",
-                  "rows_per_rank": counts, "groups_per_rank": [p.g1 - p.g0 for p in parts],
-                  "compute_ms": c_ms, "with_gather_ms": g_ms,
-                  "tflops_compute": flops / (c_ms * 1e-3) / 1e12,
-                  "tflops_with_gather": flops / (g_ms * 1e-3) / 1e12,
-                  "gather_bytes_per_rank": 2 * cfg.N * (cfg.M - me.rows),
-                  "matches_single_gpu": same, "fused_gather": fused, "scaling": "strong"}
-    del lhs, rhs, a_q, a_s, b_q, b_s, out_l, out_full
-    if rank == 0:
-        del single_cmp
-    torch.cuda.empty_cache()
     # ------------------------------------------------------- GLA by head
     gcfg = configs.GLA_CONFIGS["gla_b1_t32768"]
     inp = configs.make_gla_inputs(gcfg, device="cuda", seed=args.seed)
@@ -780,9 +816,10 @@ def run_sharded(args, rank, world, steps, warmup):
 
 def run_profile(args):
     """Small-footprint run of one kernel for ncu captures: the GMM on the
-    headline workload with the bf16 weights freed after quantisation (about
-    2.3 GB resident), the two quantisers on a slice of its operands, or the
-    GLA forward on its workload."""
+    --workload grouped-matmul workload (default the headline) with the bf16
+    operands freed after quantisation, the two quantisers on a slice of
+    gmm_moe_up's operands, the grouped-matmul backward on a 16-expert slice
+    of gmm_moe_up, or the GLA forward / backward on its workload."""
     import torch
     from glaucis_b200 import configs, ops
     torch.cuda.set_device(0)
@@ -796,7 +833,7 @@ def run_profile(args):
         out = torch.empty((cfg.M, cfg.N), dtype=torch.bfloat16, device="cuda")
         fn = lambda: ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs, out=out)
     elif args.profile == "quant":
-        # both quantisers on a slice of the headline operands: activations
+        # both quantisers on a slice of gmm_moe_up's operands: activations
         # [16384, 7168] (235 MB bf16) and 16 experts [16, 7168, 2048] (470 MB)
         gen = torch.Generator(device="cuda").manual_seed(args.seed)
         x = torch.randn((16384, 7168), device="cuda", generator=gen).to(torch.bfloat16)
@@ -806,7 +843,7 @@ def run_profile(args):
             ops.quant_act_1x128(x)
             ops.quant_w_128x128(w)
     elif args.profile == "gmm_bwd":
-        # dlhs and tgmm on a 16-expert slice of the headline workload (the
+        # dlhs and tgmm on a 16-expert slice of gmm_moe_up (the
         # same routing, K and N; M = 4096 rows): about 0.9 GB resident
         cfg = configs.GMMConfig("gmm_moe_up_g16", G=16, M=4096, K=7168, N=2048, routing="zipf_topk")
         lhs, rhs, gs = configs.make_gmm_inputs(cfg, device="cuda", seed=args.seed)
@@ -863,7 +900,7 @@ def main(argv=None):
                     help="N > 1: skip the strong-scaling rows (one workload split across ranks)")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
-    ap.add_argument("--cpu-rows", type=int, default=8192,
+    ap.add_argument("--cpu-rows", type=int, default=4096,
                     help="rows of the headline workload in one CPU-baseline step")
     ap.add_argument("--cpu-gla-tokens", type=int, default=4096)
     ap.add_argument("--profile", choices=["gmm", "gmm_bwd", "gla", "gla_bwd", "quant"], default=None,

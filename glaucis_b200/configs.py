@@ -70,6 +70,21 @@ GLA_CONFIGS = {
 }
 
 
+def routing_desc(cfg: GMMConfig) -> str:
+    """One-line statement of how the group sizes of `cfg` are drawn."""
+    if cfg.routing == "zipf_topk":
+        off = max(1, cfg.G // 32)
+        return (f"{cfg.M // cfg.topk} tokens x top-{cfg.topk} distinct experts, p(e) ~ "
+                f"rank^-{cfg.zipf} over a seeded expert permutation, the {off} lowest-ranked "
+                f"experts switched off (p = 0) so that {off} groups are empty")
+    if cfg.routing == "uniform_one_empty":
+        return ("seeded uniform-random composition of M (sorted cut points), one random group "
+                "emptied and its rows spread over the others")
+    if cfg.routing == "multinomial":
+        return f"multinomial(M, uniform 1/{cfg.G})"
+    return cfg.routing
+
+
 # ---------------------------------------------------------------------------
 # Group sizes
 # ---------------------------------------------------------------------------
