@@ -624,7 +624,13 @@ def gla_block(args, workload, rank, world, peaks, peak_kind):
         ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], 128 ** -0.5, 64,
                           g=inp["g"], h0=inp["h0"], output_final_state=True, o=go, ht=ght)
 
+    def gla_exact_step():
+        ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], 128 ** -0.5, 64,
+                          g=inp["g"], h0=inp["h0"], output_final_state=True, o=go, ht=ght,
+                          exact_intra=True)
+
     gla_ms = timed(gla_step, args.steps, args.warmup, world)
+    ex_ms = timed(gla_exact_step, max(5, args.steps // 2), 3, world)
     if ops.device_status() != 0:
         raise SystemExit("device error word set after the GLA timed region")
     gla_bytes = configs.gla_bytes(gcfg.B, gcfg.T, gcfg.H, has_h0=gcfg.h0_std > 0)
@@ -638,7 +644,14 @@ def gla_block(args, workload, rank, world, peaks, peak_kind):
                         "bf16_tensor_frac": gla_flops / (gla_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
                         "kernel": "chunk_gla_fwd_kernel", "peak_source": f"{peak_kind} hbm_gbs",
                         "algorithmic_bytes_per_step": gla_bytes,
-                        "traffic": ncu_traffic("chunk_gla_fwd_kernel", workload)}}
+                        "traffic": ncu_traffic("chunk_gla_fwd_kernel", workload)},
+           "precision": "tril(A) enters the intra-chunk product as one bf16 operand (the jnp "
+                        "oracle's einsum at TPU default precision)",
+           "exact_intra": {"ms_per_step": ex_ms,
+                           "tokens_per_s": world * gcfg.B * gcfg.T / (ex_ms * 1e-3),
+                           "hbm_frac": gla_bytes / (ex_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                           "precision": "tril(A) as a bf16 hi + lo pair (~2^-17 relative): the "
+                                        "fp32 A of the template's output kernel"}}
     # backward: the training forward (o, ht and the per-chunk states h) and the
     # backward (reverse state-gradient scan + chunk-parallel dq/dk/dv kernel)
     # on a synthetic output gradient, buffers resident

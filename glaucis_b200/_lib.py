@@ -20,6 +20,7 @@ GL_ELAUNCH = -2
 GL_EDEVICE = -3
 GL_OUT_BF16 = 0
 GL_OUT_F32 = 1
+GL_GLA_EXACT_INTRA = 1
 DEV_CODES = {0: "ok", 1: "device wait timed out", 2: "invalid group_sizes (negative or sum > M)"}
 
 # (name, restype, argtypes) for every symbol the header declares.
@@ -35,6 +36,8 @@ SIGNATURES = {
                                  _P, _P, _P, ctypes.c_size_t, _P, _P]),
     "gl_chunk_gla_fwd_states": (_I, [_P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64,
                                      _I64, _P, _P, _P, _P, ctypes.c_size_t, _P, _P]),
+    "gl_chunk_gla_fwd_ex": (_I, [_P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64, _I64,
+                                 _P, _P, _P, _P, ctypes.c_size_t, _I, _P, _P]),
     "gl_chunk_gla_fwd_intermediates": (_I, [_P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64, _P,
                                             _P, _P, _P]),
     "gl_chunk_gla_bwd_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I64, _I64]),

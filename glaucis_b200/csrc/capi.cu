@@ -27,7 +27,8 @@ int gl_launch_gmm_fp8(const void* a_q, const float* a_s, const void* b_q, const 
 int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float* g,
                         const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
                         int64_t H, int64_t K, int64_t V, void* o, float* ht, void* h_out, void* ws,
-                        size_t ws_bytes, int* err, cudaStream_t st, int num_sms, const char** why);
+                        size_t ws_bytes, int p_split, int* err, cudaStream_t st, int num_sms,
+                        const char** why);
 size_t gl_chunk_gla_ws_bytes(int64_t B, int64_t T, int64_t H, int num_sms);
 int gl_launch_gmm_fp8_multi(const void* a_q, const float* a_s, const void* b_q, const float* b_s,
                             const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
@@ -383,21 +384,8 @@ int gl_chunk_gla_fwd_ws(const void* q, const void* k, const void* v, const float
                         const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
                         int64_t H, int64_t K, int64_t V, int64_t chunk_size, void* o, float* ht,
                         void* workspace, size_t workspace_bytes, int* err_word, void* stream) {
-  if (int rc = chunk_gla_check("gl_chunk_gla_fwd", q, k, v, g, g_gamma, h0, B, T, H, K, V,
-                               chunk_size, o, ht))
-    return rc;
-  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
-    return fail(GL_EINVAL, "gl_chunk_gla_fwd_ws: workspace must be 256-byte aligned");
-  DeviceState* d = nullptr;
-  if (int rc = device_state(&d)) return rc;
-  const char* why = "";
-  const int rc = gl_launch_chunk_gla(q, k, v, g, g_gamma, h0, scale, B, T, H, K, V, o, ht,
-                                     nullptr, workspace, workspace ? workspace_bytes : 0,
-                                     err_word ? err_word : d->err,
-                                     static_cast<cudaStream_t>(stream), d->num_sms, &why);
-  if (rc == -1) return fail(GL_EINVAL, std::string("gl_chunk_gla_fwd: ") + why);
-  if (rc != 0) return fail(GL_ELAUNCH, std::string("gl_chunk_gla_fwd: ") + why);
-  return GL_OK;
+  return gl_chunk_gla_fwd_ex(q, k, v, g, g_gamma, h0, scale, B, T, H, K, V, chunk_size, o, ht,
+                             nullptr, workspace, workspace_bytes, 0, err_word, stream);
 }
 
 int gl_chunk_gla_fwd(const void* q, const void* k, const void* v, const float* g,
@@ -427,11 +415,25 @@ int gl_chunk_gla_fwd_states(const void* q, const void* k, const void* v, const f
                             int64_t T, int64_t H, int64_t K, int64_t V, int64_t chunk_size,
                             void* o, float* ht, void* h_states, void* workspace,
                             size_t workspace_bytes, int* err_word, void* stream) {
-  const char* f = "gl_chunk_gla_fwd_states";
+  if (!h_states)
+    return fail(GL_EINVAL, "gl_chunk_gla_fwd_states: h_states must be a 16-byte aligned pointer");
+  return gl_chunk_gla_fwd_ex(q, k, v, g, g_gamma, h0, scale, B, T, H, K, V, chunk_size, o, ht,
+                             h_states, workspace, workspace_bytes, 0, err_word, stream);
+}
+
+int gl_chunk_gla_fwd_ex(const void* q, const void* k, const void* v, const float* g,
+                        const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
+                        int64_t H, int64_t K, int64_t V, int64_t chunk_size, void* o, float* ht,
+                        void* h_states, void* workspace, size_t workspace_bytes, int flags,
+                        int* err_word, void* stream) {
+  const char* f = h_states ? "gl_chunk_gla_fwd_states" : "gl_chunk_gla_fwd";
   if (int rc = chunk_gla_check(f, q, k, v, g, g_gamma, h0, B, T, H, K, V, chunk_size, o, ht))
     return rc;
-  if (!h_states || !aligned16(h_states)) return fail(GL_EINVAL, std::string(f) + ": h_states must be a 16-byte aligned pointer");
-  if (!gla_states_fit(B, T, H)) return fail(GL_EINVAL, std::string(f) + ": B*T/64*H*128 must fit in 31 bits");
+  if (flags & ~GL_GLA_EXACT_INTRA) return fail(GL_EINVAL, std::string(f) + ": unknown flags");
+  if (h_states && !aligned16(h_states))
+    return fail(GL_EINVAL, std::string(f) + ": h_states must be a 16-byte aligned pointer");
+  if (h_states && !gla_states_fit(B, T, H))
+    return fail(GL_EINVAL, std::string(f) + ": B*T/64*H*128 must fit in 31 bits");
   if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return fail(GL_EINVAL, std::string(f) + ": workspace must be 256-byte aligned");
   DeviceState* d = nullptr;
@@ -439,6 +441,7 @@ int gl_chunk_gla_fwd_states(const void* q, const void* k, const void* v, const f
   const char* why = "";
   const int rc = gl_launch_chunk_gla(q, k, v, g, g_gamma, h0, scale, B, T, H, K, V, o, ht,
                                      h_states, workspace, workspace ? workspace_bytes : 0,
+                                     (flags & GL_GLA_EXACT_INTRA) ? 1 : 0,
                                      err_word ? err_word : d->err,
                                      static_cast<cudaStream_t>(stream), d->num_sms, &why);
   if (rc == -1) return fail(GL_EINVAL, std::string(f) + ": " + why);

@@ -118,6 +118,11 @@ struct Params {
   // ht_seg: the segment whose final state is written to ht.
   int c_first, rec_base, ht_seg;
   int has_hout;  // FWD: write h_n (bf16, [B,NT,H,K,V]) through tm_h; DH: E_n (always)
+  // FWD: 1 computes tril(A) V as P_hi V + P_lo V (P_hi = bf16(tril(A)),
+  // P_lo = bf16(tril(A) - P_hi), ~2^-17 relative: the fp32 A of the
+  // template's output kernel); 0 feeds the tensor core bf16(tril(A)) only
+  // (the bf16 operands of the reference jnp einsum at TPU default precision).
+  int p_split;
   float* ws_h;
   float* ws_d;
   int B, T, H, nsplit;
@@ -144,7 +149,8 @@ enum {
   B_DRAIN = 30,
   B_GSYNC = 31,      // [2] gating quarter sums written
   B_HST = 33,        // the TMA store of the previous state tile has read shared memory
-  NUM_BARS = 34
+  B_P_READ = 34,     // P_hi V committed (the P buffer may take P_lo) -> state
+  NUM_BARS = 35
 };
 static_assert(NUM_BARS * 8 <= 512, "barrier area");
 
@@ -234,6 +240,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&bar[B_S_EMPTY + i], STATE_WARPS);
     }
     mbar_init(&bar[B_P_FULL], STATE_WARPS);
+    mbar_init(&bar[B_P_READ], 1);
     mbar_init(&bar[B_H_FULL], STATE_WARPS);
     mbar_init(&bar[B_DRAIN], 1);
     mbar_init(&bar[B_HST], 1);
@@ -316,13 +323,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   sdesc(h_addr + kk * 2048, 16384, 1024, kSwizzle128B), CF::IDESC_O, kk > 0);
         }
       };
-      auto issue_o_p = [&](int n) {
+      // P V; with p_split in two parts through the one P buffer, P_hi =
+      // bf16(tril(A)) then P_lo = bf16(tril(A) - P_hi), so that the product
+      // sees A to ~2^-17 relative.  `last`: the part that completes O_n.
+      auto issue_o_p = [&](int n, bool last) {
         const int s = n & 1;
         const uint32_t v_addr = s_base + CF::OFF_V + (n % QS) * CF::V_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           mma_f16(tmem + CF::COL_O + s * VS, sdesc(p_addr + kk * 32, 16, 1024, kSwizzle128B),
                   sdesc(v_addr + kk * 2048, 8192, 1024, kSwizzle128B), CF::IDESC_O, 1);
+        }
+        if (!last) {
+          tc_commit(&bar[B_P_READ]);
+          return;
         }
         tc_commit(&bar[B_O_FULL + s]);
         tc_commit(&bar[B_QKV_EMPTY + n % QS]);
@@ -348,14 +362,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       } else {
         int na = 0, nh = 0, no = 0;
+        bool lo = false;  // p_split: P_hi V of chunk `no` issued, P_lo V next
         uint64_t t0 = global_ns();
         uint32_t spins = 0;
         while (no < NT) {
           bool progressed = false;
-          if (no < nh && mbar_test(&bar[B_P_FULL], no & 1)) {
+          // P_FULL completes once per chunk, or with p_split twice: P_hi
+          // (parity 0) and P_lo (parity 1)
+          const uint32_t pph = p.p_split ? (lo ? 1u : 0u) : static_cast<uint32_t>(no & 1);
+          if (no < nh && mbar_test(&bar[B_P_FULL], pph)) {
             tc_fence_after();
-            issue_o_p(no);
-            ++no;
+            const bool last = !p.p_split || lo;
+            issue_o_p(no, last);
+            if (last) ++no;
+            if (p.p_split) lo = !lo;
             progressed = true;
           }
           if (nh < na && nh == no && mbar_test(&bar[B_H_FULL], nh & 1) &&
@@ -637,17 +657,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ++nstore;
       return true;
     };
-    // P = tril(A_m) in bf16, K-major (row = query, 128 B).
-    auto p_epilogue = [&](int m) -> bool {
+    // P = tril(A_m) in bf16, K-major (row = query, 128 B).  With p_split in
+    // two parts through the one P buffer: lo = false writes P_hi =
+    // bf16(tril(A_m)); lo = true, once P_hi V has read the buffer
+    // (B_P_READ), writes P_lo = bf16(tril(A_m) - P_hi) from A_m read again
+    // out of TMEM.  The A buffer is released by the last part.
+    auto p_epilogue = [&](int m, bool lo) -> bool {
       const int s = m & 1;
-      if (!mbar_wait(&bar[B_A_FULL + s], (m >> 1) & 1, ab)) return false;
+      if (!lo && !mbar_wait(&bar[B_A_FULL + s], (m >> 1) & 1, ab)) return false;
+      if (lo && !mbar_wait(&bar[B_P_READ], m & 1, ab)) return false;
       tc_fence_after();
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t a[32];
         tmem_ld32(lane_addr + CF::COL_A + s * 64 + half * 32, a);
         tmem_ld_wait(a);
-        if (half == 1) {
+        if ((lo || !p.p_split) && half == 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bar[B_A_EMPTY + s]);
@@ -660,7 +685,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               const int j = half * 32 + c4 * 8 + e;
-              f[e] = j <= prow ? __uint_as_float(a[c4 * 8 + e]) : 0.f;
+              const float x = j <= prow ? __uint_as_float(a[c4 * 8 + e]) : 0.f;
+              f[e] = lo ? x - __bfloat162float(__float2bfloat16_rn(x)) : x;
             }
             const uint32_t ch = static_cast<uint32_t>(half * 4 + c4) ^ (prow & 7);
             *reinterpret_cast<uint4*>(pp + (ch << 4)) =
@@ -675,7 +701,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       return true;
     };
     bool ok = true;
-    if (!kStateOnly) ok = store_h(0) && p_epilogue(0);
+    if (!kStateOnly) ok = store_h(0) && p_epilogue(0, false) && (!p.p_split || p_epilogue(0, true));
     for (int n = 0; n < NT && ok; ++n) {
       const int s = n & 1;
       const uint32_t ph2 = (n >> 1) & 1;
@@ -721,10 +747,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) mbar_arrive(&bar[B_S_EMPTY + n % NS]);
       if (kStateOnly) continue;
       // O_n done -> H and P may be rewritten for chunk n+1 (the next O
-      // accumulates into the other TMEM buffer meanwhile)
+      // accumulates into the other TMEM buffer meanwhile).  P_lo follows
+      // P_hi as soon as P_hi V has read the buffer.
       if (!mbar_wait(&bar[B_O_FULL + s], ph2, ab)) { ok = false; break; }
       tc_fence_after();
-      if (n + 1 < NT && !(store_h(n + 1) && p_epilogue(n + 1))) { ok = false; break; }
+      if (n + 1 < NT && !(store_h(n + 1) && p_epilogue(n + 1, false) &&
+                          (!p.p_split || p_epilogue(n + 1, true)))) {
+        ok = false;
+        break;
+      }
     }
     if (st_issuer && p.has_hout) bulk_wait<0>();
     if (ok && (kMode == MODE_FWD_STATE || kMode == MODE_DH_STATE)) {
@@ -1022,9 +1053,10 @@ size_t gl_chunk_gla_ws_bytes(int64_t B, int64_t T, int64_t H, int num_sms) {
 static int gla_dispatch(const void* q, const void* kslot, const void* vslot, const float* g,
                         const float* g_gamma, const float* init, float scale, int64_t B,
                         int64_t T, int64_t H, void* o, float* fin, void* sout, void* ws,
-                        size_t ws_bytes, int* err, bool rev, cudaStream_t st, int num_sms,
-                        const char** why) {
+                        size_t ws_bytes, int* err, bool rev, int p_split, cudaStream_t st,
+                        int num_sms, const char** why) {
   gl::gla::Params p;
+  p.p_split = rev ? 0 : p_split;
   p.g_gamma = g_gamma;
   p.h0 = init;
   p.o = static_cast<__nv_bfloat16*>(o);
@@ -1069,11 +1101,12 @@ static int gla_dispatch(const void* q, const void* kslot, const void* vslot, con
 int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float* g,
                         const float* g_gamma, const float* h0, float scale, int64_t B, int64_t T,
                         int64_t H, int64_t K, int64_t V, void* o, float* ht, void* h_out, void* ws,
-                        size_t ws_bytes, int* err, cudaStream_t st, int num_sms, const char** why) {
+                        size_t ws_bytes, int p_split, int* err, cudaStream_t st, int num_sms,
+                        const char** why) {
   (void)K;
   (void)V;
   return gla_dispatch(q, k, v, g, g_gamma, h0, scale, B, T, H, o, ht, h_out, ws, ws_bytes, err,
-                      false, st, num_sms, why);
+                      false, p_split, st, num_sms, why);
 }
 
 // Reverse state-gradient scan of the backward: E_n (bf16 [B,NT,H,K,V]) for
@@ -1083,5 +1116,5 @@ int gl_launch_chunk_gla_dh(const void* q, const void* dout, const float* g, cons
                            void* e_out, float* dh0, void* ws, size_t ws_bytes, int* err,
                            cudaStream_t st, int num_sms, const char** why) {
   return gla_dispatch(nullptr, q, dout, g, g_gamma, dht, scale, B, T, H, nullptr, dh0, e_out, ws,
-                      ws_bytes, err, true, st, num_sms, why);
+                      ws_bytes, err, true, 0, st, num_sms, why);
 }

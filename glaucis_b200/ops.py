@@ -454,7 +454,7 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                   g_gamma: Optional[torch.Tensor], scale: float, chunk_size: int = 64, *,
                   g: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
                   output_final_state: bool = False, output_states: bool = False,
-                  output_intermediates: bool = False,
+                  output_intermediates: bool = False, exact_intra: bool = False,
                   o: Optional[torch.Tensor] = None,
                   ht: Optional[torch.Tensor] = None,
                   h: Optional[torch.Tensor] = None) -> GLAForward:
@@ -467,8 +467,13 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     residual of the backward.  output_intermediates=True also returns
     g_cumsum (fp32 [B, T, H, K]) and the unmasked intra-chunk A (fp32
     [B, T, H, 64]) as the reference's first two outputs, computed by a
-    separate fp32 kernel (one more pass over q, k and g).  o, ht and h may
-    be given preallocated.
+    separate fp32 kernel (one more pass over q, k and g).
+    exact_intra=True feeds tril(A) to the intra-chunk product as a bf16
+    hi + lo pair (A to ~2^-17 relative, the fp32 A of the template's output
+    kernel, chunk_gla.py:208-212) instead of one bf16 rounding (the operand
+    precision of the reference jnp oracle's einsum at TPU default precision,
+    chunk_gla_ref.py:96-97); it is slower.  o, ht and h may be given
+    preallocated.
     """
     B, T, H, K, V = _gla_check(q, k, v, g_gamma, g, h0)
     if o is None:
@@ -482,17 +487,13 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
     if output_states:
         h = _out(h, (B, T // chunk_size, H, K, V), torch.bfloat16, q.device, "h")
-        _lib.check(lib.gl_chunk_gla_fwd_states(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
-                                               _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
-                                               chunk_size, o.data_ptr(), _ptr(ht), h.data_ptr(),
-                                               _ptr(ws), ws_bytes, None, _stream()),
-                   "gl_chunk_gla_fwd_states")
-    else:
-        _lib.check(lib.gl_chunk_gla_fwd_ws(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
-                                           _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
-                                           chunk_size, o.data_ptr(), _ptr(ht), _ptr(ws), ws_bytes,
-                                           None, _stream()),
-                   "gl_chunk_gla_fwd")
+    flags = _lib.GL_GLA_EXACT_INTRA if exact_intra else 0
+    _lib.check(lib.gl_chunk_gla_fwd_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
+                                       _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
+                                       chunk_size, o.data_ptr(), _ptr(ht),
+                                       h.data_ptr() if output_states else None, _ptr(ws), ws_bytes,
+                                       flags, None, _stream()),
+               "gl_chunk_gla_fwd_states" if output_states else "gl_chunk_gla_fwd")
     g_cumsum = A = None
     if output_intermediates:
         g_cumsum = torch.empty((B, T, H, K), dtype=torch.float32, device=q.device)
@@ -558,8 +559,9 @@ class _ChunkGLA(torch.autograd.Function):
     dq, dk, dv (and dh0 when h0 is given)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, g_gamma, g, h0, scale, chunk_size):
-        res = chunk_gla_fwd(q, k, v, g_gamma, scale, chunk_size, g=g, h0=h0, output_states=True)
+    def forward(ctx, q, k, v, g_gamma, g, h0, scale, chunk_size, exact_intra):
+        res = chunk_gla_fwd(q, k, v, g_gamma, scale, chunk_size, g=g, h0=h0, output_states=True,
+                            exact_intra=exact_intra)
         ctx.save_for_backward(q, k, v, g_gamma, g, res.h)
         ctx.scale, ctx.chunk_size, ctx.has_h0 = scale, chunk_size, h0 is not None
         return res.o
@@ -569,18 +571,19 @@ class _ChunkGLA(torch.autograd.Function):
         q, k, v, g_gamma, g, h = ctx.saved_tensors
         dq, dk, dv, dh0 = chunk_gla_bwd(q, k, v, do.to(torch.bfloat16).contiguous(), h, g_gamma,
                                         ctx.scale, ctx.chunk_size, g=g, output_dh0=ctx.has_h0)
-        return dq, dk, dv, None, None, dh0, None, None
+        return dq, dk, dv, None, None, dh0, None, None, None
 
 
 def chunk_gla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g_gamma: Optional[torch.Tensor],
               scale: float, chunk_size: int = 64, *, g: Optional[torch.Tensor] = None,
-              h0: Optional[torch.Tensor] = None) -> torch.Tensor:
+              h0: Optional[torch.Tensor] = None, exact_intra: bool = False) -> torch.Tensor:
     """`chunk_gla(q, k, v, g_gamma, scale, chunk_size)`
     (KE/examples/kernels/chunk_gla.py:434-456): returns o (bf16),
-    differentiable in q, k, v (and h0) when any of them requires grad."""
+    differentiable in q, k, v (and h0) when any of them requires grad.
+    exact_intra as in chunk_gla_fwd."""
     if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (q, k, v, h0)):
-        return _ChunkGLA.apply(q, k, v, g_gamma, g, h0, scale, chunk_size)
-    return chunk_gla_fwd(q, k, v, g_gamma, scale, chunk_size, g=g, h0=h0).o
+        return _ChunkGLA.apply(q, k, v, g_gamma, g, h0, scale, chunk_size, exact_intra)
+    return chunk_gla_fwd(q, k, v, g_gamma, scale, chunk_size, g=g, h0=h0, exact_intra=exact_intra).o
 
 
 def device_status() -> int:

@@ -38,6 +38,16 @@ def value_slice(request, monkeypatch):
     return request.param
 
 
+@pytest.fixture(autouse=True, params=["bf16_p", "exact_intra"])
+def intra_precision(request, monkeypatch):
+    """... and in both precisions of the intra-chunk product: tril(A) as one
+    bf16 operand (the default) and as a bf16 hi + lo pair (exact_intra)."""
+    if request.param == "exact_intra":
+        import functools
+        monkeypatch.setattr(ops, "chunk_gla_fwd", functools.partial(ops.chunk_gla_fwd, exact_intra=True))
+    return request.param
+
+
 def _run(cuda, cfg: configs.GLAConfig, seed=0):
     inp = configs.make_gla_inputs(cfg, device="cpu", seed=seed)
     dev = {k: (v.to(cuda) if v is not None else None) for k, v in inp.items()}
@@ -153,3 +163,24 @@ def test_gla_random_shapes(cuda, monkeypatch, seed):
     if rng.random() < 0.5:
         monkeypatch.setenv("GLAUCIS_GLA_SEGMENTS", str(int(rng.integers(2, 6))))
     _check(*_run(cuda, cfg, seed=seed), f"random {cfg}")
+
+
+def test_exact_intra_is_closer_to_the_fp32_product(cuda, intra_precision):
+    # exact_intra removes the bf16 rounding of tril(A) from the intra-chunk
+    # product: against the fp32 oracle its error must not exceed the
+    # default's, and both hold the forward tolerance.
+    if intra_precision != "bf16_p":
+        pytest.skip("compares the two precisions itself")
+    cfg = configs.GLAConfig("t", B=2, T=512, H=4, h0_std=0.1)
+    inp = configs.make_gla_inputs(cfg, device="cpu", seed=13)
+    d = {k: (v.to(cuda) if v is not None else None) for k, v in inp.items()}
+    f = lambda t: None if t is None else t.float().numpy()  # noqa: E731
+    ref_o, _ = O.chunk_gla_fwd(f(inp["q"]), f(inp["k"]), f(inp["v"]), g=f(inp["g"]), h0=f(inp["h0"]))
+    errs = {}
+    for exact in (False, True):
+        o = ops.chunk_gla_fwd(d["q"], d["k"], d["v"], None, 128 ** -0.5, 64, g=d["g"], h0=d["h0"],
+                              exact_intra=exact).o.float().cpu().numpy()
+        assert ops.device_status() == 0
+        assert_close(o, ref_o, RTOL, ATOL_FRAC, what=f"exact_intra={exact}")
+        errs[exact] = rel_fro(o, ref_o)
+    assert errs[True] <= errs[False] * 1.02, errs

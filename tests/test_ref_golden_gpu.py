@@ -44,15 +44,16 @@ def _small_inputs(cuda, d):
             t(d.get("g_gamma")), t(d.get("h0")), to_bf16(d["do_bf16"]), t(d.get("dht")))
 
 
+@pytest.mark.parametrize("exact", [False, True])
 @pytest.mark.parametrize("vs", ["64", "128"])
 @pytest.mark.parametrize("name", ["ref_gla_gamma_small.npz", "ref_gla_gk_h0_small.npz"])
-def test_forward_and_intermediates_match_reference_code(cuda, name, vs, monkeypatch):
+def test_forward_and_intermediates_match_reference_code(cuda, name, vs, exact, monkeypatch):
     monkeypatch.setenv("GLAUCIS_GLA_VS", vs)
     d = load(name)
     q, k, v, g, gg, h0, _, _ = _small_inputs(cuda, d)
     C, scale = int(d["chunk_size"]), float(d["scale"])
     res = ops.chunk_gla_fwd(q, k, v, gg, scale, C, g=g, h0=h0, output_final_state=True,
-                            output_states=True, output_intermediates=True)
+                            output_states=True, output_intermediates=True, exact_intra=exact)
     assert ops.device_status() == 0
     f = lambda x: x.float().cpu().numpy()  # noqa: E731
     _check(f(res.o), d["o"], 2e-2, 3e-2, 1e-2, f"{name} o")
@@ -79,13 +80,14 @@ def test_backward_matches_reference_code(cuda, name):
             _check(f(got), d[key], 2e-2, 6e-2, 1.5e-2, f"{name} {key}")
 
 
+@pytest.mark.parametrize("exact", [False, True])
 @pytest.mark.parametrize("name", ["ref_gla_b8_t4096_head.npz", "ref_gla_b1_t32768_head.npz"])
-def test_full_size_head_matches_reference_code(cuda, name):
+def test_full_size_head_matches_reference_code(cuda, name, exact):
     d = load(name)
     cfg, inp, b, h = regenerate_head(d)
     dev = {kk: (vv.to(cuda) if vv is not None else None) for kk, vv in inp.items()}
     res = ops.chunk_gla_fwd(dev["q"], dev["k"], dev["v"], None, cfg.K ** -0.5, cfg.C, g=dev["g"],
-                            h0=dev["h0"], output_final_state=True)
+                            h0=dev["h0"], output_final_state=True, exact_intra=exact)
     assert ops.device_status() == 0
     rows = torch.from_numpy(d["rows"]).to(cuda)
     got_o = res.o[b, :, h].index_select(0, rows).float().cpu().numpy()
