@@ -118,10 +118,11 @@ struct Params {
   // ht_seg: the segment whose final state is written to ht.
   int c_first, rec_base, ht_seg;
   int has_hout;  // FWD: write h_n (bf16, [B,NT,H,K,V]) through tm_h; DH: E_n (always)
-  // FWD: 1 computes tril(A) V as P_hi V + P_lo V (P_hi = bf16(tril(A)),
-  // P_lo = bf16(tril(A) - P_hi), ~2^-17 relative: the fp32 A of the
-  // template's output kernel); 0 feeds the tensor core bf16(tril(A)) only
-  // (the bf16 operands of the reference jnp einsum at TPU default precision).
+  // FWD: 1 selects the kSplit instance of the kernel, which computes
+  // tril(A) V as P_hi V + P_lo V (P_hi = bf16(tril(A)), P_lo =
+  // bf16(tril(A) - P_hi), ~2^-17 relative: the fp32 A of the template's
+  // output kernel); 0 feeds the tensor core bf16(tril(A)) only (the bf16
+  // operands of the reference jnp einsum at TPU default precision).
   int p_split;
   float* ws_h;
   float* ws_d;
@@ -172,7 +173,7 @@ __device__ __forceinline__ uint32_t kmaj_off(uint32_t row, uint32_t col, uint32_
          (col & 7u) * 2u;
 }
 
-template <int VS, int kMode>
+template <int VS, int kMode, bool kSplit>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     chunk_gla_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
@@ -369,13 +370,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           bool progressed = false;
           // P_FULL completes once per chunk, or with p_split twice: P_hi
           // (parity 0) and P_lo (parity 1)
-          const uint32_t pph = p.p_split ? (lo ? 1u : 0u) : static_cast<uint32_t>(no & 1);
+          const uint32_t pph = kSplit ? (lo ? 1u : 0u) : static_cast<uint32_t>(no & 1);
           if (no < nh && mbar_test(&bar[B_P_FULL], pph)) {
             tc_fence_after();
-            const bool last = !p.p_split || lo;
+            const bool last = !kSplit || lo;
             issue_o_p(no, last);
             if (last) ++no;
-            if (p.p_split) lo = !lo;
+            if (kSplit) lo = !lo;
             progressed = true;
           }
           if (nh < na && nh == no && mbar_test(&bar[B_H_FULL], nh & 1) &&
@@ -672,7 +673,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t a[32];
         tmem_ld32(lane_addr + CF::COL_A + s * 64 + half * 32, a);
         tmem_ld_wait(a);
-        if ((lo || !p.p_split) && half == 1) {
+        if ((lo || !kSplit) && half == 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bar[B_A_EMPTY + s]);
@@ -686,7 +687,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int e = 0; e < 8; ++e) {
               const int j = half * 32 + c4 * 8 + e;
               const float x = j <= prow ? __uint_as_float(a[c4 * 8 + e]) : 0.f;
-              f[e] = lo ? x - __bfloat162float(__float2bfloat16_rn(x)) : x;
+              f[e] = (kSplit && lo) ? x - __bfloat162float(__float2bfloat16_rn(x)) : x;
             }
             const uint32_t ch = static_cast<uint32_t>(half * 4 + c4) ^ (prow & 7);
             *reinterpret_cast<uint4*>(pp + (ch << 4)) =
@@ -701,7 +702,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       return true;
     };
     bool ok = true;
-    if (!kStateOnly) ok = store_h(0) && p_epilogue(0, false) && (!p.p_split || p_epilogue(0, true));
+    if (!kStateOnly) ok = store_h(0) && p_epilogue(0, false) && (!kSplit || p_epilogue(0, true));
     for (int n = 0; n < NT && ok; ++n) {
       const int s = n & 1;
       const uint32_t ph2 = (n >> 1) & 1;
@@ -752,7 +753,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!mbar_wait(&bar[B_O_FULL + s], ph2, ab)) { ok = false; break; }
       tc_fence_after();
       if (n + 1 < NT && !(store_h(n + 1) && p_epilogue(n + 1, false) &&
-                          (!p.p_split || p_epilogue(n + 1, true)))) {
+                          (!kSplit || p_epilogue(n + 1, true)))) {
         ok = false;
         break;
       }
@@ -897,15 +898,17 @@ static size_t gla_ws_bytes(int64_t B, int64_t H, int nseg) {
   return ((hb + 255) / 256) * 256 + rec * 128 * 4;
 }
 
-template <int VS, int kMode>
+template <int VS, int kMode, bool kSplit = false>
 static int launch_pass(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                        const CUtensorMap& tg, const CUtensorMap& th, const gl::gla::Params& p,
                        int grid, cudaStream_t st, const char** why) {
+  if constexpr (kMode == gl::gla::MODE_FWD && !kSplit) {
+    if (p.p_split) return launch_pass<VS, kMode, true>(tq, tk, tv, tg, th, p, grid, st, why);
+  }
   using CF = gl::gla::Cfg<VS>;
-  if (!gl_set_smem_attr(reinterpret_cast<const void*>(gl::gla::chunk_gla_fwd_kernel<VS, kMode>), 0,
-                        static_cast<int>(CF::SMEM_BYTES), why))
-    return -2;
-  gl::gla::chunk_gla_fwd_kernel<VS, kMode><<<grid, gl::gla::NUM_THREADS, CF::SMEM_BYTES, st>>>(
+  const void* fn = reinterpret_cast<const void*>(gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit>);
+  if (!gl_set_smem_attr(fn, 0, static_cast<int>(CF::SMEM_BYTES), why)) return -2;
+  gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit><<<grid, gl::gla::NUM_THREADS, CF::SMEM_BYTES, st>>>(
       tq, tk, tv, tg, th, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
