@@ -458,11 +458,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(tok0) + m * C + orow;
       uint4* dst = reinterpret_cast<uint4*>(p.o + (row * H + h) * 128 + v0 + ohalf * OC);
-#pragma unroll
-      for (int j = 0; j < OC; j += 32) {
-        uint32_t ov[32];
-        tmem_ld32(o_lane + s * VS + j, ov);
-        tmem_ld_wait(ov);
+      auto store32 = [&](const uint32_t (&ov)[32], int j) {
         if (lane < 16) {
 #pragma unroll
           for (int i = 0; i < 4; ++i)
@@ -472,6 +468,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 pack_bf16x2(__uint_as_float(ov[8 * i + 4]), __uint_as_float(ov[8 * i + 5])),
                 pack_bf16x2(__uint_as_float(ov[8 * i + 6]), __uint_as_float(ov[8 * i + 7])));
         }
+      };
+      if constexpr (OC == 64) {
+        // both column halves in flight before one wait
+        uint32_t ov0[32], ov1[32];
+        tmem_ld32(o_lane + s * VS, ov0);
+        tmem_ld32(o_lane + s * VS + 32, ov1);
+        tmem_ld_wait2(ov0, ov1);
+        store32(ov0, 0);
+        store32(ov1, 32);
+      } else {
+        uint32_t ov[32];
+        tmem_ld32(o_lane + s * VS, ov);
+        tmem_ld_wait(ov);
+        store32(ov, 0);
       }
       tc_fence_before();
       __syncwarp();
@@ -484,7 +494,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t ph2 = (n >> 1) & 1;
       if (p.has_g && !mbar_wait(&bar[B_G_FULL], n & 1, ab)) { gok = false; break; }
       if (!mbar_wait(&bar[B_QKV_FULL + n % CF::QS], (n / CF::QS) & 1, ab)) { gok = false; break; }
-      if (!mbar_wait(&bar[B_DEC_EMPTY + s], ph2 ^ 1, ab)) { gok = false; break; }
       uint8_t* qs = smem + CF::OFF_Q + (n % CF::QS) * CF::Q_BYTES + qk_atom + qk_sub;
       uint8_t* ks = smem + CF::OFF_K + (n % CF::QS) * CF::Q_BYTES + qk_atom + qk_sub;
       float4 gv[8];
@@ -521,6 +530,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float2 L2 = make_float2(kLog2e, kLog2e), NL2 = make_float2(-kLog2e, -kLog2e);
       const float2 LS2 = make_float2(log2_scale, log2_scale);
       float2 G01 = make_float2(G.x, G.y), G23 = make_float2(G.z, G.w);
+      // The 8 tokens' q and k are read before any of them is written back,
+      // so the loads do not queue behind the stores of earlier tokens.
+      uint2 qv[8], kv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int t = gw * 8 + i;
+        const uint32_t off = static_cast<uint32_t>(t) * 128u + ((qk_chunk ^ (t & 7)) << 4);
+        if (!kStateOnly) qv[i] = *reinterpret_cast<const uint2*>(qs + off);
+        kv[i] = *reinterpret_cast<const uint2*>(ks + off);
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int t = gw * 8 + i;
@@ -546,7 +565,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!kStateOnly) {
           const float2 a01 = make_float2(ex2_approx(xa01.x), ex2_approx(xa01.y));
           const float2 a23 = make_float2(ex2_approx(xa23.x), ex2_approx(xa23.y));
-          const uint2 q2 = *reinterpret_cast<const uint2*>(qs + off);
+          const uint2 q2 = qv[i];
           float2 q01 = __fmul2_rn(bf16x2_f32x2(q2.x), a01), q23 = __fmul2_rn(bf16x2_f32x2(q2.y), a23);
           if (p.scale_apart) {
             q01 = __fmul2_rn(q01, make_float2(p.scale, p.scale));
@@ -555,7 +574,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           *reinterpret_cast<uint2*>(qs + off) =
               make_uint2(pack_bf16x2(q01.x, q01.y), pack_bf16x2(q23.x, q23.y));
         }
-        const uint2 k2 = *reinterpret_cast<const uint2*>(ks + off);
+        const uint2 k2 = kv[i];
         float2 k01 = __fmul2_rn(bf16x2_f32x2(k2.x), b01), k23 = __fmul2_rn(bf16x2_f32x2(k2.y), b23);
         if (kRev && p.scale_apart) {
           k01 = __fmul2_rn(k01, make_float2(p.scale, p.scale));
@@ -563,12 +582,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         *reinterpret_cast<uint2*>(ks + off) =
             make_uint2(pack_bf16x2(k01.x, k01.y), pack_bf16x2(k23.x, k23.y));
-        if (i == 7 && gw == GATE_WARPS - 1) {
-          // e^{G_last}
-          const float2 d01 = __fmul2_rn(G01, L2), d23 = __fmul2_rn(G23, L2);
-          *reinterpret_cast<float4*>(dec + s * KD + 4 * lane) =
-              make_float4(ex2_approx(d01.x), ex2_approx(d01.y), ex2_approx(d23.x), ex2_approx(d23.y));
-        }
+      }
+      if (gw == GATE_WARPS - 1) {
+        // e^{G_last}, once the state warps have taken the decay of chunk n-2
+        if (!mbar_wait(&bar[B_DEC_EMPTY + s], ph2 ^ 1, ab)) { gok = false; break; }
+        const float2 d01 = __fmul2_rn(G01, L2), d23 = __fmul2_rn(G23, L2);
+        *reinterpret_cast<float4*>(dec + s * KD + 4 * lane) =
+            make_float4(ex2_approx(d01.x), ex2_approx(d01.y), ex2_approx(d23.x), ex2_approx(d23.y));
       }
       fence_proxy_async_smem();
       __syncwarp();
