@@ -48,9 +48,11 @@ struct Cfg {
   // kStg (BN = 256): the bf16 output is staged through shared memory (one
   // 8 KB slot per promotion warp: 32 rows x 128 columns as two 128B-swizzled
   // 32x64 boxes) and TMA-stored, so the epilogue does not hold up the next
-  // tile's MMAs; the slots take the room of one operand stage.  Pays off
-  // for short reductions (few K blocks per tile, e.g. dlhs of an
-  // up-projection); long ones keep the fourth stage.
+  // tile's MMAs; the slots take the room of one operand stage.  Used for
+  // every bf16 output: the direct 16-byte stores of a 32-row slice go to 32
+  // rows N apart, ~4k separate L2 writes per SM and tile, which held the
+  // next tile's MMAs back (gmm_dense_expert 4.24 -> 3.98 ms staged; the
+  // fourth operand stage it gives up is worth nothing measurable).
   static constexpr bool STG = kStg && BN == 256;
   static constexpr int STG_BYTES = STG ? 8 * 8192 : 0;
   static constexpr int STAGES = STG ? 3
@@ -1080,10 +1082,6 @@ static bool out_tmaps(gl::gmm::Params& p, int64_t M, int64_t N, gl::gmm::OutMaps
   return true;
 }
 
-// Staged output (TMA stores) for at most this many K blocks per tile, and
-// always for several outputs or a row offset (the rows go to every output,
-// own or peer-mapped, by TMA while the next tile is computed).
-constexpr int STG_MAX_KB = 24;
 
 template <int BN, bool kTransB, bool kStg>
 static int launch_cfg(const CUtensorMap& tm_a, const CUtensorMap& tm_b, const gl::gmm::OutMaps& tm_o,
@@ -1113,11 +1111,10 @@ static int launch_bn(const CUtensorMap& tm_a, const CUtensorMap& tm_b, gl::gmm::
   for (int o = 0; o < gl::gmm::MAX_OUTS; ++o) tm_o.m[o] = tm_a;
   p.tma_out = 0;
   if constexpr (BN == 256) {
-    if (p.K / gl::gmm::BK <= STG_MAX_KB || p.n_outs > 1 || p.row_off != 0) {
-      if (!out_tmaps(p, M, N, &tm_o, why)) return -1;
-      if (p.tma_out)
-        return launch_cfg<BN, kTransB, true>(tm_a, tm_b, tm_o, p, G, M, N, st, num_sms, why);
-    }
+    // staged output whenever the outputs are bf16 (out_tmaps decides)
+    if (!out_tmaps(p, M, N, &tm_o, why)) return -1;
+    if (p.tma_out)
+      return launch_cfg<BN, kTransB, true>(tm_a, tm_b, tm_o, p, G, M, N, st, num_sms, why);
   }
   return launch_cfg<BN, kTransB, false>(tm_a, tm_b, tm_o, p, G, M, N, st, num_sms, why);
 }
