@@ -44,20 +44,22 @@ constexpr int REG_CTRL = 40, REG_STATE = 216;
 static_assert(128 * REG_CTRL + 256 * 128 + 128 * REG_STATE <= NUM_THREADS * 128,
               "register split exceeds the launch allocation");
 
-template <int VS>
+template <int VS, bool kSplit = false>
 struct Cfg {
   // q/k/v ring depth: a stage is released only once O of its chunk has
   // completed, so the load of chunk n+3 waits for the A -> P -> O chain of
   // chunk n.  The raw gate has one buffer, reloaded for chunk n+1 as soon as
   // the gating of chunk n has read it.  The S accumulator is double-buffered
-  // in TMEM when its columns fit (VS = 64).
-  static constexpr int QS = 3;
+  // in TMEM when its columns fit (VS = 64).  kSplit (P as a bf16 hi + lo
+  // pair) needs a second P buffer: it gives up the third ring stage.
+  static constexpr int QS = kSplit ? 2 : 3;
   static constexpr int NS = VS == 64 ? 2 : 1;
   static constexpr int V_BOXES = VS / 64;
   static constexpr uint32_t Q_BYTES = C * KD * 2;          // 16 KB (2 boxes of 64 features)
   static constexpr uint32_t V_BYTES = C * VS * 2;          // 8 / 16 KB
   static constexpr uint32_t G_BYTES = C * KD * 4;          // 32 KB
-  static constexpr uint32_t P_BYTES = C * C * 2;           // 8 KB
+  static constexpr uint32_t P1_BYTES = C * C * 2;          // 8 KB: one bf16 P
+  static constexpr uint32_t P_BYTES = (kSplit ? 2 : 1) * P1_BYTES;  // P (+ P_lo)
   static constexpr uint32_t H_BYTES = KD * VS * 2;         // 16 / 32 KB
   static constexpr uint32_t OFF_Q = 0;
   static constexpr uint32_t OFF_K = OFF_Q + QS * Q_BYTES;
@@ -120,8 +122,9 @@ struct Params {
   int has_hout;  // FWD: write h_n (bf16, [B,NT,H,K,V]) through tm_h; DH: E_n (always)
   // FWD: 1 selects the kSplit instance of the kernel, which computes
   // tril(A) V as P_hi V + P_lo V (P_hi = bf16(tril(A)), P_lo =
-  // bf16(tril(A) - P_hi), ~2^-17 relative: the fp32 A of the template's
-  // output kernel); 0 feeds the tensor core bf16(tril(A)) only (the bf16
+  // bf16(tril(A) - P_hi) in a second P buffer, ~2^-17 relative: the fp32 A
+  // of the template's output kernel; the buffer takes the room of the third
+  // q/k/v stage); 0 feeds the tensor core bf16(tril(A)) only (the bf16
   // operands of the reference jnp einsum at TPU default precision).
   int p_split;
   float* ws_h;
@@ -150,8 +153,7 @@ enum {
   B_DRAIN = 30,
   B_GSYNC = 31,      // [2] gating quarter sums written
   B_HST = 33,        // the TMA store of the previous state tile has read shared memory
-  B_P_READ = 34,     // P_hi V committed (the P buffer may take P_lo) -> state
-  NUM_BARS = 35
+  NUM_BARS = 34
 };
 static_assert(NUM_BARS * 8 <= 512, "barrier area");
 
@@ -180,7 +182,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                          const __grid_constant__ CUtensorMap tm_v,
                          const __grid_constant__ CUtensorMap tm_g,
                          const __grid_constant__ CUtensorMap tm_h, const Params p) {
-  using CF = Cfg<VS>;
+  using CF = Cfg<VS, kSplit>;
   // kStateOnly: S_n = (k slot)^T (v slot) only (no q, A, O).  kRev: chunks
   // in reverse order, the k slot scaled like q (Qs) instead of k (Kg).
   constexpr bool kStateOnly = kMode != MODE_FWD;
@@ -241,7 +243,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&bar[B_S_EMPTY + i], STATE_WARPS);
     }
     mbar_init(&bar[B_P_FULL], STATE_WARPS);
-    mbar_init(&bar[B_P_READ], 1);
     mbar_init(&bar[B_H_FULL], STATE_WARPS);
     mbar_init(&bar[B_DRAIN], 1);
     mbar_init(&bar[B_HST], 1);
@@ -324,21 +325,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   sdesc(h_addr + kk * 2048, 16384, 1024, kSwizzle128B), CF::IDESC_O, kk > 0);
         }
       };
-      // P V; with p_split in two parts through the one P buffer, P_hi =
-      // bf16(tril(A)) then P_lo = bf16(tril(A) - P_hi), so that the product
-      // sees A to ~2^-17 relative.  `last`: the part that completes O_n.
-      auto issue_o_p = [&](int n, bool last) {
+      // P V; with kSplit P_hi V then P_lo V (P_hi = bf16(tril(A)), P_lo =
+      // bf16(tril(A) - P_hi) in the second P buffer), so that the product
+      // sees A to ~2^-17 relative.
+      auto issue_o_p = [&](int n) {
         const int s = n & 1;
         const uint32_t v_addr = s_base + CF::OFF_V + (n % QS) * CF::V_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          mma_f16(tmem + CF::COL_O + s * VS, sdesc(p_addr + kk * 32, 16, 1024, kSwizzle128B),
-                  sdesc(v_addr + kk * 2048, 8192, 1024, kSwizzle128B), CF::IDESC_O, 1);
-        }
-        if (!last) {
-          tc_commit(&bar[B_P_READ]);
-          return;
-        }
+        for (int part = 0; part < (kSplit ? 2 : 1); ++part)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            mma_f16(tmem + CF::COL_O + s * VS,
+                    sdesc(p_addr + part * CF::P1_BYTES + kk * 32, 16, 1024, kSwizzle128B),
+                    sdesc(v_addr + kk * 2048, 8192, 1024, kSwizzle128B), CF::IDESC_O, 1);
+          }
         tc_commit(&bar[B_O_FULL + s]);
         tc_commit(&bar[B_QKV_EMPTY + n % QS]);
       };
@@ -363,20 +363,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       } else {
         int na = 0, nh = 0, no = 0;
-        bool lo = false;  // p_split: P_hi V of chunk `no` issued, P_lo V next
         uint64_t t0 = global_ns();
         uint32_t spins = 0;
         while (no < NT) {
           bool progressed = false;
-          // P_FULL completes once per chunk, or with p_split twice: P_hi
-          // (parity 0) and P_lo (parity 1)
-          const uint32_t pph = kSplit ? (lo ? 1u : 0u) : static_cast<uint32_t>(no & 1);
-          if (no < nh && mbar_test(&bar[B_P_FULL], pph)) {
+          if (no < nh && mbar_test(&bar[B_P_FULL], no & 1)) {
             tc_fence_after();
-            const bool last = !kSplit || lo;
-            issue_o_p(no, last);
-            if (last) ++no;
-            if (kSplit) lo = !lo;
+            issue_o_p(no);
+            ++no;
             progressed = true;
           }
           if (nh < na && nh == no && mbar_test(&bar[B_H_FULL], nh & 1) &&
@@ -678,22 +672,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ++nstore;
       return true;
     };
-    // P = tril(A_m) in bf16, K-major (row = query, 128 B).  With p_split in
-    // two parts through the one P buffer: lo = false writes P_hi =
-    // bf16(tril(A_m)); lo = true, once P_hi V has read the buffer
-    // (B_P_READ), writes P_lo = bf16(tril(A_m) - P_hi) from A_m read again
-    // out of TMEM.  The A buffer is released by the last part.
-    auto p_epilogue = [&](int m, bool lo) -> bool {
+    // P = tril(A_m) in bf16, K-major (row = query, 128 B); with kSplit also
+    // P_lo = bf16(tril(A_m) - P) in the second P buffer.
+    auto p_epilogue = [&](int m) -> bool {
       const int s = m & 1;
-      if (!lo && !mbar_wait(&bar[B_A_FULL + s], (m >> 1) & 1, ab)) return false;
-      if (lo && !mbar_wait(&bar[B_P_READ], m & 1, ab)) return false;
+      if (!mbar_wait(&bar[B_A_FULL + s], (m >> 1) & 1, ab)) return false;
       tc_fence_after();
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t a[32];
         tmem_ld32(lane_addr + CF::COL_A + s * 64 + half * 32, a);
         tmem_ld_wait(a);
-        if ((lo || !kSplit) && half == 1) {
+        if (half == 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bar[B_A_EMPTY + s]);
@@ -706,13 +696,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               const int j = half * 32 + c4 * 8 + e;
-              const float x = j <= prow ? __uint_as_float(a[c4 * 8 + e]) : 0.f;
-              f[e] = (kSplit && lo) ? x - __bfloat162float(__float2bfloat16_rn(x)) : x;
+              f[e] = j <= prow ? __uint_as_float(a[c4 * 8 + e]) : 0.f;
             }
             const uint32_t ch = static_cast<uint32_t>(half * 4 + c4) ^ (prow & 7);
-            *reinterpret_cast<uint4*>(pp + (ch << 4)) =
-                make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                           pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+            const uint4 hi = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                        pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+            *reinterpret_cast<uint4*>(pp + (ch << 4)) = hi;
+            if constexpr (kSplit) {
+              const uint32_t hw[4] = {hi.x, hi.y, hi.z, hi.w};
+              float r[8];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 h2 = bf16x2_f32x2(hw[e]);
+                r[2 * e] = f[2 * e] - h2.x;
+                r[2 * e + 1] = f[2 * e + 1] - h2.y;
+              }
+              *reinterpret_cast<uint4*>(pp + CF::P1_BYTES + (ch << 4)) =
+                  make_uint4(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]),
+                             pack_bf16x2(r[4], r[5]), pack_bf16x2(r[6], r[7]));
+            }
           }
         }
       }
@@ -722,7 +724,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       return true;
     };
     bool ok = true;
-    if (!kStateOnly) ok = store_h(0) && p_epilogue(0, false) && (!kSplit || p_epilogue(0, true));
+    if (!kStateOnly) ok = store_h(0) && p_epilogue(0);
     for (int n = 0; n < NT && ok; ++n) {
       const int s = n & 1;
       const uint32_t ph2 = (n >> 1) & 1;
@@ -768,15 +770,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) mbar_arrive(&bar[B_S_EMPTY + n % NS]);
       if (kStateOnly) continue;
       // O_n done -> H and P may be rewritten for chunk n+1 (the next O
-      // accumulates into the other TMEM buffer meanwhile).  P_lo follows
-      // P_hi as soon as P_hi V has read the buffer.
+      // accumulates into the other TMEM buffer meanwhile)
       if (!mbar_wait(&bar[B_O_FULL + s], ph2, ab)) { ok = false; break; }
       tc_fence_after();
-      if (n + 1 < NT && !(store_h(n + 1) && p_epilogue(n + 1, false) &&
-                          (!kSplit || p_epilogue(n + 1, true)))) {
-        ok = false;
-        break;
-      }
+      if (n + 1 < NT && !(store_h(n + 1) && p_epilogue(n + 1))) { ok = false; break; }
     }
     if (st_issuer && p.has_hout) bulk_wait<0>();
     if (ok && (kMode == MODE_FWD_STATE || kMode == MODE_DH_STATE)) {
@@ -925,7 +922,7 @@ static int launch_pass(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
   if constexpr (kMode == gl::gla::MODE_FWD && !kSplit) {
     if (p.p_split) return launch_pass<VS, kMode, true>(tq, tk, tv, tg, th, p, grid, st, why);
   }
-  using CF = gl::gla::Cfg<VS>;
+  using CF = gl::gla::Cfg<VS, kSplit>;
   const void* fn = reinterpret_cast<const void*>(gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit>);
   if (!gl_set_smem_attr(fn, 0, static_cast<int>(CF::SMEM_BYTES), why)) return -2;
   gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit><<<grid, gl::gla::NUM_THREADS, CF::SMEM_BYTES, st>>>(
