@@ -20,7 +20,7 @@ GL_ELAUNCH = -2
 GL_EDEVICE = -3
 GL_OUT_BF16 = 0
 GL_OUT_F32 = 1
-GL_GLA_EXACT_INTRA = 1
+GL_GLA_BF16_INTRA = 1
 DEV_CODES = {0: "ok", 1: "device wait timed out", 2: "invalid group_sizes (negative or sum > M)"}
 
 # (name, restype, argtypes) for every symbol the header declares.

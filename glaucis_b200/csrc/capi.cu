@@ -429,7 +429,7 @@ int gl_chunk_gla_fwd_ex(const void* q, const void* k, const void* v, const float
   const char* f = h_states ? "gl_chunk_gla_fwd_states" : "gl_chunk_gla_fwd";
   if (int rc = chunk_gla_check(f, q, k, v, g, g_gamma, h0, B, T, H, K, V, chunk_size, o, ht))
     return rc;
-  if (flags & ~GL_GLA_EXACT_INTRA) return fail(GL_EINVAL, std::string(f) + ": unknown flags");
+  if (flags & ~GL_GLA_BF16_INTRA) return fail(GL_EINVAL, std::string(f) + ": unknown flags");
   if (h_states && !aligned16(h_states))
     return fail(GL_EINVAL, std::string(f) + ": h_states must be a 16-byte aligned pointer");
   if (h_states && !gla_states_fit(B, T, H))
@@ -441,7 +441,7 @@ int gl_chunk_gla_fwd_ex(const void* q, const void* k, const void* v, const float
   const char* why = "";
   const int rc = gl_launch_chunk_gla(q, k, v, g, g_gamma, h0, scale, B, T, H, K, V, o, ht,
                                      h_states, workspace, workspace ? workspace_bytes : 0,
-                                     (flags & GL_GLA_EXACT_INTRA) ? 1 : 0,
+                                     (flags & GL_GLA_BF16_INTRA) ? 0 : 1,
                                      err_word ? err_word : d->err,
                                      static_cast<cudaStream_t>(stream), d->num_sms, &why);
   if (rc == -1) return fail(GL_EINVAL, std::string(f) + ": " + why);

@@ -454,7 +454,7 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                   g_gamma: Optional[torch.Tensor], scale: float, chunk_size: int = 64, *,
                   g: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
                   output_final_state: bool = False, output_states: bool = False,
-                  output_intermediates: bool = False, exact_intra: bool = False,
+                  output_intermediates: bool = False, exact_intra: bool = True,
                   o: Optional[torch.Tensor] = None,
                   ht: Optional[torch.Tensor] = None,
                   h: Optional[torch.Tensor] = None) -> GLAForward:
@@ -468,11 +468,12 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     g_cumsum (fp32 [B, T, H, K]) and the unmasked intra-chunk A (fp32
     [B, T, H, 64]) as the reference's first two outputs, computed by a
     separate fp32 kernel (one more pass over q, k and g).
-    exact_intra=True feeds tril(A) to the intra-chunk product as a bf16
-    hi + lo pair (A to ~2^-17 relative, the fp32 A of the template's output
-    kernel, chunk_gla.py:208-212) instead of one bf16 rounding (the operand
-    precision of the reference jnp oracle's einsum at TPU default precision,
-    chunk_gla_ref.py:96-97); it is slower.  o, ht and h may be given
+    exact_intra=True (the default) feeds tril(A) to the intra-chunk product
+    as a bf16 hi + lo pair (A to ~2^-17 relative, the fp32 A of the
+    template's output kernel, chunk_gla.py:208-212); exact_intra=False
+    rounds it to bf16 once (the operand precision of the reference jnp
+    oracle's einsum at TPU default precision, chunk_gla_ref.py:96-97),
+    about 10 % faster.  o, ht and h may be given
     preallocated.
     """
     B, T, H, K, V = _gla_check(q, k, v, g_gamma, g, h0)
@@ -487,7 +488,7 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
     if output_states:
         h = _out(h, (B, T // chunk_size, H, K, V), torch.bfloat16, q.device, "h")
-    flags = _lib.GL_GLA_EXACT_INTRA if exact_intra else 0
+    flags = 0 if exact_intra else _lib.GL_GLA_BF16_INTRA
     _lib.check(lib.gl_chunk_gla_fwd_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
                                        _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
                                        chunk_size, o.data_ptr(), _ptr(ht),
@@ -576,7 +577,7 @@ class _ChunkGLA(torch.autograd.Function):
 
 def chunk_gla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g_gamma: Optional[torch.Tensor],
               scale: float, chunk_size: int = 64, *, g: Optional[torch.Tensor] = None,
-              h0: Optional[torch.Tensor] = None, exact_intra: bool = False) -> torch.Tensor:
+              h0: Optional[torch.Tensor] = None, exact_intra: bool = True) -> torch.Tensor:
     """`chunk_gla(q, k, v, g_gamma, scale, chunk_size)`
     (KE/examples/kernels/chunk_gla.py:434-456): returns o (bf16),
     differentiable in q, k, v (and h0) when any of them requires grad.

@@ -158,21 +158,20 @@ int gl_chunk_gla_fwd(const void* q, const void* k, const void* v, const float* g
                      void* stream);
 
 /* Flags of gl_chunk_gla_fwd_ex. */
-#define GL_GLA_EXACT_INTRA 1  /* tril(A) v with A to ~2^-17 relative (see below) */
+#define GL_GLA_BF16_INTRA 1  /* tril(A) v with A rounded to bf16 once (see below) */
 
 /*
  * The chunked GLA forward with every option: gl_chunk_gla_fwd_ws (h_states
  * NULL) or gl_chunk_gla_fwd_states (h_states non-NULL) plus `flags`.
- *   flags = 0: the intra-chunk product tril(A) v takes A rounded to bf16 on
- *     the tensor core (fp32 accumulation), the operand precision of the
- *     reference's jnp oracle at default matmul precision on its TPU
- *     platform (KE/examples/kernels/chunk_gla_ref.py:96-97).
- *   flags = GL_GLA_EXACT_INTRA: tril(A) v = P_hi v + P_lo v with
- *     P_hi = bf16(tril(A)) and P_lo = bf16(tril(A) - P_hi), so A enters the
- *     product to ~2^-17 relative, as the template's output kernel multiplies
- *     fp32 A by v at Precision.HIGHEST (KE/examples/kernels/chunk_gla.py
- *     :208-212).  Slower (one more dependent MMA per chunk through the one
- *     P buffer).
+ *   flags = 0 (also every other gl_chunk_gla_fwd* entry point): the
+ *     intra-chunk product tril(A) v = P_hi v + P_lo v with P_hi =
+ *     bf16(tril(A)) and P_lo = bf16(tril(A) - P_hi), so A enters the product
+ *     to ~2^-17 relative, as the template's output kernel multiplies fp32 A
+ *     by v at Precision.HIGHEST (KE/examples/kernels/chunk_gla.py:208-212).
+ *   flags = GL_GLA_BF16_INTRA: A rounded to bf16 once on the tensor core
+ *     (fp32 accumulation), the operand precision of the reference's jnp
+ *     oracle at default matmul precision on its TPU platform
+ *     (KE/examples/kernels/chunk_gla_ref.py:96-97); about 10 % faster.
  * Replaces chunk_gla_fwd (KE/examples/kernels/chunk_gla.py:258-273) as
  * gl_chunk_gla_fwd does.
  */

@@ -38,13 +38,13 @@ def value_slice(request, monkeypatch):
     return request.param
 
 
-@pytest.fixture(autouse=True, params=["bf16_p", "exact_intra"])
+@pytest.fixture(autouse=True, params=["exact_intra", "bf16_p"])
 def intra_precision(request, monkeypatch):
-    """... and in both precisions of the intra-chunk product: tril(A) as one
-    bf16 operand (the default) and as a bf16 hi + lo pair (exact_intra)."""
-    if request.param == "exact_intra":
+    """... and in both precisions of the intra-chunk product: tril(A) as a
+    bf16 hi + lo pair (exact_intra, the default) and as one bf16 operand."""
+    if request.param == "bf16_p":
         import functools
-        monkeypatch.setattr(ops, "chunk_gla_fwd", functools.partial(ops.chunk_gla_fwd, exact_intra=True))
+        monkeypatch.setattr(ops, "chunk_gla_fwd", functools.partial(ops.chunk_gla_fwd, exact_intra=False))
     return request.param
 
 
@@ -169,7 +169,7 @@ def test_exact_intra_is_closer_to_the_fp32_product(cuda, intra_precision):
     # exact_intra removes the bf16 rounding of tril(A) from the intra-chunk
     # product: against the fp32 oracle its error must not exceed the
     # default's, and both hold the forward tolerance.
-    if intra_precision != "bf16_p":
+    if intra_precision != "exact_intra":
         pytest.skip("compares the two precisions itself")
     cfg = configs.GLAConfig("t", B=2, T=512, H=4, h0_std=0.1)
     inp = configs.make_gla_inputs(cfg, device="cpu", seed=13)
