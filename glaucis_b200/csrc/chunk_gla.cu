@@ -11,6 +11,8 @@
 //   A  = Qs Kg^T                       tcgen05 M=64  N=64   K=128  (TMEM)
 //   S  = Kg^T V                        tcgen05 M=128 N=VS   K=64   (TMEM)
 //   O  = Qs H_n + tril(A) V            tcgen05 M=64  N=VS   K=128+64
+//        (tril(A) as P_hi + P_lo, two bf16 operands, in the kSplit instance:
+//        A to ~2^-17 relative; one bf16 operand in the other instance)
 //   h_{n+1} = e^{G_last} * (h_n + S)   fp32 in registers, H_{n+1} = bf16(h_{n+1})
 // which is the reference recurrence h_{n+1} = e^{G_last} h_n
 // + (k e^{G_last-G})^T v with the per-key decay factored out of the sum.
@@ -28,9 +30,10 @@
 //                 of the chunk two behind (TMEM -> bf16 -> HBM)
 //   warps 12-15   state warpgroup: A -> tril -> bf16 P, state update
 //                 (thread = key row, VS fp32 columns in registers)
-// Buffers: g double-buffered, q/k/v in a 3-stage (VS = 64) or 2-stage ring;
-// A and O double-buffered in TMEM, S double-buffered when VS = 64; P and the
-// bf16 state copy H single-buffered (rewritten only after O_n completed).
+// Buffers: one g buffer, q/k/v in a 3-stage ring (2 stages in the kSplit
+// instance, whose second P buffer takes the third stage's room); A and O
+// double-buffered in TMEM, S double-buffered when VS = 64; P (P_hi, P_lo) and
+// the bf16 state copy H single-buffered (rewritten only after O_n completed).
 #include "common.cuh"
 
 namespace gl {
