@@ -212,6 +212,11 @@ def gmm_fp8_fwd_gathered(a_q: torch.Tensor, a_s: torch.Tensor, b_q: torch.Tensor
         gs = group_sizes
         if gs is None:
             gs = torch.from_numpy(np.ascontiguousarray(me.sizes, np.int32)).to(a_q.device)
-        ops.gmm_fp8_fwd_scatter(a_q, a_s, b_q, b_s, gs, peers.ptrs, me.r0)
+        # every slice goes to the outputs in this order: own buffer first,
+        # then the next ranks round the ring, so that at any moment the
+        # ranks store into different peers (NVLink ingress spread evenly)
+        r = dist.get_rank()
+        ring = peers.ptrs[r:] + peers.ptrs[:r]
+        ops.gmm_fp8_fwd_scatter(a_q, a_s, b_q, b_s, gs, ring, me.r0)
     dist.all_reduce(flag)
     return peers.local
