@@ -105,6 +105,14 @@ def all_gather_rows(local: torch.Tensor, counts: List[int], out: torch.Tensor) -
     return out
 
 
+def ring_order(items: list, rank: int) -> list:
+    """`items` (one per rank) starting at this rank's and continuing round
+    the ring: the order in which a rank's scatter epilogue stores every
+    slice, so that at any moment the ranks store into different peers (their
+    NVLink ingress spread evenly) rather than all into rank 0 first."""
+    return list(items[rank:]) + list(items[:rank])
+
+
 class _CudaArray:
     """A raw device allocation seen through __cuda_array_interface__."""
 
@@ -212,11 +220,7 @@ def gmm_fp8_fwd_gathered(a_q: torch.Tensor, a_s: torch.Tensor, b_q: torch.Tensor
         gs = group_sizes
         if gs is None:
             gs = torch.from_numpy(np.ascontiguousarray(me.sizes, np.int32)).to(a_q.device)
-        # every slice goes to the outputs in this order: own buffer first,
-        # then the next ranks round the ring, so that at any moment the
-        # ranks store into different peers (NVLink ingress spread evenly)
-        r = dist.get_rank()
-        ring = peers.ptrs[r:] + peers.ptrs[:r]
-        ops.gmm_fp8_fwd_scatter(a_q, a_s, b_q, b_s, gs, ring, me.r0)
+        ops.gmm_fp8_fwd_scatter(a_q, a_s, b_q, b_s, gs, ring_order(peers.ptrs, dist.get_rank()),
+                                me.r0)
     dist.all_reduce(flag)
     return peers.local

@@ -84,3 +84,11 @@ def test_all_gather_rows_two_gloo_ranks():
                                for r in range(world)])
         for r in range(world):
             np.testing.assert_array_equal(np.asarray(res[(r, tuple(counts))]), want)
+
+
+def test_ring_order_spreads_the_first_peer_store():
+    ptrs = [100, 101, 102, 103]
+    orders = [shard.ring_order(ptrs, r) for r in range(4)]
+    assert orders[0] == [100, 101, 102, 103] and orders[2] == [102, 103, 100, 101]
+    for k in range(4):  # at every position the four ranks target four different buffers
+        assert sorted(o[k] for o in orders) == ptrs
