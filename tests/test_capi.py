@@ -99,3 +99,24 @@ def test_ops_refuse_cpu_tensors():
     from glaucis_b200 import ops
     with pytest.raises(ValueError, match="CUDA"):
         ops.quant_act_1x128(torch.zeros(4, 128, dtype=torch.bfloat16))
+
+
+def test_gla_options_and_intermediates_reject_bad_arguments_without_device():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    f = ctypes.c_void_p(32)
+    # gl_chunk_gla_fwd_ex: only GL_GLA_BF16_INTRA is a known flag
+    rc = lib.gl_chunk_gla_fwd_ex(p, p, p, f, None, None, 0.1, 1, 64, 1, 128, 128, 64, p, None,
+                                 None, None, 0, 2, None, None)
+    assert rc == _lib.GL_EINVAL and "unknown flags" in _err()
+    rc = lib.gl_chunk_gla_fwd_ex(p, p, p, f, f, None, 0.1, 1, 64, 1, 128, 128, 64, p, None,
+                                 None, None, 0, _lib.GL_GLA_BF16_INTRA, None, None)
+    assert rc == _lib.GL_EINVAL and "exactly one" in _err()
+    # gl_chunk_gla_fwd_intermediates: at least one output, one gate, K = 128
+    rc = lib.gl_chunk_gla_fwd_intermediates(p, p, f, None, 0.1, 1, 64, 1, 128, 64, None, None,
+                                            None, None)
+    assert rc == _lib.GL_EINVAL and "neither" in _err()
+    rc = lib.gl_chunk_gla_fwd_intermediates(p, p, f, f, 0.1, 1, 64, 1, 128, 64, f, None, None, None)
+    assert rc == _lib.GL_EINVAL and "exactly one" in _err()
+    rc = lib.gl_chunk_gla_fwd_intermediates(p, p, f, None, 0.1, 1, 64, 1, 64, 64, f, None, None, None)
+    assert rc == _lib.GL_EINVAL and "128" in _err()
