@@ -612,7 +612,7 @@ def secondary_gmm(args, workload, rank, world, peaks, peak_kind, with_extras: bo
     return blk
 
 
-def gla_block(args, workload, rank, world, peaks, peak_kind):
+def gla_block(args, workload, rank, world, peaks, peak_kind, local=0):
     import torch
     from glaucis_b200 import configs, ops
     gcfg = configs.GLA_CONFIGS[workload]
@@ -629,8 +629,14 @@ def gla_block(args, workload, rank, world, peaks, peak_kind):
                           g=inp["g"], h0=inp["h0"], output_final_state=True, o=go, ht=ght,
                           exact_intra=False)
 
-    gla_ms = timed(gla_step, args.steps, args.warmup, world)
-    bf_ms = timed(gla_bf16_step, max(5, args.steps // 2), 3, world)
+    # The GLA kernels are latency-bound, so their time follows the SM clock:
+    # a longer warm-up lets the clock settle after the power-capped matmul
+    # rows, and the clock is recorded beside each timing.
+    gwarm = max(args.warmup, 100)
+    cs_ex = ClockSampler(local) if rank == 0 else None
+    gla_ms = timed(gla_step, args.steps, gwarm, world, cs_ex)
+    cs_bf = ClockSampler(local) if rank == 0 else None
+    bf_ms = timed(gla_bf16_step, args.steps, gwarm, world, cs_bf)
     if ops.device_status() != 0:
         raise SystemExit("device error word set after the GLA timed region")
     gla_bytes = configs.gla_bytes(gcfg.B, gcfg.T, gcfg.H, has_h0=gcfg.h0_std > 0)
@@ -647,7 +653,9 @@ def gla_block(args, workload, rank, world, peaks, peak_kind):
                         "traffic": ncu_traffic("chunk_gla_fwd_kernel", workload)},
            "precision": "tril(A) enters the intra-chunk product as a bf16 hi + lo pair (~2^-17 "
                         "relative): the fp32 A of the template's output kernel",
+           "clocks": cs_ex.summary() if cs_ex else None,
            "bf16_intra": {"ms_per_step": bf_ms,
+                          "clocks": cs_bf.summary() if cs_bf else None,
                           "tokens_per_s": world * gcfg.B * gcfg.T / (bf_ms * 1e-3),
                           "hbm_frac": gla_bytes / (bf_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
                           "precision": "tril(A) rounded to bf16 once (the jnp oracle's einsum at "
@@ -708,8 +716,8 @@ def run_b200(args):
     value = head["flops_total"] / (ms * 1e-3) / 1e12
     moe = secondary_gmm(args, MOE_WORKLOAD, rank, world, peaks, peak_kind, with_extras=True)
     small = secondary_gmm(args, SMALL_WORKLOAD, rank, world, peaks, peak_kind, with_extras=False)
-    gla = gla_block(args, GLA_WORKLOAD, rank, world, peaks, peak_kind)
-    gla_long = gla_block(args, GLA_LONG_WORKLOAD, rank, world, peaks, peak_kind)
+    gla = gla_block(args, GLA_WORKLOAD, rank, world, peaks, peak_kind, local)
+    gla_long = gla_block(args, GLA_LONG_WORKLOAD, rank, world, peaks, peak_kind, local)
 
     sharded = None
     if world > 1 and not args.skip_sharded:
