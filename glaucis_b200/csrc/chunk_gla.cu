@@ -117,8 +117,8 @@ struct Params {
   // Forward split with a short first segment (c_first > 0 chunks): segment 0
   // runs the full pass from h0 while the state-only pass covers segments
   // 1..nseg-2; segment 0's full pass writes its final state, as its ht, into
-  // record 0 (ht = ws_h, ht_seg = 0), which the fold passes through (zero
-  // start, decay 0); segments 1.. share the remaining chunks.  c_first = 0:
+  // record 0 (ht = ws_h, ht_seg = 0), from which the fold starts (its decay
+  // record is not written); segments 1.. share the remaining chunks.  c_first = 0:
   // equal segments as above.  Record of segment seg: seg - rec_base.
   // ht_seg: the segment whose final state is written to ht.
   int c_first, rec_base, ht_seg;
@@ -808,24 +808,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // the recurrence h_{n+1} = d_n (h_n + S_n) being linear in h_n with a per-row
 // scale.  reverse (the DH scan): record j holds segment j+1's zero-start
 // gradient and decay, folded from the last segment down, starting from dht
-// (passed as h0).  One thread per 4 state entries of one (batch, head).
+// (passed as h0).  pass_first (forward only): record 0 already holds the
+// true state after segment 0 and is the start; its decay is not read.
+// One thread per state entry of one (batch, head), a warp per 32 columns of
+// one key row.  The records do not depend on the running state, so all
+// their loads (up to FOLD_BATCH) are issued before the dependent
+// multiply-adds: one memory latency per call rather than one per record.
+constexpr int FOLD_BATCH = 40;
 __global__ void __launch_bounds__(256) gla_fold_kernel(const float* __restrict__ h0,
                                                        float* __restrict__ ws_h,
                                                        const float* __restrict__ ws_d, int BH,
-                                                       int nseg, int reverse) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= static_cast<int64_t>(BH) * KD * 32) return;
-  const int bh = static_cast<int>(i / (KD * 32));
-  const int key = static_cast<int>((i / 32) % KD), c4 = static_cast<int>(i % 32);
-  float4 h = h0 ? reinterpret_cast<const float4*>(h0)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int i = 0; i < nseg - 1; ++i) {
-    const int j = reverse ? nseg - 2 - i : i;
-    const int64_t rec = static_cast<int64_t>(j) * BH + bh;
-    const float d = ws_d[rec * KD + key];
-    float4* slot = reinterpret_cast<float4*>(ws_h + (rec * KD + key) * 128) + c4;
-    const float4 x = *slot;
-    h = make_float4(fmaf(d, h.x, x.x), fmaf(d, h.y, x.y), fmaf(d, h.z, x.z), fmaf(d, h.w, x.w));
-    *slot = h;
+                                                       int nseg, int reverse, int pass_first) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= static_cast<int64_t>(BH) * KD * 128) return;
+  const int bh = static_cast<int>(t / (KD * 128));
+  const int key = static_cast<int>((t / 128) % KD), col = static_cast<int>(t % 128);
+  auto rec_of = [&](int j) -> int64_t { return static_cast<int64_t>(j) * BH + bh; };
+  const int nrec = nseg - 1;
+  float h;
+  int i = 0;
+  if (pass_first && !reverse && nrec > 0) {
+    h = ws_h[(rec_of(0) * KD + key) * 128 + col];
+    i = 1;
+  } else {
+    h = h0 ? h0[t] : 0.f;
+  }
+  for (; i < nrec; i += FOLD_BATCH) {
+    float d[FOLD_BATCH], x[FOLD_BATCH];
+#pragma unroll
+    for (int u = 0; u < FOLD_BATCH; ++u) {
+      if (i + u < nrec) {
+        const int64_t r = rec_of(reverse ? nrec - 1 - (i + u) : i + u);
+        d[u] = ws_d[r * KD + key];
+        x[u] = ws_h[(r * KD + key) * 128 + col];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < FOLD_BATCH; ++u) {
+      if (i + u < nrec) {
+        const int64_t r = rec_of(reverse ? nrec - 1 - (i + u) : i + u);
+        h = fmaf(d[u], h, x[u]);
+        ws_h[(r * KD + key) * 128 + col] = h;
+      }
+    }
   }
 }
 
@@ -1016,15 +1041,11 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
       }
       if (rc_a) return rc_a;
     }
-    // Record 0 already holds the true state after segment 0: fold from a
-    // zero start with its decay cleared, so it passes through unchanged.
-    if (cudaMemsetAsync(p.ws_d, 0, static_cast<size_t>(p.B) * p.H * 128 * sizeof(float), st) != cudaSuccess) {
-      *why = "clearing the first segment's decay record failed";
-      return -2;
-    }
-    const int64_t n4 = static_cast<int64_t>(p.B) * p.H * 128 * 32;
-    gl::gla::gla_fold_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, st>>>(
-        nullptr, p.ws_h, p.ws_d, p.B * p.H, p.nseg, 0);
+    // Record 0 already holds the true state after segment 0: the fold
+    // starts from it and leaves it unchanged.
+    const int64_t n1 = static_cast<int64_t>(p.B) * p.H * 128 * 128;
+    gl::gla::gla_fold_kernel<<<static_cast<unsigned>((n1 + 255) / 256), 256, 0, st>>>(
+        nullptr, p.ws_h, p.ws_d, p.B * p.H, p.nseg, 0, 1);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
       *why = cudaGetErrorString(e);
@@ -1049,9 +1070,9 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
                        : launch_pass<VS, gl::gla::MODE_FWD_STATE>(tq, tk, tv, tg, th, p1,
                                                                   items * p1.seg_grid, st, why);
     if (rc) return rc;
-    const int64_t n4 = static_cast<int64_t>(p.B) * p.H * 128 * 32;
-    gl::gla::gla_fold_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, st>>>(
-        p.h0, p.ws_h, p.ws_d, p.B * p.H, p.nseg, rev ? 1 : 0);
+    const int64_t n1 = static_cast<int64_t>(p.B) * p.H * 128 * 128;
+    gl::gla::gla_fold_kernel<<<static_cast<unsigned>((n1 + 255) / 256), 256, 0, st>>>(
+        p.h0, p.ws_h, p.ws_d, p.B * p.H, p.nseg, rev ? 1 : 0, 0);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
       *why = cudaGetErrorString(e);
