@@ -121,6 +121,14 @@ def test_backward_sequence_split(cuda, monkeypatch, nseg, gate):
     _check(got, ref, f"nseg={nseg} {gate}")
 
 
+def test_backward_sequence_split_many_segments(cuda, monkeypatch):
+    # 45 segments: 44 records, two batches of the fold kernel's loads
+    monkeypatch.setenv("GLAUCIS_GLA_SEGMENTS", "45")
+    cfg = configs.GLAConfig("t", B=1, T=64 * 48, H=2, h0_std=0.1, gate="per_key")
+    got, ref = _run_bwd(cuda, cfg, seed=6, with_dht=True)
+    _check(got, ref, "nseg=45")
+
+
 def test_autograd_function_and_template(cuda):
     from glaucis_b200.kernels import chunk_gla as tmpl
     cfg = configs.GLAConfig("t", B=1, T=192, H=2, h0_std=0.1, gate="gamma")

@@ -100,6 +100,14 @@ def test_gla_sequence_split(cuda, monkeypatch, nseg, gate):
     _check(*_run(cuda, cfg, seed=7), what=f"split {nseg} {gate}")
 
 
+def test_gla_sequence_split_many_segments(cuda, monkeypatch):
+    # 45 segments of 48 chunks: 44 state records, more than the fold kernel
+    # loads in one batch (40), so its second batch runs too.
+    monkeypatch.setenv("GLAUCIS_GLA_SEGMENTS", "45")
+    cfg = configs.GLAConfig("t", B=1, T=64 * 48, H=2, gate="per_key", h0_std=0.1)
+    _check(*_run(cuda, cfg, seed=9), what="split 45")
+
+
 def test_gla_split_workspace_query(cuda):
     from glaucis_b200 import _lib
     lib = _lib.load()
