@@ -900,6 +900,15 @@ def run_profile(args):
     else:
         gcfg = configs.GLA_CONFIGS[args.gla_workload]
         inp = configs.make_gla_inputs(gcfg, device="cuda", seed=args.seed)
+        if args.gla_heads:
+            # heads 0 .. gla_heads-1 only: one rank's share of the head split
+            # (gla_b1_t32768 at N=8: 4 heads, a 38-segment sequence split)
+            hh = args.gla_heads
+            inp = {n: (None if t is None else
+                       t[:, :hh].contiguous() if n == "h0" else
+                       t[:hh].contiguous() if n == "g_gamma" else
+                       t[:, :, :hh].contiguous())
+                   for n, t in inp.items()}
         fn = lambda: ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], inp["g_gamma"], 128 ** -0.5,
                                        64, g=inp["g"], h0=inp["h0"], output_final_state=True)
     ms = timed(fn, args.steps, args.warmup, 1)
@@ -927,6 +936,8 @@ def main(argv=None):
     ap.add_argument("--profile", choices=["gmm", "gmm_bwd", "gla", "gla_bwd", "quant"], default=None,
                     help="run one kernel only, small footprint (for ncu captures)")
     ap.add_argument("--gla-workload", default=GLA_WORKLOAD)
+    ap.add_argument("--gla-heads", type=int, default=0,
+                    help="--profile gla: run only the first H heads of the GLA workload")
     args = ap.parse_args(argv)
     if args.profile:
         return run_profile(args)

@@ -810,45 +810,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // gradient and decay, folded from the last segment down, starting from dht
 // (passed as h0).  pass_first (forward only): record 0 already holds the
 // true state after segment 0 and is the start; its decay is not read.
-// One thread per state entry of one (batch, head), a warp per 32 columns of
-// one key row.  The records do not depend on the running state, so all
-// their loads (up to FOLD_BATCH) are issued before the dependent
-// multiply-adds: one memory latency per call rather than one per record.
-constexpr int FOLD_BATCH = 40;
+// One thread per 4 state entries (a float4) of one (batch, head).  The
+// records do not depend on the running state, so their loads are issued NB
+// at a time ahead of the dependent multiply-adds; the launcher takes NB = 4
+// for few records (low registers, full occupancy) and up to 16 for many.
+template <int NB>
 __global__ void __launch_bounds__(256) gla_fold_kernel(const float* __restrict__ h0,
                                                        float* __restrict__ ws_h,
                                                        const float* __restrict__ ws_d, int BH,
                                                        int nseg, int reverse, int pass_first) {
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (t >= static_cast<int64_t>(BH) * KD * 128) return;
-  const int bh = static_cast<int>(t / (KD * 128));
-  const int key = static_cast<int>((t / 128) % KD), col = static_cast<int>(t % 128);
+  if (t >= static_cast<int64_t>(BH) * KD * 32) return;
+  const int bh = static_cast<int>(t / (KD * 32));
+  const int key = static_cast<int>((t / 32) % KD), c4 = static_cast<int>(t % 32);
   auto rec_of = [&](int j) -> int64_t { return static_cast<int64_t>(j) * BH + bh; };
+  auto slot_of = [&](int64_t r) -> float4* {
+    return reinterpret_cast<float4*>(ws_h + (r * KD + key) * 128) + c4;
+  };
   const int nrec = nseg - 1;
-  float h;
+  float4 h;
   int i = 0;
   if (pass_first && !reverse && nrec > 0) {
-    h = ws_h[(rec_of(0) * KD + key) * 128 + col];
+    h = *slot_of(rec_of(0));
     i = 1;
   } else {
-    h = h0 ? h0[t] : 0.f;
+    h = h0 ? reinterpret_cast<const float4*>(h0)[t] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  for (; i < nrec; i += FOLD_BATCH) {
-    float d[FOLD_BATCH], x[FOLD_BATCH];
+  for (; i < nrec; i += NB) {
+    float d[NB];
+    float4 x[NB];
 #pragma unroll
-    for (int u = 0; u < FOLD_BATCH; ++u) {
+    for (int u = 0; u < NB; ++u) {
       if (i + u < nrec) {
         const int64_t r = rec_of(reverse ? nrec - 1 - (i + u) : i + u);
         d[u] = ws_d[r * KD + key];
-        x[u] = ws_h[(r * KD + key) * 128 + col];
+        x[u] = *slot_of(r);
       }
     }
 #pragma unroll
-    for (int u = 0; u < FOLD_BATCH; ++u) {
+    for (int u = 0; u < NB; ++u) {
       if (i + u < nrec) {
         const int64_t r = rec_of(reverse ? nrec - 1 - (i + u) : i + u);
-        h = fmaf(d[u], h, x[u]);
-        ws_h[(r * KD + key) * 128 + col] = h;
+        h = make_float4(fmaf(d[u], h.x, x[u].x), fmaf(d[u], h.y, x[u].y), fmaf(d[u], h.z, x[u].z),
+                        fmaf(d[u], h.w, x[u].w));
+        *slot_of(r) = h;
       }
     }
   }
@@ -904,6 +909,27 @@ static int gla_first_segment(int64_t NT, int nseg) {
   if (c < 1) c = 1;
   if (c > NT - (nseg - 1)) c = NT - (nseg - 1);
   return static_cast<int>(c);
+}
+
+// The fold of a split's records (see gla_fold_kernel): pass_first starts
+// from record 0 unchanged (forward split with a short first segment).
+static int launch_fold(const float* h0, const gl::gla::Params& p, int reverse, int pass_first,
+                       cudaStream_t st, const char** why) {
+  const int64_t n4 = static_cast<int64_t>(p.B) * p.H * 128 * 32;
+  const unsigned grid = static_cast<unsigned>((n4 + 255) / 256);
+  const int nrec = p.nseg - 1 - (pass_first ? 1 : 0);
+  if (nrec <= 4)
+    gl::gla::gla_fold_kernel<4><<<grid, 256, 0, st>>>(h0, p.ws_h, p.ws_d, p.B * p.H, p.nseg, reverse, pass_first);
+  else if (nrec <= 8)
+    gl::gla::gla_fold_kernel<8><<<grid, 256, 0, st>>>(h0, p.ws_h, p.ws_d, p.B * p.H, p.nseg, reverse, pass_first);
+  else
+    gl::gla::gla_fold_kernel<16><<<grid, 256, 0, st>>>(h0, p.ws_h, p.ws_d, p.B * p.H, p.nseg, reverse, pass_first);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return -2;
+  }
+  return 0;
 }
 
 // A second stream per device for the first phase of the forward split, and
@@ -1043,14 +1069,7 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
     }
     // Record 0 already holds the true state after segment 0: the fold
     // starts from it and leaves it unchanged.
-    const int64_t n1 = static_cast<int64_t>(p.B) * p.H * 128 * 128;
-    gl::gla::gla_fold_kernel<<<static_cast<unsigned>((n1 + 255) / 256), 256, 0, st>>>(
-        nullptr, p.ws_h, p.ws_d, p.B * p.H, p.nseg, 0, 1);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-      *why = cudaGetErrorString(e);
-      return -2;
-    }
+    if (int rc = launch_fold(nullptr, p, 0, 1, st, why)) return rc;
     p.seg_base = 1;
     p.seg_grid = p.nseg - 1;
     p.ht_seg = p.nseg - 1;
@@ -1070,14 +1089,7 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
                        : launch_pass<VS, gl::gla::MODE_FWD_STATE>(tq, tk, tv, tg, th, p1,
                                                                   items * p1.seg_grid, st, why);
     if (rc) return rc;
-    const int64_t n1 = static_cast<int64_t>(p.B) * p.H * 128 * 128;
-    gl::gla::gla_fold_kernel<<<static_cast<unsigned>((n1 + 255) / 256), 256, 0, st>>>(
-        p.h0, p.ws_h, p.ws_d, p.B * p.H, p.nseg, rev ? 1 : 0, 0);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-      *why = cudaGetErrorString(e);
-      return -2;
-    }
+    if (int rc2 = launch_fold(p.h0, p, rev ? 1 : 0, 0, st, why)) return rc2;
   }
   p.seg_grid = p.nseg;
   p.seg_base = 0;
