@@ -521,6 +521,38 @@ def headline_gmm(args, rank, world, local, peaks, peak_kind):
     return res
 
 
+def rw_rates(nbytes: int = 2 << 30, reps: int = 10):
+    """Write-only and read-only HBM rates of this GPU (GB/s), measured with
+    torch's fill and fp32 sum over a 2 GiB bf16 buffer (larger than L2),
+    median of `reps` CUDA-event timings.  Writes alone run well below reads
+    alone on B200 (about 3.9 vs 6.1 TB/s), which bounds the write-heavy
+    backward kernels."""
+    import statistics
+    import torch
+    buf = torch.empty(nbytes // 2, dtype=torch.bfloat16, device="cuda")
+
+    def med(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    w = nbytes / (med(lambda: buf.fill_(1.0)) * 1e-3) / 1e9
+    r = nbytes / (med(lambda: torch.sum(buf, dtype=torch.float32)) * 1e-3) / 1e9
+    del buf
+    return {"write_only_gbs": w, "read_only_gbs": r,
+            "how": "torch fill_ / fp32 sum over a 2 GiB bf16 buffer, median of 10 CUDA-event timings"}
+
+
 def secondary_gmm(args, workload, rank, world, peaks, peak_kind, with_extras: bool):
     """One instance of a grouped-matmul workload per rank (weak scaling), with
     its HBM / tensor roofline; with_extras adds the quantiser and backward rows."""
@@ -595,18 +627,33 @@ def secondary_gmm(args, workload, rank, world, peaks, peak_kind, with_extras: bo
                 + 2 * cfg.G * cfg.K * cfg.N)
     qc_bytes = grad.numel() * 3 + grad.numel() // 128 * 4
 
-    def row(ms_, by, fl):
+    # bytes written by each kernel (the rest of its algorithmic bytes are reads)
+    dl_w = 2 * cfg.M * cfg.K
+    tg_w = 2 * cfg.G * cfg.K * cfg.N
+    qc_w = grad.numel() + grad.numel() // 128 * 4
+    rw = rw_rates()
+
+    def row(ms_, by, fl, wr):
         g = by / (ms_ * 1e-3) / 1e9
-        r = {"ms": ms_, "achieved_gbs": g, "hbm_frac": g / peaks["hbm_gbs"], "algorithmic_bytes": by}
+        r = {"ms": ms_, "achieved_gbs": g, "hbm_frac": g / peaks["hbm_gbs"], "algorithmic_bytes": by,
+             "written_bytes": wr}
+        # floor of a kernel that reads R and writes W bytes: the slowest of the
+        # read-only, write-only and copy rates measured on this GPU
+        floor_ms = max((by - wr) / rw["read_only_gbs"], wr / rw["write_only_gbs"],
+                       by / peaks["hbm_gbs"]) / 1e6
+        r["rw_floor_ms"] = floor_ms
+        r["frac_of_rw_floor"] = floor_ms / ms_
         if fl:
             r["tflops"] = world * fl / (ms_ * 1e-3) / 1e12
             r["fp8_tensor_frac"] = fl / (ms_ * 1e-3) / 1e12 / fp8_peak
         return r
 
-    blk["bwd"] = {"dlhs": row(dl_ms, dl_bytes, flops), "tgmm": row(tg_ms, tg_bytes, flops),
-                  "quant_col_128x1": row(qc_ms, qc_bytes, 0.0),
+    blk["bwd"] = {"dlhs": row(dl_ms, dl_bytes, flops, dl_w), "tgmm": row(tg_ms, tg_bytes, flops, tg_w),
+                  "quant_col_128x1": row(qc_ms, qc_bytes, 0.0, qc_w),
+                  "rw_rates": rw,
                   "note": "dlhs = gl_gmm_fp8_dlhs (grouped kernel, K-major weight); tgmm writes "
-                          "drhs [G, K, N] bf16 for every group (empty ones as zeros)"}
+                          "drhs [G, K, N] bf16 for every group (empty ones as zeros), so it is "
+                          "bound by the write-only rate"}
     del grad, dq1, ds1, dq2, ds2, lq, ls, dlhs, drhs, lhs, rhs, a_q, a_s, b_q, b_s, out
     torch.cuda.empty_cache()
     return blk
