@@ -1,6 +1,14 @@
 """Shared comparison helpers for the parity tests."""
 import numpy as np
 
+# GLA forward (o and the final state) against the fp32 oracle:
+# |gpu - ref| <= GLA_RTOL |ref| + GLA_ATOL_FRAC rms(ref) element-wise and a
+# relative Frobenius error below GLA_FRO.  The absolute term holds the
+# reference template's own bf16 operand roundings, which a CPU emulation of
+# every one of its casts measures at up to 3.2 % of rms on the inputs of
+# tests/test_oracle_gla.py::test_reference_bf16_casts_stay_within_the_kernel_tolerance.
+GLA_RTOL, GLA_ATOL_FRAC, GLA_FRO = 2e-2, 4e-2, 1e-2
+
 
 def rms(x):
     x = np.asarray(x, np.float64)

@@ -2,17 +2,24 @@
 through the C ABI.  The launcher reads GLAUCIS_GLA_VS at every call, so
 each test runs on both kernel instances.
 
-Tolerance (o and the final state): |gpu - ref| <= 2e-2 * |ref| + 3e-2 * rms(ref)
-element-wise, plus a relative Frobenius error below 1e-2.  The kernel feeds
-the tensor cores bf16 operands (q e^G, k e^-G, tril(A), the state copy h_n)
-with fp32 accumulation and an fp32 recurrent state; the oracle is fp32
-throughout.  The reference itself casts q e^G and the state h to bf16 before
-its output dot (KE/examples/kernels/chunk_gla.py:204-205); with slowly
-decaying per-head gates that alone moves single outputs up to ~3 % of
-rms(o) from the fp32 oracle beyond the relative term
-(tests/test_oracle_gla.py::test_reference_bf16_casts_stay_within_the_kernel_tolerance),
-so the absolute term is 3e-2 * rms.  The kernel's further bf16 rounding of
-tril(A) adds well under 1e-2 * rms.
+Tolerance (o and the final state): |gpu - ref| <= 2e-2 * |ref| + 4e-2 * rms(ref)
+element-wise, plus a relative Frobenius error below 1e-2 (tests/helpers.py).
+The kernel feeds the tensor cores bf16 operands (q e^G, k e^-G, the state
+copy h_n, and tril(A) as a bf16 hi + lo pair or as one bf16 operand) with
+fp32 accumulation and an fp32 recurrent state; the oracle is fp32
+throughout.  The reference template rounds operands to bf16 as well: the
+decayed v of its state update (KE/examples/kernels/chunk_gla.py:79), q e^G
+and k e^-G before the intra-chunk A (:151-152), and q e^G and the state h
+before its output dot (:204-205).  Where an output is a near cancellation of
+its intra- and inter-chunk parts, those roundings alone move it up to 3.2 %
+of rms(o) from the fp32 oracle beyond the relative term (a CPU emulation of
+all of them, tests/test_oracle_gla.py::
+test_reference_bf16_casts_stay_within_the_kernel_tolerance, on the inputs of
+test_gla_more_sequences_than_sms among others), so the absolute term is
+4e-2 * rms.  The kernel's roundings are of the same kinds; on those inputs
+its largest deviation is of the same size (3.2-3.5 % of rms, one element of
+5.1 M), and its relative Frobenius error is the template emulation's
+(~2.5e-3).
 """
 import os
 
@@ -23,11 +30,11 @@ import torch
 from glaucis_b200 import configs, ops
 from oracle import gla_oracle as O
 from oracle.gmm_oracle import bf16_bits_to_f32
-from tests.helpers import assert_close, rel_fro
+from tests.helpers import GLA_ATOL_FRAC, GLA_FRO, GLA_RTOL, assert_close, rel_fro
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
-RTOL, ATOL_FRAC, FRO = 2e-2, 3e-2, 1e-2
+RTOL, ATOL_FRAC, FRO = GLA_RTOL, GLA_ATOL_FRAC, GLA_FRO
 
 
 @pytest.fixture(autouse=True, params=["64", "128"])
@@ -106,6 +113,15 @@ def test_gla_sequence_split_many_segments(cuda, monkeypatch):
     monkeypatch.setenv("GLAUCIS_GLA_SEGMENTS", "45")
     cfg = configs.GLAConfig("t", B=1, T=64 * 48, H=2, gate="per_key", h0_std=0.1)
     _check(*_run(cuda, cfg, seed=9), what="split 45")
+
+
+@pytest.mark.parametrize("gate", ["per_key", "gamma"])
+def test_gla_more_sequences_than_sms(cuda, gate):
+    # 4 x 52 = 208 (batch, head) pairs, one CTA each: more CTAs than the 148
+    # SMs, so a second wave of CTAs runs after the first frees its SMs.
+    cfg = configs.GLAConfig("t", B=4, T=64 * 3, H=52, gate=gate,
+                            h0_std=0.1 if gate == "per_key" else 0.0)
+    _check(*_run(cuda, cfg, seed=12), what=f"208 sequences {gate}")
 
 
 def test_gla_split_workspace_query(cuda):

@@ -136,6 +136,16 @@ def test_gmm_public_op_matches_oracle_end_to_end(cuda):
     assert rel_fro(got.cpu().numpy(), bf) < 0.15
 
 
+def test_gmm_every_group_empty(cuda):
+    # no rows in any group: no tiles; the public op returns an all-zero output
+    lhs = torch.randn((256, 256)).to(torch.bfloat16).to(cuda)
+    rhs = (torch.randn((3, 256, 384)) * 0.02).to(torch.bfloat16).to(cuda)
+    gs = torch.zeros(3, dtype=torch.int32, device=cuda)
+    out = ops.gmm_fp8_blockwise(lhs, rhs, gs)
+    assert ops.device_status() == 0
+    assert out.shape == (256, 384) and torch.count_nonzero(out) == 0
+
+
 def test_gmm_tail_rows_zero_in_public_op(cuda):
     lhs = torch.randn((300, 256)).to(torch.bfloat16).to(cuda)
     rhs = (torch.randn((2, 256, 256)) * 0.02).to(torch.bfloat16).to(cuda)

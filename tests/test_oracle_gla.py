@@ -147,35 +147,55 @@ def test_gla_chunked_bwd_oracle_against_autograd(gate, with_state):
         np.testing.assert_allclose(a, b, rtol=2e-4, atol=2e-4 * np.abs(b).max(), err_msg=name)
 
 
-def test_reference_bf16_casts_stay_within_the_kernel_tolerance():
-    # The reference's output kernel casts q e^G and the state h to bf16
-    # before its dot (KE/examples/kernels/chunk_gla.py:204-205).  With slowly
-    # decaying per-head gates that rounding alone moves single outputs by a
-    # few percent of rms(o) from the fp32 oracle; the GPU tests' absolute
-    # term (3e-2 * rms) is chosen to hold the reference's own deviation.
+def _template_casts_forward(q, k, v, g_gamma, scale, C):
+    """The reference template's forward for the per-head gate with every one
+    of its bf16 roundings (KE/examples/kernels/chunk_gla.py): the state
+    update adds k^T bf16(v e^{g_last - g}) to the fp32 state (:79-86), A =
+    bf16(q e^G) bf16(k e^-G)^T scale in fp32 (:151-156), and o = scale
+    bf16(q e^G) bf16(h) + tril(A) v in fp32 (:204-213).  float64 elsewhere."""
     import torch
-    from glaucis_b200 import configs
 
     def bf(x):
-        return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.bfloat16).float().numpy()
+        return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.bfloat16).double().numpy()
 
-    cfg = configs.GLAConfig("t", B=1, T=1024, H=8, gate="gamma")
-    inp = configs.make_gla_inputs(cfg, device="cpu", seed=3)
+    B, T, H, _ = q.shape
+    NT = T // C
+    q, k, v = (np.asarray(x, np.float64) for x in (q, k, v))
+    o = np.zeros(v.shape)
+    mask = np.tril(np.ones((C, C)))
+    for h in range(H):
+        G = float(g_gamma[h]) * (np.arange(C) + 1)
+        for b in range(B):
+            s = np.zeros((q.shape[-1], v.shape[-1]))
+            for n in range(NT):
+                sl = slice(n * C, (n + 1) * C)
+                qc, kc, vc = q[b, sl, h], k[b, sl, h], v[b, sl, h]
+                qg, kg = bf(qc * np.exp(G)[:, None]), bf(kc * np.exp(-G)[:, None])
+                A = (qg @ kg.T) * scale * mask
+                o[b, sl, h] = scale * (qg @ bf(s)) + A @ vc
+                s = s * np.exp(G[-1]) + kc.T @ bf(vc * np.exp(G[-1] - G)[:, None])
+    return o
+
+
+@pytest.mark.parametrize("B,T,H,seed", [(1, 1024, 8, 3), (4, 192, 52, 12)])
+def test_reference_bf16_casts_stay_within_the_kernel_tolerance(B, T, H, seed):
+    # The reference template's own bf16 roundings move single outputs, where
+    # the intra- and inter-chunk parts nearly cancel, by a few percent of
+    # rms(o) from the fp32 oracle; the GPU tests' absolute term must hold
+    # that deviation (the second case is test_gla_more_sequences_than_sms's
+    # gamma-gate input, where it reaches 3.2 % of rms).
+    from glaucis_b200 import configs
+    from tests.helpers import GLA_ATOL_FRAC, GLA_FRO, GLA_RTOL
+
+    cfg = configs.GLAConfig("t", B=B, T=T, H=H, gate="gamma")
+    inp = configs.make_gla_inputs(cfg, device="cpu", seed=seed)
     q, k, v = (inp[n].float().numpy() for n in ("q", "k", "v"))
     gg = inp["g_gamma"].numpy()
     scale = np.float32(cfg.K ** -0.5)
-    ref_o, _, h_all = O.chunk_gla_fwd(q, k, v, g_gamma=gg, scale=scale, return_states=True)
-    B, T, H, K, C = 1, cfg.T, cfg.H, cfg.K, cfg.C
-    NT = T // C
-    gc = O.g_cumsum_from(None, gg, B, T, H, K, C).reshape(B, NT, C, H, K)
-    qc, kc, vc = (x.reshape(B, NT, C, H, -1) for x in (q, k, v))
-    qg = bf(qc * np.exp(gc))                               # the reference's bf16 q e^G
-    A = np.einsum("bnihk,bnjhk->bnhij", qc * np.exp(gc), kc * np.exp(-gc)) * scale
-    A = A * np.tril(np.ones((C, C), np.float32))
-    o = scale * np.einsum("bnchk,bnhkv->bnchv", qg, bf(h_all)) + np.einsum("bnhij,bnjhv->bnihv", A, vc)
-    o = o.reshape(ref_o.shape)
+    ref_o, _ = O.chunk_gla_fwd(q, k, v, g_gamma=gg, scale=scale)
+    o = _template_casts_forward(q, k, v, gg, float(scale), cfg.C)
     rms = float(np.sqrt(np.mean(ref_o.astype(np.float64) ** 2)))
-    excess = float(np.max(np.maximum(np.abs(o - ref_o) - 2e-2 * np.abs(ref_o), 0.0))) / rms
-    print(f"reference casts: largest deviation beyond 2e-2*|ref| = {excess:.4f} * rms")
-    assert excess < 3e-2
-    assert np.linalg.norm(o - ref_o) / np.linalg.norm(ref_o) < 1e-2
+    excess = float(np.max(np.maximum(np.abs(o - ref_o) - GLA_RTOL * np.abs(ref_o), 0.0))) / rms
+    print(f"reference casts: largest deviation beyond {GLA_RTOL}*|ref| = {excess:.4f} * rms")
+    assert excess < GLA_ATOL_FRAC
+    assert np.linalg.norm(o - ref_o) / np.linalg.norm(ref_o) < GLA_FRO
