@@ -74,7 +74,16 @@ struct Cfg {
   static constexpr uint32_t OFF_PART = OFF_DEC + 2 * KD * 4;  // [2][8 warps][32 lanes] float4
   static constexpr uint32_t OFF_BAR = OFF_PART + 2 * 8 * 32 * 16;
   static constexpr uint32_t OFF_MISC = OFF_BAR + 512;
-  static constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;
+  // O leaves through shared memory and TMA stores where the room is there
+  // (the kSplit instance at VS = 128, which gave up a 48 KB ring stage for an
+  // 8 KB P buffer): per gating warp a 2 KB slot (its 16 rows x 64 columns,
+  // 128B-swizzled), two slots deep.  Elsewhere the gating warps store O to
+  // global memory from registers.
+  static constexpr bool O_STG = kSplit && VS == 128;
+  static constexpr uint32_t OSTG_SLOT = 16 * 64 * 2;
+  static constexpr uint32_t OFF_OSTG = (OFF_MISC + 64 + 1023) / 1024 * 1024;
+  static constexpr uint32_t OSTG_BYTES = O_STG ? 2 * 8 * OSTG_SLOT : 0;
+  static constexpr uint32_t SMEM_BYTES = OFF_OSTG + OSTG_BYTES + 1024;
   // TMEM columns: A0, A1 [0,128), O0, O1 [128,128+2VS), S0 (, S1) from 128+2VS
   static constexpr uint32_t COL_A = 0, COL_O = 128, COL_S = 128 + 2 * VS;
   static_assert(COL_S + NS * VS <= 512, "TMEM columns");
@@ -184,7 +193,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v,
                          const __grid_constant__ CUtensorMap tm_g,
-                         const __grid_constant__ CUtensorMap tm_h, const Params p) {
+                         const __grid_constant__ CUtensorMap tm_h,
+                         const __grid_constant__ CUtensorMap tm_o, const Params p) {
   using CF = Cfg<VS, kSplit>;
   // kStateOnly: S_n = (k slot)^T (v slot) only (no q, A, O).  kRev: chunks
   // in reverse order, the k slot scaled like q (Qs) instead of k (Kg).
@@ -466,7 +476,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 pack_bf16x2(__uint_as_float(ov[8 * i + 6]), __uint_as_float(ov[8 * i + 7])));
         }
       };
-      if constexpr (OC == 64) {
+      if constexpr (CF::O_STG) {
+        // this warp's 16 rows x 64 columns -> its slot (row = lane, 16-byte
+        // chunk c at c ^ (row & 7): the 128B swizzle of the map) -> one TMA
+        // store of a 64 x 1 x 16 box
+        uint32_t ov0[32], ov1[32];
+        tmem_ld32(o_lane + s * VS, ov0);
+        tmem_ld32(o_lane + s * VS + 32, ov1);
+        uint8_t* slot = smem + CF::OFF_OSTG + ((m & 1) * GATE_WARPS + (warp - 4)) * CF::OSTG_SLOT;
+        if (lane == 0) bulk_wait_read<1>();  // the store of chunk m-2 has read this slot
+        tmem_ld_wait2(ov0, ov1);
+        __syncwarp();
+        if (lane < 16) {
+          const uint32_t srow = smem_u32(slot) + lane * 128u;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t* w = c < 4 ? ov0 + 8 * c : ov1 + 8 * (c - 4);
+            st_shared_v4(srow + ((c ^ (lane & 7)) << 4),
+                         pack_bf16x2(__uint_as_float(w[0]), __uint_as_float(w[1])),
+                         pack_bf16x2(__uint_as_float(w[2]), __uint_as_float(w[3])),
+                         pack_bf16x2(__uint_as_float(w[4]), __uint_as_float(w[5])),
+                         pack_bf16x2(__uint_as_float(w[6]), __uint_as_float(w[7])));
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&tm_o, slot, v0 + ohalf * OC, h, tok0 + m * C + oquad * 16);
+          bulk_commit();
+        }
+      } else if constexpr (OC == 64) {
         // both column halves in flight before one wait
         uint32_t ov0[32], ov1[32];
         tmem_ld32(o_lane + s * VS, ov0);
@@ -597,6 +636,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     if (!kStateOnly)
       for (int m = NT >= 2 ? NT - 2 : 0; m < NT && gok; ++m) gok = o_epilogue(m);
+    if constexpr (CF::O_STG && !kStateOnly) {
+      if (lane == 0) bulk_wait<0>();  // the O stores are complete before the CTA exits
+      __syncwarp();
+    }
   } else if (warp >= 4 + GATE_WARPS) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_STATE));
     // ------------------------- P epilogue, state update, O epilogue
@@ -971,16 +1014,16 @@ static size_t gla_ws_bytes(int64_t B, int64_t H, int nseg) {
 
 template <int VS, int kMode, bool kSplit = false>
 static int launch_pass(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                       const CUtensorMap& tg, const CUtensorMap& th, const gl::gla::Params& p,
-                       int grid, cudaStream_t st, const char** why) {
+                       const CUtensorMap& tg, const CUtensorMap& th, const CUtensorMap& to,
+                       const gl::gla::Params& p, int grid, cudaStream_t st, const char** why) {
   if constexpr (kMode == gl::gla::MODE_FWD && !kSplit) {
-    if (p.p_split) return launch_pass<VS, kMode, true>(tq, tk, tv, tg, th, p, grid, st, why);
+    if (p.p_split) return launch_pass<VS, kMode, true>(tq, tk, tv, tg, th, to, p, grid, st, why);
   }
   using CF = gl::gla::Cfg<VS, kSplit>;
   const void* fn = reinterpret_cast<const void*>(gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit>);
   if (!gl_set_smem_attr(fn, 0, static_cast<int>(CF::SMEM_BYTES), why)) return -2;
   gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit><<<grid, gl::gla::NUM_THREADS, CF::SMEM_BYTES, st>>>(
-      tq, tk, tv, tg, th, p);
+      tq, tk, tv, tg, th, to, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     *why = cudaGetErrorString(e);
@@ -1027,6 +1070,16 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
   } else {
     th = tk;  // unused
   }
+  CUtensorMap to;
+  if (!rev && VS == 128 && p.o != nullptr) {
+    // o [B*T, H, 128] bf16, boxes of 64 columns x 1 head x 16 rows: one
+    // gating warp's share of a chunk's O (used by the kSplit instance)
+    if (!gl_make_tmap_3d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.o, 128, p.H, BT, 128,
+                         static_cast<int64_t>(p.H) * 128, 64, 1, 16, CU_TENSOR_MAP_SWIZZLE_128B, why))
+      return -1;
+  } else {
+    to = tk;  // unused
+  }
   const int items = p.B * p.H * p.nsplit;
   if (p.nseg > 1 && !rev && p.c_first > 0) {
     // Phase 1: segment 0's full pass (from h0; its final state becomes
@@ -1053,11 +1106,11 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
         ps.seg_grid = p.nseg - 2;
         ps.rec_base = 0;
         ps.has_hout = 0;
-        if (int rc = launch_pass<VS, gl::gla::MODE_FWD_STATE>(tq, tk, tv, tg, th, ps, items * ps.seg_grid,
+        if (int rc = launch_pass<VS, gl::gla::MODE_FWD_STATE>(tq, tk, tv, tg, th, to, ps, items * ps.seg_grid,
                                                               ss->s, why))
           return rc;
       }
-      const int rc_a = launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, pa, items, st, why);
+      const int rc_a = launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, to, pa, items, st, why);
       // join even when that launch failed, so that nothing of this call runs
       // on the side stream after the caller's stream has moved on
       if (ss != nullptr &&
@@ -1074,7 +1127,7 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
     p.seg_grid = p.nseg - 1;
     p.ht_seg = p.nseg - 1;
     p.has_hout = sout != nullptr;
-    return launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, p, items * p.seg_grid, st, why);
+    return launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, to, p, items * p.seg_grid, st, why);
   }
   if (p.nseg > 1) {
     // State-only pass over segments 0 .. nseg-2 (reverse: 1 .. nseg-1), the
@@ -1084,9 +1137,9 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
     p1.seg_base = rev ? 1 : 0;
     p1.rec_base = p1.seg_base;
     p1.has_hout = 0;
-    const int rc = rev ? launch_pass<VS, gl::gla::MODE_DH_STATE>(tq, tk, tv, tg, th, p1,
+    const int rc = rev ? launch_pass<VS, gl::gla::MODE_DH_STATE>(tq, tk, tv, tg, th, to, p1,
                                                                  items * p1.seg_grid, st, why)
-                       : launch_pass<VS, gl::gla::MODE_FWD_STATE>(tq, tk, tv, tg, th, p1,
+                       : launch_pass<VS, gl::gla::MODE_FWD_STATE>(tq, tk, tv, tg, th, to, p1,
                                                                   items * p1.seg_grid, st, why);
     if (rc) return rc;
     if (int rc2 = launch_fold(p.h0, p, rev ? 1 : 0, 0, st, why)) return rc2;
@@ -1095,8 +1148,8 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
   p.seg_base = 0;
   p.ht_seg = rev ? 0 : p.nseg - 1;
   p.has_hout = sout != nullptr;
-  return rev ? launch_pass<VS, gl::gla::MODE_DH>(tq, tk, tv, tg, th, p, items * p.nseg, st, why)
-             : launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, p, items * p.nseg, st, why);
+  return rev ? launch_pass<VS, gl::gla::MODE_DH>(tq, tk, tv, tg, th, to, p, items * p.nseg, st, why)
+             : launch_pass<VS, gl::gla::MODE_FWD>(tq, tk, tv, tg, th, to, p, items * p.nseg, st, why);
 }
 
 size_t gl_chunk_gla_ws_bytes(int64_t B, int64_t T, int64_t H, int num_sms) {
