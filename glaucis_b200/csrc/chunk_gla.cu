@@ -83,7 +83,7 @@ struct Cfg {
   static constexpr uint32_t OSTG_SLOT = 16 * 64 * 2;
   static constexpr uint32_t OFF_OSTG = (OFF_MISC + 64 + 1023) / 1024 * 1024;
   static constexpr uint32_t OSTG_BYTES = O_STG ? 2 * 8 * OSTG_SLOT : 0;
-  static constexpr uint32_t SMEM_BYTES = OFF_OSTG + OSTG_BYTES + 1024;
+  static constexpr uint32_t SMEM_BYTES = O_STG ? OFF_OSTG + OSTG_BYTES + 1024 : OFF_MISC + 64 + 1024;
   // TMEM columns: A0, A1 [0,128), O0, O1 [128,128+2VS), S0 (, S1) from 128+2VS
   static constexpr uint32_t COL_A = 0, COL_O = 128, COL_S = 128 + 2 * VS;
   static_assert(COL_S + NS * VS <= 512, "TMEM columns");
