@@ -589,6 +589,25 @@ def secondary_gmm(args, workload, rank, world, peaks, peak_kind, with_extras: bo
                         "algorithmic_bytes_per_launch": alg_bytes,
                         "algorithmic_flops_per_launch": flops, "kernel": "gmm_fp8_fwd_kernel",
                         "peak_source": f"{peak_kind} hbm_gbs / 2 x {peak_kind} bf16_tflops"}}
+    if workload == SMALL_WORKLOAD:
+        # A problem this small is bound by the launch path of the eager call
+        # (Python, tensor-map encoding, launch), so the same call is also
+        # captured once in a CUDA graph and replayed: the row's device rate.
+        fn = lambda: ops.gmm_fp8_fwd(a_q, a_s, b_q, b_s, gs, out=out)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        g_ms = timed(graph.replay, args.steps, args.warmup, world)
+        blk["graph"] = {"ms_per_step": g_ms, "tflops": world * flops / (g_ms * 1e-3) / 1e12,
+                        "how": "the same gmm_fp8_fwd call captured in a torch.cuda.CUDAGraph and "
+                               "replayed; the eager ms_per_step includes the launch path"}
+        del graph
     if not with_extras:
         del lhs, rhs, a_q, a_s, b_q, b_s, out
         torch.cuda.empty_cache()
