@@ -1,5 +1,6 @@
 """numpy stand-in for the `jax` names the reference's jnp GLA code uses
-(test infrastructure for tests/golden/make_ref_golden.py; see README.md)."""
+(test infrastructure: only tests/golden/make_ref_golden.py imports it, to run
+the reference's jnp code unchanged where JAX is not installed)."""
 import numpy as _np
 
 from . import lax, numpy  # noqa: F401

@@ -1,5 +1,5 @@
 """numpy stand-in for the jax.lax names the reference's jnp GLA code uses:
-Precision, dot_general, scan, iota (see README.md)."""
+Precision, dot_general, scan, iota."""
 import string
 
 import numpy as _np

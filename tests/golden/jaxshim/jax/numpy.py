@@ -1,4 +1,4 @@
-"""numpy stand-in for jax.numpy (see README.md).  Elementwise functions are
+"""numpy stand-in for jax.numpy.  Elementwise functions are
 numpy's own; contractions run in float64 and are rounded to the JAX result
 type (float32 unless every operand is bfloat16)."""
 import ml_dtypes as _ml
