@@ -264,6 +264,15 @@ def test_gmm_bf16_output_is_the_rounded_fp32_output(cuda, K, N):
         assert torch.equal(o16[:total], o32[:total].to(torch.bfloat16)), name
 
 
+def test_gmm_many_small_groups(cuda):
+    # 700 groups of 0-24 rows (a third of them empty): one tile per non-empty
+    # group, most of each tile padding, the tile table near its 1024-group
+    # limit, several tiles per CTA
+    rng = np.random.default_rng(77)
+    sizes = [int(x) if rng.random() > 0.33 else 0 for x in rng.integers(1, 25, size=700)]
+    _gmm_case(cuda, len(sizes), sum(sizes) + 5, 256, 384, sizes, seed=77)
+
+
 @pytest.mark.parametrize("seed", range(6))
 def test_gmm_random_ragged_shapes(cuda, seed):
     # Seeded random problems: group counts from 1 to 40 with empty groups and
