@@ -47,15 +47,17 @@ constexpr int REG_CTRL = 40, REG_STATE = 216;
 static_assert(128 * REG_CTRL + 256 * 128 + 128 * REG_STATE <= NUM_THREADS * 128,
               "register split exceeds the launch allocation");
 
-template <int VS, bool kSplit = false>
+template <int VS, bool kSplit = false, bool kFwd = false>
 struct Cfg {
   // q/k/v ring depth: a stage is released only once O of its chunk has
   // completed, so the load of chunk n+3 waits for the A -> P -> O chain of
   // chunk n.  The raw gate has one buffer, reloaded for chunk n+1 as soon as
   // the gating of chunk n has read it.  The S accumulator is double-buffered
-  // in TMEM when its columns fit (VS = 64).  kSplit (P as a bf16 hi + lo
-  // pair) needs a second P buffer: it gives up the third ring stage.
-  static constexpr int QS = kSplit ? 2 : 3;
+  // in TMEM when its columns fit (VS = 64).  The forward at VS = 128 (kFwd)
+  // gives up the third ring stage for the O staging slots below (and kSplit,
+  // P as a bf16 hi + lo pair, for its second P buffer as well): measured
+  // faster than three stages with O stored from registers.
+  static constexpr int QS = (kSplit || (kFwd && VS == 128)) ? 2 : 3;
   static constexpr int NS = VS == 64 ? 2 : 1;
   static constexpr int V_BOXES = VS / 64;
   static constexpr uint32_t Q_BYTES = C * KD * 2;          // 16 KB (2 boxes of 64 features)
@@ -74,12 +76,11 @@ struct Cfg {
   static constexpr uint32_t OFF_PART = OFF_DEC + 2 * KD * 4;  // [2][8 warps][32 lanes] float4
   static constexpr uint32_t OFF_BAR = OFF_PART + 2 * 8 * 32 * 16;
   static constexpr uint32_t OFF_MISC = OFF_BAR + 512;
-  // O leaves through shared memory and TMA stores where the room is there
-  // (the kSplit instance at VS = 128, which gave up a 48 KB ring stage for an
-  // 8 KB P buffer): per gating warp a 2 KB slot (its 16 rows x 64 columns,
-  // 128B-swizzled), two slots deep.  Elsewhere the gating warps store O to
-  // global memory from registers.
-  static constexpr bool O_STG = kSplit && VS == 128;
+  // The forward at VS = 128 sends O through shared memory and TMA stores:
+  // per gating warp a 2 KB slot (its 16 rows x 64 columns, 128B-swizzled),
+  // two slots deep.  At VS = 64 the gating warps store O to global memory
+  // from registers.
+  static constexpr bool O_STG = kFwd && VS == 128;
   static constexpr uint32_t OSTG_SLOT = 16 * 64 * 2;
   static constexpr uint32_t OFF_OSTG = (OFF_MISC + 64 + 1023) / 1024 * 1024;
   static constexpr uint32_t OSTG_BYTES = O_STG ? 2 * 8 * OSTG_SLOT : 0;
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                          const __grid_constant__ CUtensorMap tm_g,
                          const __grid_constant__ CUtensorMap tm_h,
                          const __grid_constant__ CUtensorMap tm_o, const Params p) {
-  using CF = Cfg<VS, kSplit>;
+  using CF = Cfg<VS, kSplit, kMode == MODE_FWD>;
   // kStateOnly: S_n = (k slot)^T (v slot) only (no q, A, O).  kRev: chunks
   // in reverse order, the k slot scaled like q (Qs) instead of k (Kg).
   constexpr bool kStateOnly = kMode != MODE_FWD;
@@ -1019,7 +1020,7 @@ static int launch_pass(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
   if constexpr (kMode == gl::gla::MODE_FWD && !kSplit) {
     if (p.p_split) return launch_pass<VS, kMode, true>(tq, tk, tv, tg, th, to, p, grid, st, why);
   }
-  using CF = gl::gla::Cfg<VS, kSplit>;
+  using CF = gl::gla::Cfg<VS, kSplit, kMode == gl::gla::MODE_FWD>;
   const void* fn = reinterpret_cast<const void*>(gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit>);
   if (!gl_set_smem_attr(fn, 0, static_cast<int>(CF::SMEM_BYTES), why)) return -2;
   gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit><<<grid, gl::gla::NUM_THREADS, CF::SMEM_BYTES, st>>>(
