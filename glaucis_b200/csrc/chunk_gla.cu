@@ -27,13 +27,15 @@
 //   warps 4-11    gating (warp = 8 tokens, lane = 4 keys): chunk-local cumsum
 //                 of the gate (per-warp prefixes exchanged through shared
 //                 memory), Qs, Kg in place, e^{G_last}; then the O epilogue
-//                 of the chunk two behind (TMEM -> bf16 -> HBM)
+//                 of the chunk two behind (TMEM -> bf16 -> HBM; at VS = 128
+//                 through per-warp shared-memory slots and TMA stores)
 //   warps 12-15   state warpgroup: A -> tril -> bf16 P, state update
 //                 (thread = key row, VS fp32 columns in registers)
-// Buffers: one g buffer, q/k/v in a 3-stage ring (2 stages in the kSplit
-// instance, whose second P buffer takes the third stage's room); A and O
-// double-buffered in TMEM, S double-buffered when VS = 64; P (P_hi, P_lo) and
-// the bf16 state copy H single-buffered (rewritten only after O_n completed).
+// Buffers: one g buffer, q/k/v in a 3-stage ring (2 stages in the forward at
+// VS = 128, whose O slots, and in the kSplit instance also the second P
+// buffer, take the third stage's room); A and O double-buffered in TMEM, S
+// double-buffered when VS = 64; P (P_hi, P_lo) and the bf16 state copy H
+// single-buffered (rewritten only after O_n completed).
 #include "common.cuh"
 
 namespace gl {
