@@ -45,8 +45,9 @@ __device__ __forceinline__ uint16_t cvt_e4m3x2(float lo, float hi) {
 // exact only while it stays above the subnormal range: with s >= 2^-64 every
 // element whose quotient can reach a non-zero e4m3 value has |x| >= 2^-74, far
 // from it.  Blocks with smaller (or non-finite) scales take the plain
-// division.  A quotient by s > 0 has the sign of x, which copysign restores
-// for x = -0.  The arithmetic runs on packed f32x2 FMAs.  Tests compare this
+// division.  A quotient by s > 0 has the sign of x; the packed form
+// (markstein2) works on -x and -y so that x = -0 keeps its sign without a
+// copysign.  The arithmetic runs on packed f32x2 FMAs.  Tests compare this
 // path with IEEE division for every finite bf16 block maximum and every bf16
 // element value.
 struct BlockDiv {
@@ -57,10 +58,31 @@ struct BlockDiv {
     fast = scale >= 0x1p-64f && scale <= 3.40282347e38f;
     y = 1.0f / scale;
   }
+  // recip = 1.0f / scale computed elsewhere (the same IEEE division)
+  __device__ __forceinline__ BlockDiv(float scale, float recip) : s(scale), y(recip) {
+    fast = scale >= 0x1p-64f && scale <= 3.40282347e38f;
+  }
 };
 
 __device__ __forceinline__ float2 bf16x2_to_f32x2(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+// The two bf16 values of w as negated floats (sign bit flipped in the same
+// integer operation that widens them).
+__device__ __forceinline__ float2 bf16x2_to_neg_f32x2(uint32_t w) {
+  return make_float2(__uint_as_float((w << 16) ^ 0x80000000u), __uint_as_float((w & 0xFFFF0000u) ^ 0x80000000u));
+}
+
+// Markstein's quotient of two elements on packed FMAs, in negated form so
+// that zeros keep their sign without a copysign: with nx = -x and ny = -y,
+// q = nx ny = RN(x y), r' = RN(q s + nx) = q s - x (exact, = -r),
+// v = RN(r' ny + q) = RN(q + r y).  For x = +0: q = +0, r' = +0,
+// v = -0 + +0 = +0; for x = -0: q = -0, r' = +0, v = -0 + -0 = -0.
+__device__ __forceinline__ float2 markstein2(float2 nx, float2 ny, float2 s) {
+  const float2 q = __fmul2_rn(nx, ny);
+  const float2 r = __ffma2_rn(q, s, nx);
+  return __ffma2_rn(r, ny, q);
 }
 
 // Eight bf16 values (one 16-byte chunk) -> eight e4m3 bytes.
@@ -68,14 +90,11 @@ __device__ __forceinline__ uint2 quant8(const uint4& u, const BlockDiv& d) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
   uint32_t p[4];
   if (d.fast) {
-    const float2 y2 = make_float2(d.y, d.y), ns2 = make_float2(-d.s, -d.s);
+    const float2 ny2 = make_float2(-d.y, -d.y), s2 = make_float2(d.s, d.s);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 x = bf16x2_to_f32x2(w[i]);
-      const float2 q = __fmul2_rn(x, y2);
-      const float2 r = __ffma2_rn(q, ns2, x);
-      const float2 v = __ffma2_rn(r, y2, q);
-      p[i] = cvt_e4m3x2(copysignf(v.x, x.x), copysignf(v.y, x.y));
+      const float2 v = markstein2(bf16x2_to_neg_f32x2(w[i]), ny2, s2);
+      p[i] = cvt_e4m3x2(v.x, v.y);
     }
   } else {
 #pragma unroll
@@ -99,16 +118,14 @@ __device__ __forceinline__ uint2 quant8_cols(const uint4& u, const BlockDiv (&d)
   uint32_t p[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float2 x = bf16x2_to_f32x2(w[i]);
     const BlockDiv& d0 = d[2 * i];
     const BlockDiv& d1 = d[2 * i + 1];
     if (d0.fast && d1.fast) {
-      const float2 y2 = make_float2(d0.y, d1.y), ns2 = make_float2(-d0.s, -d1.s);
-      const float2 q = __fmul2_rn(x, y2);
-      const float2 r = __ffma2_rn(q, ns2, x);
-      const float2 v = __ffma2_rn(r, y2, q);
-      p[i] = cvt_e4m3x2(copysignf(v.x, x.x), copysignf(v.y, x.y));
+      const float2 v = markstein2(bf16x2_to_neg_f32x2(w[i]), make_float2(-d0.y, -d1.y),
+                                  make_float2(d0.s, d1.s));
+      p[i] = cvt_e4m3x2(v.x, v.y);
     } else {
+      const float2 x = bf16x2_to_f32x2(w[i]);
       p[i] = cvt_e4m3x2(div1(x.x, d0), div1(x.y, d1));
     }
   }
@@ -153,7 +170,11 @@ struct Layout {
   static constexpr int RED_PER_WARP = kMode == COL ? 128 : 1;
   static constexpr uint32_t OFF_BAR = STAGES * IN_BYTES;
   static constexpr uint32_t OFF_RED = OFF_BAR + 2 * STAGES * 8;
-  static constexpr uint32_t OFF_FLAG = OFF_RED + W_GROUPS * 2 * W_GROUP_WARPS * RED_PER_WARP * 4;
+  // COL: per group, the tile's 128 column scales and their reciprocals,
+  // computed once per column by the thread that owns it
+  static constexpr uint32_t OFF_CSC = OFF_RED + W_GROUPS * 2 * W_GROUP_WARPS * RED_PER_WARP * 4;
+  static constexpr uint32_t CSC_BYTES = kMode == COL ? W_GROUPS * 2 * 128 * 4 : 0;
+  static constexpr uint32_t OFF_FLAG = OFF_CSC + CSC_BYTES;
   static constexpr uint32_t SMEM_BYTES = OFF_FLAG + 16 + 1024;  // + slack for 1 KB alignment
 };
 
@@ -269,28 +290,30 @@ __global__ void __launch_bounds__(THREADS, Ring<kMode>::CTAS_PER_SM)
         for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (lane == 0) r[gw] = m;
       } else {
-        // per-column maxima over this thread's 16 rows, then over the two
-        // row groups of the warp (lanes l and l ^ 16 share the chunk)
-        float cm[8];
+        // per-column maxima over this thread's 16 rows on packed bf16 (exact:
+        // the maximum is one of the values), then over the two row groups of
+        // the warp (lanes l and l ^ 16 share the chunk)
+        __nv_bfloat162 cm2[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) cm[e] = 0.f;
+        for (int h = 0; h < 4; ++h) cm2[h] = __floats2bfloat162_rn(0.f, 0.f);
 #pragma unroll 4
         for (int j = 0; j < 16; ++j) {
           const uint4 u = in[tg + 128 * j];
-          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+          const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const float2 v = bf16x2_to_f32x2(w[h]);
-            cm[2 * h] = fmaxf(cm[2 * h], fabsf(v.x));
-            cm[2 * h + 1] = fmaxf(cm[2 * h + 1], fabsf(v.y));
-          }
+          for (int h = 0; h < 4; ++h) cm2[h] = __hmax2(cm2[h], __habs2(hv[h]));
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) cm[e] = fmaxf(cm[e], __shfl_xor_sync(0xffffffffu, cm[e], 16));
+        for (int h = 0; h < 4; ++h) {
+          const uint32_t o = __shfl_xor_sync(0xffffffffu, *reinterpret_cast<const uint32_t*>(&cm2[h]), 16);
+          cm2[h] = __hmax2(cm2[h], *reinterpret_cast<const __nv_bfloat162*>(&o));
+        }
         if (lane < 16) {
           float4* rc = reinterpret_cast<float4*>(r + gw * 128 + c16 * 8);
-          rc[0] = make_float4(cm[0], cm[1], cm[2], cm[3]);
-          rc[1] = make_float4(cm[4], cm[5], cm[6], cm[7]);
+          rc[0] = make_float4(__low2float(cm2[0]), __high2float(cm2[0]), __low2float(cm2[1]),
+                              __high2float(cm2[1]));
+          rc[1] = make_float4(__low2float(cm2[2]), __high2float(cm2[2]), __low2float(cm2[3]),
+                              __high2float(cm2[3]));
         }
       }
       if (bar_or(1 + grp, W_GROUP_WARPS * 32, !ok || *static_cast<volatile int*>(abort_flag))) break;
@@ -313,20 +336,23 @@ __global__ void __launch_bounds__(THREADS, Ring<kMode>::CTAS_PER_SM)
         if (lane == 0) mbar_arrive(&empty[st]);
         if (tg == 0) a.s[(y / 128) * NB + x / 128] = sc;  // s[g, kb, nb]; y / 128 = g * KB + kb
       } else {
-        float cm[8];
+        // thread tg owns column tg of the tile: its maximum over the group's
+        // warps, its scale (also stored to s[row block, column]) and the
+        // scale's reciprocal, shared through shared memory
+        float* csc = reinterpret_cast<float*>(smem + L::OFF_CSC) + grp * 256;
+        {
+          float m = r[tg];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) cm[e] = r[c16 * 8 + e];
-#pragma unroll
-        for (int w = 1; w < W_GROUP_WARPS; ++w)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) cm[e] = fmaxf(cm[e], r[w * 128 + c16 * 8 + e]);
-        float sc[8];
+          for (int w = 1; w < W_GROUP_WARPS; ++w) m = fmaxf(m, r[w * 128 + tg]);
+          const float sc1 = scale_of(m);
+          csc[tg] = sc1;
+          csc[128 + tg] = 1.0f / sc1;
+          a.s[static_cast<int64_t>(y / 128) * a.K + x + tg] = sc1;
+        }
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(W_GROUP_WARPS * 32) : "memory");
         BlockDiv div[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          sc[e] = scale_of(cm[e]);
-          div[e] = BlockDiv(sc[e]);
-        }
+        for (int e = 0; e < 8; ++e) div[e] = BlockDiv(csc[c16 * 8 + e], csc[128 + c16 * 8 + e]);
 #pragma unroll 4
         for (int j = 0; j < 16; ++j) {
           const int row = (tg >> 4) + 8 * j;
@@ -335,11 +361,6 @@ __global__ void __launch_bounds__(THREADS, Ring<kMode>::CTAS_PER_SM)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
-        if (tg < 16) {  // s[row block, column]
-          float4* sd = reinterpret_cast<float4*>(a.s + static_cast<int64_t>(y / 128) * a.K + x + c16 * 8);
-          sd[0] = make_float4(sc[0], sc[1], sc[2], sc[3]);
-          sd[1] = make_float4(sc[4], sc[5], sc[6], sc[7]);
-        }
       }
     }
   } else {

@@ -48,6 +48,23 @@ def test_quant_col_bit_exact(cuda):
     assert np.array_equal(s.cpu().numpy(), rs)
 
 
+def test_quant_col_bit_exact_more_tiles(cuda):
+    # 8 x 6 tiles: per-column maxima over 128 rows, scales shared by the
+    # column owners, a block small enough for the plain-division path
+    # (scale < 2^-64), a block of negative zeros, huge and tiny columns
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn((1024, 768), generator=g) * torch.logspace(-4, 3, 768)[None, :]
+    x[128:256, 9] = torch.randn(128, generator=g) * 1e-30
+    x[256:384, 11] = -0.0
+    x[512:640, 700:704] *= 1e20
+    x = x.to(torch.bfloat16)
+    q, s = ops.quant_col_128x1(x.to(cuda))
+    assert ops.device_status() == 0
+    rq, rs = B.quant_col_128x1(x.float().numpy())
+    assert np.array_equal(_bytes(q), rq)
+    assert np.array_equal(s.cpu().numpy(), rs)
+
+
 @pytest.mark.parametrize("sizes,N", [([100, 0, 300, 128, 100], 384), ([512], 256), ([0, 0, 640], 512)])
 def test_dlhs_matches_oracle(cuda, sizes, N):
     G, M, K = len(sizes), 640, 384
