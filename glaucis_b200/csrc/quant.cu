@@ -156,6 +156,16 @@ namespace quant {
 enum Mode : int { ACT = 0, WEIGHT = 1, COL = 2 };
 template <int kMode> struct Ring { static constexpr int STAGES = 4, CTAS_PER_SM = 1; };
 template <> struct Ring<ACT> { static constexpr int STAGES = 3, CTAS_PER_SM = 2; };
+// COL tiles are 128 rows x 64 columns (16 KB), so that each of the four warp
+// groups has two stages of the ring: the next tile of a group loads while the
+// group quantises the current one (with 32 KB tiles a group owns one stage
+// and waits for every load).
+template <> struct Ring<COL> { static constexpr int STAGES = 8, CTAS_PER_SM = 1; };
+template <int kMode> struct TileShape {
+  static constexpr int W = kMode == COL ? 64 : 128;         // columns of a tile
+  static constexpr uint32_t BYTES = 128u * W * 2u;          // bf16
+  static constexpr int CPR = W / 8;                         // 16-byte chunks per row
+};
 constexpr int CONSUMER_WARPS = 16;
 constexpr int THREADS = 32 * (CONSUMER_WARPS + 1);  // + producer warp
 constexpr int W_GROUPS = 4;                          // weight quantiser: tile groups
@@ -167,13 +177,13 @@ template <int kMode>
 struct Layout {
   static constexpr int STAGES = Ring<kMode>::STAGES;
   // per group and parity: one float per warp (WEIGHT) or per warp and column (COL)
-  static constexpr int RED_PER_WARP = kMode == COL ? 128 : 1;
-  static constexpr uint32_t OFF_BAR = STAGES * IN_BYTES;
+  static constexpr int RED_PER_WARP = kMode == COL ? TileShape<kMode>::W : 1;
+  static constexpr uint32_t OFF_BAR = STAGES * TileShape<kMode>::BYTES;
   static constexpr uint32_t OFF_RED = OFF_BAR + 2 * STAGES * 8;
-  // COL: per group, the tile's 128 column scales and their reciprocals,
+  // COL: per group, the tile's column scales and their reciprocals,
   // computed once per column by the thread that owns it
   static constexpr uint32_t OFF_CSC = OFF_RED + W_GROUPS * 2 * W_GROUP_WARPS * RED_PER_WARP * 4;
-  static constexpr uint32_t CSC_BYTES = kMode == COL ? W_GROUPS * 2 * 128 * 4 : 0;
+  static constexpr uint32_t CSC_BYTES = kMode == COL ? W_GROUPS * 2 * TileShape<kMode>::W * 4 : 0;
   static constexpr uint32_t OFF_FLAG = OFF_CSC + CSC_BYTES;
   static constexpr uint32_t SMEM_BYTES = OFF_FLAG + 16 + 1024;  // + slack for 1 KB alignment
 };
@@ -189,7 +199,8 @@ struct Args {
 };
 
 // Tile -> (x, y) element coordinates of its top-left corner.
-//   ACT / COL: tiles are (128-row slab, 128-column block), column block fastest;
+//   ACT / COL: tiles are (128-row slab, column block of TileShape::W),
+//              column block fastest;
 //   WEIGHT:    tiles are (group, K block, N block), N block fastest.
 template <int kMode>
 __device__ __forceinline__ void tile_xy(const Args& a, int64_t t, int32_t& x, int32_t& y) {
@@ -199,8 +210,9 @@ __device__ __forceinline__ void tile_xy(const Args& a, int64_t t, int32_t& x, in
     x = static_cast<int32_t>(nb * 128);
     y = static_cast<int32_t>(g * a.K + kb * 128);
   } else {
-    const int64_t KB = a.K / 128;
-    x = static_cast<int32_t>((t % KB) * 128);
+    constexpr int W = TileShape<kMode>::W;
+    const int64_t KB = a.K / W;
+    x = static_cast<int32_t>((t % KB) * W);
     y = static_cast<int32_t>((t / KB) * 128);
   }
 }
@@ -254,8 +266,8 @@ __global__ void __launch_bounds__(THREADS, Ring<kMode>::CTAS_PER_SM)
         if (!mbar_wait(&empty[st], (static_cast<uint32_t>(i / STAGES) & 1u) ^ 1u, ab)) break;
         int32_t x, y;
         tile_xy<kMode>(a, blockIdx.x + i * gridDim.x, x, y);
-        mbar_arrive_expect_tx(&full[st], IN_BYTES);
-        tma_load_2d(smem + st * IN_BYTES, &tm_in, &full[st], x, y);
+        mbar_arrive_expect_tx(&full[st], TileShape<kMode>::BYTES);
+        tma_load_2d(smem + st * TileShape<kMode>::BYTES, &tm_in, &full[st], x, y);
       }
       if (i < n) {
         // Aborted: let the loads in flight land before the CTA can exit.
@@ -279,9 +291,12 @@ __global__ void __launch_bounds__(THREADS, Ring<kMode>::CTAS_PER_SM)
     for (int64_t i = grp; i < n; i += W_GROUPS, par ^= 1) {
       const int st = static_cast<int>(i % STAGES);
       const bool ok = mbar_wait(&full[st], static_cast<uint32_t>(i / STAGES) & 1u, ab);
-      const uint4* in = reinterpret_cast<const uint4*>(smem + st * IN_BYTES);
+      const uint4* in = reinterpret_cast<const uint4*>(smem + st * TileShape<kMode>::BYTES);
       float* r = red + (grp * 2 + par) * W_GROUP_WARPS * L::RED_PER_WARP;
-      const int c16 = tg & 15;  // this thread's 8-column chunk of the tile
+      // this thread's 16-byte (8-column) chunk of the tile's rows: chunk
+      // tg % CPR of rows tg / CPR + (128 / CPR) j, i.e. in[tg + 128 j]
+      constexpr int CPR = TileShape<kMode>::CPR, RSTEP = 128 / CPR;
+      const int c16 = tg % CPR;
       if (kMode == WEIGHT) {
         float m = 0.f;
 #pragma unroll 8
@@ -290,26 +305,28 @@ __global__ void __launch_bounds__(THREADS, Ring<kMode>::CTAS_PER_SM)
         for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (lane == 0) r[gw] = m;
       } else {
-        // per-column maxima over this thread's 16 rows on packed bf16 (exact:
-        // the maximum is one of the values), then over the two row groups of
-        // the warp (lanes l and l ^ 16 share the chunk)
+        // per-column maxima over this thread's CPR rows on packed bf16 (exact:
+        // the maximum is one of the values), then over the warp's lanes that
+        // share the chunk (l, l ^ CPR, l ^ 2 CPR, ...)
         __nv_bfloat162 cm2[4];
 #pragma unroll
         for (int h = 0; h < 4; ++h) cm2[h] = __floats2bfloat162_rn(0.f, 0.f);
 #pragma unroll 4
-        for (int j = 0; j < 16; ++j) {
+        for (int j = 0; j < CPR; ++j) {
           const uint4 u = in[tg + 128 * j];
           const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
           for (int h = 0; h < 4; ++h) cm2[h] = __hmax2(cm2[h], __habs2(hv[h]));
         }
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const uint32_t o = __shfl_xor_sync(0xffffffffu, *reinterpret_cast<const uint32_t*>(&cm2[h]), 16);
-          cm2[h] = __hmax2(cm2[h], *reinterpret_cast<const __nv_bfloat162*>(&o));
-        }
-        if (lane < 16) {
-          float4* rc = reinterpret_cast<float4*>(r + gw * 128 + c16 * 8);
+        for (int o = CPR; o < 32; o <<= 1)
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const uint32_t v = __shfl_xor_sync(0xffffffffu, *reinterpret_cast<const uint32_t*>(&cm2[h]), o);
+            cm2[h] = __hmax2(cm2[h], *reinterpret_cast<const __nv_bfloat162*>(&v));
+          }
+        if (lane < CPR) {
+          float4* rc = reinterpret_cast<float4*>(r + gw * TileShape<kMode>::W + c16 * 8);
           rc[0] = make_float4(__low2float(cm2[0]), __high2float(cm2[0]), __low2float(cm2[1]),
                               __high2float(cm2[1]));
           rc[1] = make_float4(__low2float(cm2[2]), __high2float(cm2[2]), __low2float(cm2[3]),
@@ -339,23 +356,24 @@ __global__ void __launch_bounds__(THREADS, Ring<kMode>::CTAS_PER_SM)
         // thread tg owns column tg of the tile: its maximum over the group's
         // warps, its scale (also stored to s[row block, column]) and the
         // scale's reciprocal, shared through shared memory
-        float* csc = reinterpret_cast<float*>(smem + L::OFF_CSC) + grp * 256;
-        {
+        constexpr int W = TileShape<kMode>::W;
+        float* csc = reinterpret_cast<float*>(smem + L::OFF_CSC) + grp * 2 * W;
+        if (tg < W) {
           float m = r[tg];
 #pragma unroll
-          for (int w = 1; w < W_GROUP_WARPS; ++w) m = fmaxf(m, r[w * 128 + tg]);
+          for (int w = 1; w < W_GROUP_WARPS; ++w) m = fmaxf(m, r[w * W + tg]);
           const float sc1 = scale_of(m);
           csc[tg] = sc1;
-          csc[128 + tg] = 1.0f / sc1;
+          csc[W + tg] = 1.0f / sc1;
           a.s[static_cast<int64_t>(y / 128) * a.K + x + tg] = sc1;
         }
         asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(W_GROUP_WARPS * 32) : "memory");
         BlockDiv div[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) div[e] = BlockDiv(csc[c16 * 8 + e], csc[128 + c16 * 8 + e]);
+        for (int e = 0; e < 8; ++e) div[e] = BlockDiv(csc[c16 * 8 + e], csc[W + c16 * 8 + e]);
 #pragma unroll 4
-        for (int j = 0; j < 16; ++j) {
-          const int row = (tg >> 4) + 8 * j;
+        for (int j = 0; j < CPR; ++j) {
+          const int row = tg / CPR + RSTEP * j;
           *reinterpret_cast<uint2*>(qbase + static_cast<int64_t>(row) * ld) =
               quant8_cols(in[tg + 128 * j], div);
         }
@@ -373,7 +391,7 @@ __global__ void __launch_bounds__(THREADS, Ring<kMode>::CTAS_PER_SM)
     for (int64_t i = 0; i < n; ++i) {
       const int st = static_cast<int>(i % STAGES);
       if (!mbar_wait(&full[st], static_cast<uint32_t>(i / STAGES) & 1u, ab)) break;
-      const uint4* in = reinterpret_cast<const uint4*>(smem + st * IN_BYTES);
+      const uint4* in = reinterpret_cast<const uint4*>(smem + st * TileShape<kMode>::BYTES);
       int32_t x, y;
       tile_xy<kMode>(a, blockIdx.x + i * gridDim.x, x, y);
       uint4 u[2][2];
@@ -414,8 +432,8 @@ int launch_quant(const void* in, void* q, float* s, int* err, int64_t rows, int6
   using namespace gl::quant;
   const int64_t inner = kMode == WEIGHT ? N : K;
   CUtensorMap tm_in;
-  if (!gl_make_tmap_2d(&tm_in, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, in, inner, rows, inner, 128, 128,
-                       CU_TENSOR_MAP_SWIZZLE_NONE, why))
+  if (!gl_make_tmap_2d(&tm_in, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, in, inner, rows, inner,
+                       gl::quant::TileShape<kMode>::W, 128, CU_TENSOR_MAP_SWIZZLE_NONE, why))
     return -1;
   Args a;
   a.q = static_cast<uint8_t*>(q);
@@ -424,7 +442,8 @@ int launch_quant(const void* in, void* q, float* s, int* err, int64_t rows, int6
   a.rows = rows;
   a.K = K;
   a.N = N;
-  a.tiles = kMode == WEIGHT ? (rows / 128) * (N / 128) : ((rows + 127) / 128) * (K / 128);
+  a.tiles = kMode == WEIGHT ? (rows / 128) * (N / 128)
+                            : ((rows + 127) / 128) * (K / TileShape<kMode>::W);
   const void* fn = reinterpret_cast<const void*>(quant_kernel<kMode>);
   constexpr uint32_t smem_bytes = Layout<kMode>::SMEM_BYTES;
   if (!gl_set_smem_attr(fn, 0, static_cast<int>(smem_bytes), why)) return -2;
