@@ -876,18 +876,29 @@ def run_sharded(args, rank, world, steps, warmup):
 
     c2 = timed(gla_local, steps, warmup, world)
     g2 = timed(gla_gathered, steps, warmup, world)
-    err = None
+    # the same gather inside the forward: every chunk's O is TMA-stored into
+    # block `rank` of every rank's IPC-shared buffer (shard.gla_fwd_gathered)
+    peers = shard.PeerBuffers(world, width)
+
+    def gla_scattered():
+        shard.gla_fwd_gathered(q, k, v, g, h0, 128 ** -0.5, peers, width, ht=ht_l)
+
+    k2 = timed(gla_scattered, steps, warmup, world)
+    err = err_k = None
     if rank == 0:
         full = ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], None, 128 ** -0.5, 64, g=inp["g"],
                                  h0=inp["h0"], output_final_state=True).o
-        worst = 0.0
+        worst = worst_k = 0.0
         for r, hrange in enumerate(shard.gla_head_partition(gcfg.H, world)):
-            got = stage[r, : gcfg.B * gcfg.T * len(hrange) * gcfg.V].view(
-                gcfg.B, gcfg.T, len(hrange), gcfg.V).float()
+            n_r = gcfg.B * gcfg.T * len(hrange) * gcfg.V
             want = full[:, :, hrange.start:hrange.stop].float()
+            got = stage[r, :n_r].view(gcfg.B, gcfg.T, len(hrange), gcfg.V).float()
             worst = max(worst, float((got - want).norm() / want.norm()))
-        err = worst
+            got = peers.local[r, :n_r].view(gcfg.B, gcfg.T, len(hrange), gcfg.V).float()
+            worst_k = max(worst_k, float((got - want).norm() / want.norm()))
+        err, err_k = worst, worst_k
         del full
+    peers.close()
     if ops.device_status() != 0:
         raise SystemExit("device error word set after the sharded GLA")
     res["gla"] = {"workload": "gla_b1_t32768", "split": "heads", "heads_per_rank": heads,
@@ -895,7 +906,13 @@ def run_sharded(args, rank, world, steps, warmup):
                   "tokens_per_s_compute": gcfg.B * gcfg.T / (c2 * 1e-3),
                   "tokens_per_s_with_gather": gcfg.B * gcfg.T / (g2 * 1e-3),
                   "gathered_layout": "[world, B, T, H/world, V] head blocks",
-                  "rel_err_vs_single_gpu": err, "scaling": "strong"}
+                  "rel_err_vs_single_gpu": err,
+                  "with_gather_in_kernel_ms": k2,
+                  "tokens_per_s_with_gather_in_kernel": gcfg.B * gcfg.T / (k2 * 1e-3),
+                  "in_kernel_rel_err_vs_single_gpu": err_k,
+                  "gather": "with_gather: NCCL all-gather after the forward; in_kernel: the forward "
+                            "TMA-stores every chunk's O into every rank's IPC-shared buffer",
+                  "scaling": "strong"}
     del inp, q, k, v, g, h0, o_l, ht_l, stage
     torch.cuda.empty_cache()
     return res

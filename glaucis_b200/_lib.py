@@ -38,6 +38,8 @@ SIGNATURES = {
                                      _I64, _P, _P, _P, _P, ctypes.c_size_t, _P, _P]),
     "gl_chunk_gla_fwd_ex": (_I, [_P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64, _I64,
                                  _P, _P, _P, _P, ctypes.c_size_t, _I, _P, _P]),
+    "gl_chunk_gla_fwd_scatter": (_I, [_P, _P, _P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64,
+                                      _I64, _P, _I, _P, _P, ctypes.c_size_t, _I, _P, _P]),
     "gl_chunk_gla_fwd_intermediates": (_I, [_P, _P, _P, _P, _F, _I64, _I64, _I64, _I64, _I64, _P,
                                             _P, _P, _P]),
     "gl_chunk_gla_bwd_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I64, _I64]),

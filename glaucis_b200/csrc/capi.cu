@@ -34,6 +34,11 @@ int gl_launch_gmm_fp8_multi(const void* a_q, const float* a_s, const void* b_q, 
                             const int32_t* group_sizes, int64_t G, int64_t M, int64_t K, int64_t N,
                             void* const* outs, int n_outs, int64_t row_off, int out_f32, int* err,
                             cudaStream_t st, int num_sms, const char** why);
+int gl_launch_chunk_gla_scatter(const void* q, const void* k, const void* v, const float* g,
+                                const float* g_gamma, const float* h0, float scale, int64_t B,
+                                int64_t T, int64_t H, void* const* outs, int n_outs, float* ht,
+                                void* ws, size_t ws_bytes, int p_split, int* err, cudaStream_t st,
+                                int num_sms, const char** why);
 int gl_launch_chunk_gla_dh(const void* q, const void* dout, const float* g, const float* g_gamma,
                            const float* dht, float scale, int64_t B, int64_t T, int64_t H,
                            void* e_out, float* dh0, void* ws, size_t ws_bytes, int* err,
@@ -377,6 +382,36 @@ static int chunk_gla_check(const char* fn, const void* q, const void* k, const v
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || (g && !aligned16(g)) ||
       (h0 && !aligned16(h0)) || (ht && !aligned16(ht)))
     return fail(GL_EINVAL, f + ": tensors must be 16-byte aligned");
+  return GL_OK;
+}
+
+int gl_chunk_gla_fwd_scatter(const void* q, const void* k, const void* v, const float* g,
+                             const float* g_gamma, const float* h0, float scale, int64_t B,
+                             int64_t T, int64_t H, int64_t K, int64_t V, int64_t chunk_size,
+                             void* const* outs, int n_outs, float* ht, void* workspace,
+                             size_t workspace_bytes, int flags, int* err_word, void* stream) {
+  const char* f = "gl_chunk_gla_fwd_scatter";
+  if (!outs) return fail(GL_EINVAL, std::string(f) + ": null pointer");
+  if (n_outs < 1 || n_outs > GL_MAX_SCATTER_OUTS)
+    return fail(GL_EINVAL, std::string(f) + ": need 1 <= n_outs <= GL_MAX_SCATTER_OUTS");
+  for (int i = 0; i < n_outs; ++i)
+    if (!outs[i] || !aligned16(outs[i]))
+      return fail(GL_EINVAL, std::string(f) + ": every output must be a 16-byte aligned pointer");
+  if (int rc = chunk_gla_check(f, q, k, v, g, g_gamma, h0, B, T, H, K, V, chunk_size, outs[0], ht))
+    return rc;
+  if (flags & ~GL_GLA_BF16_INTRA) return fail(GL_EINVAL, std::string(f) + ": unknown flags");
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(GL_EINVAL, std::string(f) + ": workspace must be 256-byte aligned");
+  DeviceState* d = nullptr;
+  if (int rc = device_state(&d)) return rc;
+  const char* why = "";
+  const int rc = gl_launch_chunk_gla_scatter(q, k, v, g, g_gamma, h0, scale, B, T, H, outs, n_outs,
+                                             ht, workspace, workspace ? workspace_bytes : 0,
+                                             (flags & GL_GLA_BF16_INTRA) ? 0 : 1,
+                                             err_word ? err_word : d->err,
+                                             static_cast<cudaStream_t>(stream), d->num_sms, &why);
+  if (rc == -1) return fail(GL_EINVAL, std::string(f) + ": " + why);
+  if (rc != 0) return fail(GL_ELAUNCH, std::string(f) + ": " + why);
   return GL_OK;
 }
 

@@ -105,10 +105,20 @@ struct Cfg {
 // D_0 = dh0.  DH_STATE: its state-only pre-pass.
 enum { MODE_FWD = 0, MODE_FWD_STATE = 1, MODE_DH_STATE = 2, MODE_DH = 3 };
 
+// Output tensor maps of the forward at VS = 128: O is stored into each of
+// Params::n_outs buffers of the layout of o (the own output and, for a
+// head-sharded forward, the same block of every peer's gather buffer).
+constexpr int MAX_OUTS = 8;
+static_assert(MAX_OUTS == GL_MAX_SCATTER_OUTS, "output count of the C ABI");
+struct OutMaps {
+  CUtensorMap m[MAX_OUTS];
+};
+
 struct Params {
   const float* g_gamma;  // [H] or null
   const float* h0;       // [B,H,K,V] or null (DH: the final-state gradient dht, or null)
-  __nv_bfloat16* o;      // [B,T,H,V]
+  __nv_bfloat16* o;      // [B,T,H,V] (the first output)
+  int n_outs;            // outputs of O (1..MAX_OUTS; > 1 only at VS = 128)
   float* ht;             // [B,H,K,V] or null (DH: dh0)
   int* err;
   float scale;
@@ -190,14 +200,17 @@ __device__ __forceinline__ uint32_t kmaj_off(uint32_t row, uint32_t col, uint32_
          (col & 7u) * 2u;
 }
 
-template <int VS, int kMode, bool kSplit>
+// kScatter (forward at VS = 128 only): O goes to Params::n_outs outputs;
+// a separate instance, since the extra stores cost the gating warps
+// registers.
+template <int VS, int kMode, bool kSplit, bool kScatter = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     chunk_gla_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v,
                          const __grid_constant__ CUtensorMap tm_g,
                          const __grid_constant__ CUtensorMap tm_h,
-                         const __grid_constant__ CUtensorMap tm_o, const Params p) {
+                         const __grid_constant__ OutMaps tm_o, const Params p) {
   using CF = Cfg<VS, kSplit, kMode == MODE_FWD>;
   // kStateOnly: S_n = (k slot)^T (v slot) only (no q, A, O).  kRev: chunks
   // in reverse order, the k slot scaled like q (Qs) instead of k (Kg).
@@ -505,7 +518,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_3d(&tm_o, slot, v0 + ohalf * OC, h, tok0 + m * C + oquad * 16);
+          const int32_t ox = v0 + ohalf * OC, oz = tok0 + m * C + oquad * 16;
+          if constexpr (kScatter) {
+#pragma unroll
+            for (int oo = 0; oo < MAX_OUTS; ++oo)  // constant map offsets, predicated
+              if (oo < p.n_outs) tma_store_3d(&tm_o.m[oo], slot, ox, h, oz);
+          } else {
+            tma_store_3d(&tm_o.m[0], slot, ox, h, oz);
+          }
           bulk_commit();
         }
       } else if constexpr (OC == 64) {
@@ -1015,17 +1035,20 @@ static size_t gla_ws_bytes(int64_t B, int64_t H, int nseg) {
   return ((hb + 255) / 256) * 256 + rec * 128 * 4;
 }
 
-template <int VS, int kMode, bool kSplit = false>
+template <int VS, int kMode, bool kSplit = false, bool kScatter = false>
 static int launch_pass(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                       const CUtensorMap& tg, const CUtensorMap& th, const CUtensorMap& to,
+                       const CUtensorMap& tg, const CUtensorMap& th, const gl::gla::OutMaps& to,
                        const gl::gla::Params& p, int grid, cudaStream_t st, const char** why) {
-  if constexpr (kMode == gl::gla::MODE_FWD && !kSplit) {
+  if constexpr (kMode == gl::gla::MODE_FWD && !kSplit && !kScatter) {
     if (p.p_split) return launch_pass<VS, kMode, true>(tq, tk, tv, tg, th, to, p, grid, st, why);
   }
+  if constexpr (kMode == gl::gla::MODE_FWD && VS == 128 && !kScatter) {
+    if (p.n_outs > 1) return launch_pass<VS, kMode, kSplit, true>(tq, tk, tv, tg, th, to, p, grid, st, why);
+  }
   using CF = gl::gla::Cfg<VS, kSplit, kMode == gl::gla::MODE_FWD>;
-  const void* fn = reinterpret_cast<const void*>(gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit>);
+  const void* fn = reinterpret_cast<const void*>(gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit, kScatter>);
   if (!gl_set_smem_attr(fn, 0, static_cast<int>(CF::SMEM_BYTES), why)) return -2;
-  gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit><<<grid, gl::gla::NUM_THREADS, CF::SMEM_BYTES, st>>>(
+  gl::gla::chunk_gla_fwd_kernel<VS, kMode, kSplit, kScatter><<<grid, gl::gla::NUM_THREADS, CF::SMEM_BYTES, st>>>(
       tq, tk, tv, tg, th, to, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -1040,7 +1063,8 @@ static int launch_pass(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
 // output E_n), with the state-only pre-pass and the fold of a sequence split.
 template <int VS>
 static int launch_vs(const void* q, const void* kslot, const void* vslot, const float* g,
-                     void* sout, gl::gla::Params p, bool rev, cudaStream_t st, const char** why) {
+                     void* sout, void* const* outs, gl::gla::Params p, bool rev, cudaStream_t st,
+                     const char** why) {
   const int64_t BT = static_cast<int64_t>(p.B) * p.T;
   CUtensorMap tq, tk, tv, tg, th;
   if (!gl_make_tmap_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kslot, 128, p.H, BT, 128,
@@ -1073,16 +1097,21 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
   } else {
     th = tk;  // unused
   }
-  CUtensorMap to;
+  gl::gla::OutMaps to;
   if (!rev && VS == 128 && p.o != nullptr) {
-    // o [B*T, H, 128] bf16, boxes of 64 columns x 1 head x 16 rows: one
-    // gating warp's share of a chunk's O (used by the kSplit instance)
-    if (!gl_make_tmap_3d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.o, 128, p.H, BT, 128,
-                         static_cast<int64_t>(p.H) * 128, 64, 1, 16, CU_TENSOR_MAP_SWIZZLE_128B, why))
-      return -1;
-  } else {
-    to = tk;  // unused
+    // each output [B*T, H, 128] bf16, boxes of 64 columns x 1 head x 16
+    // rows: one gating warp's share of a chunk's O
+    for (int i = 0; i < p.n_outs; ++i)
+      if (!gl_make_tmap_3d(&to.m[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, outs[i], 128, p.H, BT, 128,
+                           static_cast<int64_t>(p.H) * 128, 64, 1, 16, CU_TENSOR_MAP_SWIZZLE_128B,
+                           why))
+        return -1;
+  } else if (p.n_outs > 1) {
+    *why = "several outputs need the full-width (VS = 128) forward: pass a workspace";
+    return -1;
   }
+  for (int i = (!rev && VS == 128 && p.o != nullptr) ? p.n_outs : 0; i < gl::gla::MAX_OUTS; ++i)
+    to.m[i] = tk;  // unused
   const int items = p.B * p.H * p.nsplit;
   if (p.nseg > 1 && !rev && p.c_first > 0) {
     // Phase 1: segment 0's full pass (from h0; its final state becomes
@@ -1164,14 +1193,15 @@ size_t gl_chunk_gla_ws_bytes(int64_t B, int64_t T, int64_t H, int num_sms) {
 // Shared set-up of the forward and the reverse scan: scale, segments, V split.
 static int gla_dispatch(const void* q, const void* kslot, const void* vslot, const float* g,
                         const float* g_gamma, const float* init, float scale, int64_t B,
-                        int64_t T, int64_t H, void* o, float* fin, void* sout, void* ws,
-                        size_t ws_bytes, int* err, bool rev, int p_split, cudaStream_t st,
+                        int64_t T, int64_t H, void* const* outs, int n_outs, float* fin, void* sout,
+                        void* ws, size_t ws_bytes, int* err, bool rev, int p_split, cudaStream_t st,
                         int num_sms, const char** why) {
   gl::gla::Params p;
   p.p_split = rev ? 0 : p_split;
   p.g_gamma = g_gamma;
   p.h0 = init;
-  p.o = static_cast<__nv_bfloat16*>(o);
+  p.o = n_outs > 0 ? static_cast<__nv_bfloat16*>(outs[0]) : nullptr;
+  p.n_outs = n_outs > 0 ? n_outs : 1;
   p.ht = fin;
   p.err = err;
   p.scale = scale;
@@ -1204,10 +1234,10 @@ static int gla_dispatch(const void* q, const void* kslot, const void* vslot, con
   if (const char* e = std::getenv("GLAUCIS_GLA_VS")) split_v = std::atoi(e) == 64;
   if (split_v) {
     p.nsplit = 2;
-    return launch_vs<64>(q, kslot, vslot, g, sout, p, rev, st, why);
+    return launch_vs<64>(q, kslot, vslot, g, sout, outs, p, rev, st, why);
   }
   p.nsplit = 1;
-  return launch_vs<128>(q, kslot, vslot, g, sout, p, rev, st, why);
+  return launch_vs<128>(q, kslot, vslot, g, sout, outs, p, rev, st, why);
 }
 
 int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float* g,
@@ -1217,8 +1247,20 @@ int gl_launch_chunk_gla(const void* q, const void* k, const void* v, const float
                         const char** why) {
   (void)K;
   (void)V;
-  return gla_dispatch(q, k, v, g, g_gamma, h0, scale, B, T, H, o, ht, h_out, ws, ws_bytes, err,
-                      false, p_split, st, num_sms, why);
+  void* outs[1] = {o};
+  return gla_dispatch(q, k, v, g, g_gamma, h0, scale, B, T, H, outs, 1, ht, h_out, ws, ws_bytes,
+                      err, false, p_split, st, num_sms, why);
+}
+
+// The forward with O stored into n_outs buffers of o's layout (see
+// gl_chunk_gla_fwd_scatter).
+int gl_launch_chunk_gla_scatter(const void* q, const void* k, const void* v, const float* g,
+                                const float* g_gamma, const float* h0, float scale, int64_t B,
+                                int64_t T, int64_t H, void* const* outs, int n_outs, float* ht,
+                                void* ws, size_t ws_bytes, int p_split, int* err, cudaStream_t st,
+                                int num_sms, const char** why) {
+  return gla_dispatch(q, k, v, g, g_gamma, h0, scale, B, T, H, outs, n_outs, ht, nullptr, ws,
+                      ws_bytes, err, false, p_split, st, num_sms, why);
 }
 
 // Reverse state-gradient scan of the backward: E_n (bf16 [B,NT,H,K,V]) for
@@ -1227,6 +1269,6 @@ int gl_launch_chunk_gla_dh(const void* q, const void* dout, const float* g, cons
                            const float* dht, float scale, int64_t B, int64_t T, int64_t H,
                            void* e_out, float* dh0, void* ws, size_t ws_bytes, int* err,
                            cudaStream_t st, int num_sms, const char** why) {
-  return gla_dispatch(nullptr, q, dout, g, g_gamma, dht, scale, B, T, H, nullptr, dh0, e_out, ws,
+  return gla_dispatch(nullptr, q, dout, g, g_gamma, dht, scale, B, T, H, nullptr, 0, dh0, e_out, ws,
                       ws_bytes, err, true, 0, st, num_sms, why);
 }

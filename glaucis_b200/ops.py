@@ -507,6 +507,37 @@ def chunk_gla_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return GLAForward(o, ht if output_final_state else None, h, g_cumsum, A)
 
 
+def chunk_gla_fwd_scatter(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                          g_gamma: Optional[torch.Tensor], scale: float, chunk_size: int = 64, *,
+                          outs, g: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
+                          ht: Optional[torch.Tensor] = None, exact_intra: bool = True) -> None:
+    """chunk_gla_fwd whose output o is stored into every buffer of `outs`
+    (tensors on this device, or integer device addresses of peer-mapped
+    buffers such as shard.PeerBuffers.ptrs plus an offset), each holding o's
+    layout [B, T, H, V] bf16.  Used to assemble a head-sharded forward on
+    every rank inside the kernel; the caller synchronises the ranks after it.
+    ht (fp32 [B, H, K, V]) receives the final state when given."""
+    B, T, H, K, V = _gla_check(q, k, v, g_gamma, g, h0)
+    ptrs = [o.data_ptr() if isinstance(o, torch.Tensor) else int(o) for o in outs]
+    for o in outs:
+        if isinstance(o, torch.Tensor) and (o.dtype != torch.bfloat16 or tuple(o.shape) != (B, T, H, V)
+                                            or not o.is_contiguous()):
+            raise ValueError("each output must be a contiguous bf16 [B, T, H, V] tensor")
+    if ht is not None and (ht.dtype != torch.float32 or tuple(ht.shape) != (B, H, K, V)):
+        raise ValueError("ht must be fp32 [B, H, K, V]")
+    lib = _lib.load()
+    ws_bytes = lib.gl_chunk_gla_fwd_workspace_bytes(B, T, H, K, V, chunk_size)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+    import ctypes
+    arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    flags = 0 if exact_intra else _lib.GL_GLA_BF16_INTRA
+    _lib.check(lib.gl_chunk_gla_fwd_scatter(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(g),
+                                            _ptr(g_gamma), _ptr(h0), float(scale), B, T, H, K, V,
+                                            chunk_size, ctypes.cast(arr, ctypes.c_void_p), len(ptrs),
+                                            _ptr(ht), _ptr(ws), ws_bytes, flags, None, _stream()),
+               "gl_chunk_gla_fwd_scatter")
+
+
 def chunk_gla_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, do: torch.Tensor,
                   h: torch.Tensor, g_gamma: Optional[torch.Tensor], scale: float,
                   chunk_size: int = 64, *, g: Optional[torch.Tensor] = None,

@@ -224,3 +224,34 @@ def gmm_fp8_fwd_gathered(a_q: torch.Tensor, a_s: torch.Tensor, b_q: torch.Tensor
                                 me.r0)
     dist.all_reduce(flag)
     return peers.local
+
+
+def gla_fwd_gathered(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
+                     h0: torch.Tensor, scale: float, peers: PeerBuffers, width: int,
+                     ht: torch.Tensor = None, exact_intra: bool = True) -> torch.Tensor:
+    """This rank's heads of a head-sharded chunked-GLA forward, with the
+    output assembled on every rank by the forward itself: q, k, v, g
+    ([B, T, H_r, *]) and h0 ([B, H_r, K, V]) hold this rank's head range,
+    and every chunk's O is TMA-stored from the kernel into block `rank` of
+    every rank's `peers` buffer (PeerBuffers(world, width): block r = rank
+    r's [B, T, H_r, V] output, width >= B*T*max(H_r)*V), over NVLink
+    (gl_chunk_gla_fwd_scatter).  The same two stream-ordered all-reduces of
+    one int as gmm_fp8_fwd_gathered order the stores after every rank's
+    earlier work on its buffer and the readers after every rank's kernel.
+    Returns `peers.local` ([world, width]): the shared buffer, valid until
+    the next call.  Collective: every rank calls it, in the same order.
+    Each head's computation is the single-GPU one, so the blocks equal a
+    one-GPU forward of the same heads bit for bit."""
+    import torch.distributed as dist
+    from . import ops
+    rank, world = dist.get_rank(), dist.get_world_size()
+    B, T, Hr, V = v.shape
+    if B * T * Hr * V > width or tuple(peers.local.shape) != (world, width):
+        raise ValueError("peers must be PeerBuffers(world, width) with width >= B*T*H_r*V")
+    flag = torch.zeros(1, dtype=torch.int32, device=peers.local.device)
+    dist.all_reduce(flag)
+    outs = [p + rank * width * 2 for p in ring_order(peers.ptrs, rank)]
+    ops.chunk_gla_fwd_scatter(q, k, v, None, scale, 64, outs=outs, g=g, h0=h0, ht=ht,
+                              exact_intra=exact_intra)
+    dist.all_reduce(flag)
+    return peers.local

@@ -182,6 +182,25 @@ int gl_chunk_gla_fwd_ex(const void* q, const void* k, const void* v, const float
                         int* err_word, void* stream);
 
 /*
+ * gl_chunk_gla_fwd_ex (h_states NULL) with o stored into several buffers:
+ * outs[0 .. n_outs-1], each of o's layout [B, T, H, V] bf16 and 16-byte
+ * aligned, receive the same output.  The buffers may be other GPUs' memory
+ * mapped into this process (CUDA IPC peer mappings over NVLink, e.g.
+ * gl_ipc_open): the forward stores each chunk's O from shared memory with TMA
+ * stores into every buffer, so a forward sharded by head across ranks
+ * assembles its output on every rank inside the kernel instead of an
+ * all-gather after it.  Needs the full-width kernel, i.e. a workspace when
+ * B*H*2 <= the SM count (GL_EINVAL otherwise).  The caller orders the
+ * readers after the kernels of all ranks.  No counterpart in the reference
+ * (chunk_gla.py:258-273 writes one o; a head-sharded caller would all-gather).
+ */
+int gl_chunk_gla_fwd_scatter(const void* q, const void* k, const void* v, const float* g,
+                             const float* g_gamma, const float* h0, float scale, int64_t B,
+                             int64_t T, int64_t H, int64_t K, int64_t V, int64_t chunk_size,
+                             void* const* outs, int n_outs, float* ht, void* workspace,
+                             size_t workspace_bytes, int flags, int* err_word, void* stream);
+
+/*
  * The intermediates of the chunked GLA forward that gl_chunk_gla_fwd keeps on
  * chip, for callers that read them:
  *   g_cumsum fp32 [B, T, H, K]  chunk-local cumsum of g (or g_gamma[h]*(1..64))

@@ -120,3 +120,24 @@ def test_gla_options_and_intermediates_reject_bad_arguments_without_device():
     assert rc == _lib.GL_EINVAL and "exactly one" in _err()
     rc = lib.gl_chunk_gla_fwd_intermediates(p, p, f, None, 0.1, 1, 64, 1, 64, 64, f, None, None, None)
     assert rc == _lib.GL_EINVAL and "128" in _err()
+
+
+def test_gla_scatter_rejects_bad_arguments_without_device():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    f = ctypes.c_void_p(32)
+    one = (ctypes.c_void_p * 1)(16)
+    nine = (ctypes.c_void_p * 9)(*([16] * 9))
+    odd = (ctypes.c_void_p * 2)(16, 24)  # the second output is not 16-byte aligned
+
+    def call(outs, n, flags=0, g=f, gg=None):
+        return lib.gl_chunk_gla_fwd_scatter(p, p, p, g, gg, None, 0.1, 1, 64, 1, 128, 128, 64,
+                                            ctypes.cast(outs, ctypes.c_void_p) if outs is not None
+                                            else None, n, None, None, 0, flags, None, None)
+
+    assert call(None, 1) == _lib.GL_EINVAL and "null" in _err()
+    assert call(one, 0) == _lib.GL_EINVAL and "n_outs" in _err()
+    assert call(nine, 9) == _lib.GL_EINVAL and "n_outs" in _err()
+    assert call(odd, 2) == _lib.GL_EINVAL and "aligned" in _err()
+    assert call(one, 1, flags=4) == _lib.GL_EINVAL and "unknown flags" in _err()
+    assert call(one, 1, gg=f) == _lib.GL_EINVAL and "exactly one" in _err()

@@ -69,3 +69,46 @@ def test_gathered_matmul_two_calls_with_different_inputs(cuda, one_rank_group):
             assert torch.equal(got, want)
     finally:
         peers.close()
+
+
+@pytest.mark.parametrize("B,T,H", [(1, 2048, 4), (2, 512, 80)])
+def test_gathered_gla_equals_one_gpu(cuda, one_rank_group, B, T, H):
+    # The head-sharded GLA forward whose kernel stores O into block `rank` of
+    # every rank's buffer (one rank: its own block).  (1, 2048, 4) runs the
+    # sequence split (O from both full passes), (2, 512, 80) one CTA per
+    # (batch, head).  Both equal the plain forward bit for bit.
+    cfg = configs.GLAConfig("t", B=B, T=T, H=H, h0_std=0.1)
+    inp = configs.make_gla_inputs(cfg, device=cuda, seed=33)
+    want = ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], None, 128 ** -0.5, 64, g=inp["g"],
+                             h0=inp["h0"], output_final_state=True)
+    width = B * T * H * 128 + 256  # a padded block, like unequal head counts need
+    peers = shard.PeerBuffers(1, width)
+    try:
+        peers.local.fill_(7.0)
+        ht = torch.empty_like(inp["h0"])
+        got = shard.gla_fwd_gathered(inp["q"], inp["k"], inp["v"], inp["g"], inp["h0"],
+                                     128 ** -0.5, peers, width, ht=ht)
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        blk = got[0, : B * T * H * 128].view(B, T, H, 128)
+        assert torch.equal(blk, want.o)
+        assert torch.equal(ht, want.ht)
+        assert torch.all(got[0, B * T * H * 128:] == 7.0)  # the padding is not written
+    finally:
+        peers.close()
+
+
+def test_gla_scatter_writes_every_output(cuda):
+    # the raw op with three local outputs, both precisions
+    cfg = configs.GLAConfig("t", B=2, T=256, H=80)
+    inp = configs.make_gla_inputs(cfg, device=cuda, seed=34)
+    for exact in (True, False):
+        want = ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], None, 128 ** -0.5, 64, g=inp["g"],
+                                 exact_intra=exact).o
+        outs = [torch.full_like(want, 3.0) for _ in range(3)]
+        ops.chunk_gla_fwd_scatter(inp["q"], inp["k"], inp["v"], None, 128 ** -0.5, 64, outs=outs,
+                                  g=inp["g"], exact_intra=exact)
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        for o in outs:
+            assert torch.equal(o, want)
