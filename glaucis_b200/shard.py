@@ -248,6 +248,8 @@ def gla_fwd_gathered(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch
     B, T, Hr, V = v.shape
     if B * T * Hr * V > width or tuple(peers.local.shape) != (world, width):
         raise ValueError("peers must be PeerBuffers(world, width) with width >= B*T*H_r*V")
+    if width % 8:  # every block must start 16-byte aligned
+        raise ValueError("width must be a multiple of 8 elements")
     flag = torch.zeros(1, dtype=torch.int32, device=peers.local.device)
     dist.all_reduce(flag)
     outs = [p + rank * width * 2 for p in ring_order(peers.ptrs, rank)]
