@@ -178,9 +178,7 @@ enum {
   B_DRAIN = 30,
   B_GSYNC = 31,      // [2] gating quarter sums written
   B_HST = 33,        // the TMA store of the previous state tile has read shared memory
-  B_OP_FREE = 34,    // [4] scatter O: the pair's slots are free (lead warp)
-  B_OP_DONE = 38,    // [4] scatter O: both warps of the pair wrote their rows
-  NUM_BARS = 42
+  NUM_BARS = 34
 };
 static_assert(NUM_BARS * 8 <= 512, "barrier area");
 
@@ -277,10 +275,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(&bar[B_H_FULL], STATE_WARPS);
     mbar_init(&bar[B_DRAIN], 1);
     mbar_init(&bar[B_HST], 1);
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(&bar[B_OP_FREE + i], 1);
-      mbar_init(&bar[B_OP_DONE + i], 2);
-    }
     mbar_init(&bar[B_G_FULL], 1);
     mbar_init(&bar[B_G_EMPTY], GATE_WARPS);
     *abort_flag = 0;
@@ -500,32 +494,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       };
       if constexpr (CF::O_STG) {
         // this warp's 16 rows x 64 columns -> its slot (row = lane, 16-byte
-        // chunk c at c ^ (row & 7): the 128B swizzle of the map) -> TMA
-        // stores.  Plain forward: one 64 x 1 x 16 box per warp.  kScatter:
-        // the slots of quads 2j and 2j+1 (same column half) are adjacent and
-        // form one 32-row box, which the even (lead) warp stores to every
-        // output once both warps wrote, so that fewer, larger stores cross
-        // NVLink; the pair hands off through two mbarriers with bounded waits
-        // (B_OP_FREE: the lead's stores of chunk m-2 have read both slots;
-        // B_OP_DONE: both halves written).
+        // chunk c at c ^ (row & 7): the 128B swizzle of the map) -> one TMA
+        // store of a 64 x 1 x 16 box
         uint32_t ov0[32], ov1[32];
         tmem_ld32(o_lane + s * VS, ov0);
         tmem_ld32(o_lane + s * VS + 32, ov1);
         uint8_t* slot = smem + CF::OFF_OSTG + ((m & 1) * GATE_WARPS + (warp - 4)) * CF::OSTG_SLOT;
-        [[maybe_unused]] const int pair = ohalf * 2 + (oquad >> 1);
-        [[maybe_unused]] const bool lead = (oquad & 1) == 0;
-        if constexpr (kScatter) {
-          if (lead) {
-            if (lane == 0) {
-              bulk_wait_read<1>();
-              mbar_arrive(&bar[B_OP_FREE + pair]);
-            }
-          } else if (!mbar_wait(&bar[B_OP_FREE + pair], m & 1, ab)) {
-            return false;
-          }
-        } else {
-          if (lane == 0) bulk_wait_read<1>();  // the store of chunk m-2 has read this slot
-        }
+        if (lane == 0) bulk_wait_read<1>();  // the store of chunk m-2 has read this slot
         tmem_ld_wait2(ov0, ov1);
         __syncwarp();
         if (lane < 16) {
@@ -542,20 +517,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        const int32_t ox = v0 + ohalf * OC, oz = tok0 + m * C + oquad * 16;
-        if constexpr (kScatter) {
-          if (lane == 0) mbar_arrive(&bar[B_OP_DONE + pair]);
-          if (lead) {
-            if (!mbar_wait(&bar[B_OP_DONE + pair], m & 1, ab)) return false;
-            if (lane == 0) {
+        if (lane == 0) {
+          const int32_t ox = v0 + ohalf * OC, oz = tok0 + m * C + oquad * 16;
+          if constexpr (kScatter) {
 #pragma unroll
-              for (int oo = 0; oo < MAX_OUTS; ++oo)  // constant map offsets, predicated
-                if (oo < p.n_outs) tma_store_3d(&tm_o.m[oo], slot, ox, h, oz);
-              bulk_commit();
-            }
+            for (int oo = 0; oo < MAX_OUTS; ++oo)  // constant map offsets, predicated
+              if (oo < p.n_outs) tma_store_3d(&tm_o.m[oo], slot, ox, h, oz);
+          } else {
+            tma_store_3d(&tm_o.m[0], slot, ox, h, oz);
           }
-        } else if (lane == 0) {
-          tma_store_3d(&tm_o.m[0], slot, ox, h, oz);
           bulk_commit();
         }
       } else if constexpr (OC == 64) {
@@ -1130,12 +1100,10 @@ static int launch_vs(const void* q, const void* kslot, const void* vslot, const 
   gl::gla::OutMaps to;
   if (!rev && VS == 128 && p.o != nullptr) {
     // each output [B*T, H, 128] bf16, boxes of 64 columns x 1 head x 16
-    // rows (one gating warp's share of a chunk's O) or, with several
-    // outputs, 32 rows (a pair of warps' shares)
-    const uint32_t rows = p.n_outs > 1 ? 32 : 16;
+    // rows: one gating warp's share of a chunk's O
     for (int i = 0; i < p.n_outs; ++i)
       if (!gl_make_tmap_3d(&to.m[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, outs[i], 128, p.H, BT, 128,
-                           static_cast<int64_t>(p.H) * 128, 64, 1, rows, CU_TENSOR_MAP_SWIZZLE_128B,
+                           static_cast<int64_t>(p.H) * 128, 64, 1, 16, CU_TENSOR_MAP_SWIZZLE_128B,
                            why))
         return -1;
   } else if (p.n_outs > 1) {
