@@ -98,9 +98,12 @@ def test_gathered_gla_equals_one_gpu(cuda, one_rank_group, B, T, H):
         peers.close()
 
 
-def test_gla_scatter_writes_every_output(cuda):
-    # the raw op with three local outputs, both precisions
-    cfg = configs.GLAConfig("t", B=2, T=256, H=80)
+@pytest.mark.parametrize("B,T,H", [(2, 256, 80), (1, 2048, 4)])
+def test_gla_scatter_writes_every_output(cuda, B, T, H):
+    # the raw op with three local outputs (the scatter instance), both
+    # precisions; (1, 2048, 4) takes the sequence split, whose two full
+    # passes both store O
+    cfg = configs.GLAConfig("t", B=B, T=T, H=H)
     inp = configs.make_gla_inputs(cfg, device=cuda, seed=34)
     for exact in (True, False):
         want = ops.chunk_gla_fwd(inp["q"], inp["k"], inp["v"], None, 128 ** -0.5, 64, g=inp["g"],
