@@ -28,7 +28,8 @@
 //                 of the gate (per-warp prefixes exchanged through shared
 //                 memory), Qs, Kg in place, e^{G_last}; then the O epilogue
 //                 of the chunk two behind (TMEM -> bf16 -> HBM; at VS = 128
-//                 through per-warp shared-memory slots and TMA stores)
+//                 through per-warp shared-memory slots and TMA stores, to
+//                 several buffers in the kScatter instance)
 //   warps 12-15   state warpgroup: A -> tril -> bf16 P, state update
 //                 (thread = key row, VS fp32 columns in registers)
 // Buffers: one g buffer, q/k/v in a 3-stage ring (2 stages in the forward at
